@@ -1,0 +1,51 @@
+"""ZOH discretisation, restated from ``discretize_kernel.py`` (test oracle only)."""
+import torch
+
+
+def expm1_ref(x, variant="fp32"):
+    """The reference's guarded ``exp(x) - 1``.
+
+    fp32 kernel (``discretize_kernel.py:51-53``): ``exp(x)-1`` if ``|x| > 1e-5``
+    else ``x*(1 + x*0.5)``.  bf16 kernel (``:88``): the small branch is written
+    ``x + x*x*0.5``.  Both are kept because they round differently.
+    """
+    big = torch.exp(x) - 1.0
+    small = x * (1.0 + x * 0.5) if variant == "fp32" else x + x * x * 0.5
+    return torch.where(x.abs() > 1e-5, big, small)
+
+
+def zoh_discretize(A_log, B, dt, variant="fp32", out_dtype=None):
+    """``zoh_discretize_diag_kernel`` (``discretize_kernel.py:15-57``) and its
+    bf16 twin (``:60-94``).
+
+    A_log [H] holds log(-a); B [Bt,T,H]; dt [Bt,T] (one dt per (b,t), shared
+    over H).  Returns (Abar, Bbar) [Bt,T,H]:
+        a = -exp(A_log);  x = dt*a;  Abar = exp(x);
+        Bbar = expm1_ref(x) / (a + 1e-12) * B.
+    Math is fp32; outputs are cast to ``out_dtype`` (B's dtype by default).
+    """
+    out_dtype = out_dtype or B.dtype
+    a = -torch.exp(A_log.float())                      # :39-41
+    x = dt.float()[..., None] * a                      # :44,50
+    Abar = torch.exp(x)
+    Bbar = expm1_ref(x, variant) / (a + 1e-12) * B.float()   # :51-54
+    return Abar.to(out_dtype), Bbar.to(out_dtype)
+
+
+def zoh_discretize_bwd(A_log, B, dt, Abar, dAbar, dBbar):
+    """``zoh_discretize_bwd_kernel`` (``discretize_kernel.py:97-162``) without
+    its ddt store/atomic race (``:159-162``): ddt is the full sum over H.
+
+    Returns (dA_log [H], dB [Bt,T,H], ddt [Bt,T]).
+    """
+    a = -torch.exp(A_log.float())
+    neg_a = -a
+    dtv = dt.float()[..., None]
+    x = dtv * a
+    em1 = expm1_ref(x, "bf16")                         # :134 uses x + x*x*0.5
+    dex = torch.exp(x)
+    ddt = (dAbar * a * Abar).sum(-1) + (dBbar * dex * B).sum(-1)      # :130-140
+    da = dAbar * dtv * Abar + dBbar * ((dex * dtv * a - em1) / (a * a + 1e-18)) * B  # :143-148
+    dA_log = (da * (-neg_a)).reshape(-1, A_log.shape[0]).sum(0)       # :151,156
+    dB = dBbar * em1 / (a + 1e-12)                     # :154
+    return dA_log, dB, ddt
