@@ -1,0 +1,161 @@
+"""GPU parity: discretize, ssm_forward, selective_scan and the streaming steps
+against the golden fixtures and the CPU oracle on the same seeded inputs."""
+import pytest
+import torch
+
+import oracle
+from conftest import TOL_BF16, TOL_FP32, load_golden, rel_err
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def cu(t):
+    return t.to(dev)
+
+
+def test_discretize_golden(cuda_ops):
+    for name, dty, tol in (("discretize_fp32", torch.float32, 1e-5),
+                           ("discretize_bf16", torch.bfloat16, 1e-2)):
+        g = load_golden(name)
+        Ab, Bb = cuda_ops.zoh_discretize(cu(g["A_log"]), cu(g["B"].to(dty)), cu(g["dt"]))
+        assert Ab.dtype == dty
+        assert rel_err(Ab, g["Abar"]) < tol, name
+        assert rel_err(Bb, g["Bbar"]) < tol, name
+
+
+@pytest.mark.parametrize("H", [1, 37, 1024])
+@pytest.mark.parametrize("dty", [torch.float32, torch.bfloat16])
+def test_discretize_random_vs_oracle(cuda_ops, H, dty):
+    g = torch.Generator().manual_seed(H)
+    Bt, T = 3, 33
+    A_log = torch.log(torch.empty(H).uniform_(0.5, 16, generator=g))
+    B = torch.randn(Bt, T, H, generator=g).to(dty)
+    dt = torch.empty(Bt, T).exponential_(1.0, generator=g).clamp_(1e-6, 10)
+    Ab, Bb = cuda_ops.zoh_discretize(cu(A_log), cu(B), cu(dt))
+    rA, rB = oracle.zoh_discretize(A_log, B, dt, variant="fp32" if dty == torch.float32 else "bf16")
+    tol = 1e-5 if dty == torch.float32 else 1e-2
+    assert rel_err(Ab, rA) < tol and rel_err(Bb, rB) < tol
+
+
+def test_discretize_strided_and_empty(cuda_ops):
+    g = torch.Generator().manual_seed(1)
+    big = torch.randn(2, 9, 64, generator=g)
+    dtb = torch.rand(2, 9, generator=g)
+    A_log = torch.log(torch.empty(64).uniform_(0.5, 16, generator=g))
+    Ab, Bb = cuda_ops.zoh_discretize(cu(A_log), cu(big)[:, ::2, :], cu(dtb)[:, ::2])
+    rA, rB = oracle.zoh_discretize(A_log, big[:, ::2, :], dtb[:, ::2])
+    assert rel_err(Ab, rA) < 1e-5 and rel_err(Bb, rB) < 1e-5
+    e = cuda_ops.zoh_discretize(cu(A_log), torch.zeros(0, 5, 64, device=dev),
+                                torch.zeros(0, 5, device=dev))
+    assert e[0].numel() == 0
+
+
+def test_ssm_forward_golden(cuda_ops):
+    for name in ("ssm_forward_a", "ssm_forward_b"):
+        g = load_golden(name)
+        y, h = cuda_ops.ssm_forward(*(cu(g[k]) for k in ("u", "A", "B", "C", "D")))
+        assert rel_err(y, g["y"]) < TOL_FP32, name
+        assert rel_err(h, g["h"]) < TOL_FP32, name
+
+
+@pytest.mark.parametrize("shape", [(3, 1000, 70), (1, 1, 1), (2, 4097, 33), (4, 1024, 1024)])
+def test_ssm_forward_random_vs_oracle(cuda_ops, shape):
+    g = torch.Generator().manual_seed(sum(shape))
+    Bt, L, H = shape
+    u = torch.randn(Bt, L, H, generator=g)
+    A = torch.rand(Bt, L, H, generator=g) * 0.2 + 0.8
+    B = torch.randn(Bt, L, H, generator=g)
+    C = torch.randn(Bt, L, H, generator=g)
+    D = torch.randn(H, generator=g)
+    y, h = cuda_ops.ssm_forward(cu(u), cu(A), cu(B), cu(C), cu(D))
+    ry, rh = oracle.ssm_forward(u, A, B, C, D)
+    assert rel_err(y, ry) < TOL_FP32 and rel_err(h, rh) < TOL_FP32
+    y2, h2 = cuda_ops.ssm_forward(cu(u), cu(A), cu(B), cu(C), cu(D), store_h=False)
+    assert h2 is None and torch.equal(y2, y)
+
+
+def test_ssm_forward_bf16_vs_oracle(cuda_ops):
+    g = torch.Generator().manual_seed(7)
+    Bt, L, H = 2, 700, 96
+    ts = [torch.randn(Bt, L, H, generator=g) for _ in range(3)]
+    A = (torch.rand(Bt, L, H, generator=g) * 0.2 + 0.8)
+    D = torch.randn(H, generator=g)
+    u, B, C = (t.bfloat16() for t in ts)
+    A, D = A.bfloat16(), D.bfloat16()
+    y, h = cuda_ops.ssm_forward(cu(u), cu(A), cu(B), cu(C), cu(D))
+    ry, rh = oracle.ssm_forward(u, A, B, C, D)
+    assert y.dtype == torch.bfloat16
+    assert rel_err(y, ry) < TOL_BF16 and rel_err(h, rh) < TOL_BF16
+
+
+def test_selective_scan_golden(cuda_ops):
+    g = load_golden("c1_pair")
+    y, h = cuda_ops.selective_scan(*(cu(g[k]) for k in ("x", "dt", "A_log", "B", "C", "D")))
+    assert rel_err(y, g["y"]) < TOL_FP32
+    assert rel_err(h, g["h_last"]) < TOL_FP32
+
+
+@pytest.mark.parametrize("N,Dm,L", [(16, 64, 1024), (5, 7, 300), (32, 3, 513), (1, 9, 40)])
+def test_selective_scan_random_vs_oracle(cuda_ops, N, Dm, L):
+    g = torch.Generator().manual_seed(N * 100 + Dm)
+    Bt = 2
+    x = torch.randn(Bt, L, Dm, generator=g)
+    dt = torch.empty(Bt, L).exponential_(1.0, generator=g).clamp_(1e-3, 10)
+    A_log = torch.log(torch.arange(1, N + 1, dtype=torch.float32)).repeat(Dm, 1)
+    B = torch.randn(Bt, L, N, generator=g) / N ** 0.5
+    C = torch.randn(Bt, L, N, generator=g) / N ** 0.5
+    D = torch.randn(Dm, generator=g)
+    y, h = cuda_ops.selective_scan(cu(x), cu(dt), cu(A_log), cu(B), cu(C), cu(D))
+    ry, rh = oracle.selective_scan(x, dt, A_log, B, C, D)
+    assert rel_err(y, ry) < TOL_FP32 and rel_err(h, rh) < TOL_FP32
+
+
+def test_streaming_inplace_golden(cuda_ops):
+    for dtn, dty, tol in (("fp32", torch.float32, 1e-6), ("bf16", torch.bfloat16, 1e-2)):
+        g = load_golden("stream_inplace_" + dtn)
+        h = cu(g["h_in"].to(dty))
+        y = cuda_ops.streaming_ssm_inplace(cu(g["vhat"].to(dty)), h, cu(g["Abar"].to(dty)),
+                                           cu(g["Bbar"].to(dty)), cu(g["C"].to(dty)), cu(g["D"].to(dty)))
+        assert rel_err(h, g["h_out"]) < tol and rel_err(y, g["y"]) < tol
+
+
+def test_streaming_step_golden(cuda_ops):
+    g = load_golden("stream_step_composed")
+    h = cu(g["h0"]).contiguous()
+    for s in range(g["x"].shape[0]):
+        y = cuda_ops.streaming_step(cu(g["x"][s].bfloat16()), cu(g["dt"][s]), h, cu(g["A_log"]),
+                                    cu(g["B"][s].bfloat16()), cu(g["C"][s].bfloat16()), cu(g["D"]))
+        assert rel_err(y, g["y"][s]) < TOL_BF16
+    assert rel_err(h, g["h_final"]) < TOL_FP32
+
+
+@pytest.mark.parametrize("N", [3, 4, 16, 64, 128])
+@pytest.mark.parametrize("io", [torch.bfloat16, torch.float32])
+def test_streaming_step_random_vs_oracle(cuda_ops, N, io):
+    g = torch.Generator().manual_seed(N)
+    S, H, P = 37, 3, 10
+    x = torch.randn(S, H, P, generator=g).to(io)
+    dt = torch.empty(S).exponential_(1.0, generator=g)
+    dt[:3] = torch.tensor([1e-7, 2e-6, 1e-5])
+    h = torch.randn(S, H, P, N, generator=g)
+    A_log = torch.log(torch.empty(H).uniform_(0.5, 16, generator=g))
+    B = (torch.randn(S, H, N, generator=g) / N ** 0.5).to(io)
+    C = (torch.randn(S, H, N, generator=g) / N ** 0.5).to(io)
+    D = torch.randn(H, P, generator=g)
+    hd = cu(h)
+    y = cuda_ops.streaming_step(cu(x), cu(dt), hd, cu(A_log), cu(B), cu(C), cu(D))
+    rh, ry = oracle.streaming_step(x, dt, h, A_log, B, C, D)
+    ytol = TOL_FP32 if io == torch.float32 else TOL_BF16
+    assert rel_err(hd, rh) < TOL_FP32 and rel_err(y, ry) < ytol
+
+
+def test_streaming_step_rejects_bad_shapes(cuda_ops):
+    S, H, P, N = 2, 2, 2, 12
+    with pytest.raises(ValueError):
+        cuda_ops.streaming_step(torch.zeros(S, H, P + 1, device=dev, dtype=torch.bfloat16),
+                                torch.ones(S, device=dev), torch.zeros(S, H, P, N, device=dev),
+                                torch.zeros(H, device=dev),
+                                torch.zeros(S, H, N, device=dev, dtype=torch.bfloat16),
+                                torch.zeros(S, H, N, device=dev, dtype=torch.bfloat16),
+                                torch.zeros(H, P, device=dev))

@@ -1,0 +1,76 @@
+// Shared device/host helpers for the tssm_b200 kernels (sm_100a only).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "../../include/tssm.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "tssm_b200 kernels target sm_100a (B200) only"
+#endif
+
+namespace tssm {
+
+// ---------------------------------------------------------------- errors
+// Host-side status reporting: the last error message is kept per host thread.
+void set_error(const char* fmt, ...);
+int check_launch(const char* what);
+
+#define TSSM_REQUIRE(cond, ...)                 \
+  do {                                          \
+    if (!(cond)) {                              \
+      ::tssm::set_error(__VA_ARGS__);           \
+      return TSSM_ERR_INVALID;                  \
+    }                                           \
+  } while (0)
+
+// ---------------------------------------------------------------- dtypes
+template <typename T> struct io;
+template <> struct io<float> {
+  __device__ __forceinline__ static float ld(const float* p) { return *p; }
+  __device__ __forceinline__ static void st(float* p, float v) { *p = v; }
+};
+template <> struct io<__nv_bfloat16> {
+  __device__ __forceinline__ static float ld(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  __device__ __forceinline__ static void st(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+};
+template <> struct io<__half> {
+  __device__ __forceinline__ static float ld(const __half* p) { return __half2float(*p); }
+  __device__ __forceinline__ static void st(__half* p, float v) { *p = __float2half_rn(v); }
+};
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p) { return io<T>::ld(p); }
+template <typename T>
+__device__ __forceinline__ void stf(T* p, float v) { io<T>::st(p, v); }
+
+// The reference's guarded exp(x)-1 (discretize_kernel.py:51-53 and :88).
+// `e` is exp(x), already computed by the caller.
+__device__ __forceinline__ float expm1_guard_f32(float x, float e) {
+  return fabsf(x) > 1e-5f ? e - 1.0f : x * (1.0f + x * 0.5f);
+}
+__device__ __forceinline__ float expm1_guard_bf16(float x, float e) {
+  return fabsf(x) > 1e-5f ? e - 1.0f : x + x * x * 0.5f;
+}
+
+// ZOH input coefficient (exp(x)-1)/(a+1e-12) with x = dt*a (discretize_kernel.py:50-54).
+__device__ __forceinline__ float zoh_coeff(float x, float e, float a) {
+  return expm1_guard_f32(x, e) / (a + 1e-12f);
+}
+
+// Streaming (evict-first) 128-bit accesses for data touched once.
+__device__ __forceinline__ float4 ld_stream_f4(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream_f4(float4* p, float4 v) { __stcs(p, v); }
+
+__host__ __device__ constexpr inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kNumSMs = 148;
+
+}  // namespace tssm
