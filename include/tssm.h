@@ -119,6 +119,35 @@ int tssm_streaming_step(const void* x, const void* dt, void* h, const void* A_lo
                         int64_t S, int64_t Hh, int64_t P, int64_t N,
                         int io_dtype, tssm_stream_t stream);
 
+/*
+ * Multi-head chunked scan with an outer-product state h[b,h,p,n] on tcgen05
+ * tensor cores.  Replaces the multi-head chunked associative scan
+ * multihead_ssm_fwd_local_kernel / multihead_ssm_carry_scan_kernel /
+ * multihead_ssm_output_kernel (multihead_ssm_kernel.py:19-187) for the
+ * B*L*H*P*N-state workload, in one launch:
+ *   h_t = exp(dt_t*A_h) h_{t-1} + beta_t x_t (x) B_t ;  y_t[p] = sum_n C_t[n] h_t[p,n] + D[p] x_t[p]
+ *   beta_t = dt_t (bdisc 0, Euler, multihead_ssm_kernel.py:73) or
+ *            expm1*(dt_t*a)/(a+1e-12) (bdisc 1, ZOH, discretize_kernel.py:50-54), a = -exp(A_log[h]).
+ *   x [Bsz,L,H*P] bf16; dt [Bsz,L,H] f32; A_log [H] f32; B, C [Bsz,L,H,N] bf16;
+ *   Dskip [H*P] f32; y [Bsz,L,H*P] bf16; h0 [Bsz,H,P,N] f32 or NULL (zero
+ *   initial state); h_last [Bsz,H,P,N] f32 or NULL.
+ * P = 64 and N in {64, 128}; all tensors contiguous; x, B, C, y 16-byte
+ * aligned.  Device-side waits are bounded: a wait that gives up is reported
+ * by tssm_check_device_status.
+ */
+int tssm_multihead_ssd(const void* x, const void* dt, const void* A_log, const void* B,
+                       const void* C, const void* Dskip, void* y, const void* h0, void* h_last,
+                       int64_t Bsz, int64_t L, int64_t H, int64_t P, int64_t N, int bdisc,
+                       tssm_stream_t stream);
+
+/*
+ * Synchronise `stream` and report (then clear) this device's status word:
+ * TSSM_ERR_TIMEOUT if a kernel's bounded device-side wait gave up since the
+ * last check, else TSSM_OK.  No reference counterpart (the reference has no
+ * device-side waits).
+ */
+int tssm_check_device_status(tssm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -32,6 +32,8 @@ SIGNATURES = {
     "tssm_selective_scan": ([P] * 8 + [I64] * 4 + [P], I32),
     "tssm_streaming_inplace": ([P] * 7 + [I64] * 2 + [I64] * 3 + [I32, P], I32),
     "tssm_streaming_step": ([P] * 8 + [I64] * 4 + [I32, P], I32),
+    "tssm_multihead_ssd": ([P] * 9 + [I64] * 5 + [I32, P], I32),
+    "tssm_check_device_status": ([P], I32),
 }
 
 _lib = None

@@ -1,4 +1,5 @@
 // Status reporting shared by every entry point.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -25,7 +26,38 @@ int check_launch(const char* what) {
   return TSSM_OK;
 }
 
+// Device status word written by kernels whose bounded waits give up (one per
+// device: a __device__ variable lives in each device's copy of the module).
+__device__ int g_device_status;
+
+int* device_status_ptr() {
+  static std::atomic<int*> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  int* p = cache[dev].load();
+  if (!p) {
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_device_status) != cudaSuccess) return nullptr;
+    cache[dev].store(p);
+  }
+  return p;
+}
+
 }  // namespace tssm
+
+extern "C" int tssm_check_device_status(tssm_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return tssm::check_launch("check_device_status");
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tssm::g_device_status, sizeof(int)) != cudaSuccess)
+    return tssm::check_launch("check_device_status");
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(tssm::g_device_status, &zero, sizeof(int));
+    tssm::set_error("a kernel's bounded device-side wait gave up (code %d)", v);
+    return TSSM_ERR_TIMEOUT;
+  }
+  return TSSM_OK;
+}
 
 extern "C" int tssm_version(void) { return 100; }
 

@@ -20,6 +20,9 @@ namespace tssm {
 // Host-side status reporting: the last error message is kept per host thread.
 void set_error(const char* fmt, ...);
 int check_launch(const char* what);
+// Device address of this device's status word (0 = fine); kernels with bounded
+// waits store a non-zero code there when a wait gives up.
+int* device_status_ptr();
 
 #define TSSM_REQUIRE(cond, ...)                 \
   do {                                          \

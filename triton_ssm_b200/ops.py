@@ -12,7 +12,7 @@ from . import _lib
 from ._lib import call, dtype_code, ptr, stream_of
 
 __all__ = ["zoh_discretize", "ssm_forward", "selective_scan", "streaming_ssm_inplace",
-           "streaming_step"]
+           "streaming_step", "multihead_ssm", "check_device_status"]
 
 
 def _cuda(*ts):
@@ -164,3 +164,59 @@ def streaming_step(x, dt, h, A_log, B, C, D, y=None):
     call("tssm_streaming_step", ptr(x), ptr(dt), ptr(h), ptr(A_log), ptr(B), ptr(C), ptr(D), ptr(y),
          S, H, P, N, dtype_code(x), stream_of(x))
     return y
+
+
+_BDISC = {"euler": 0, "zoh": 1}
+
+
+def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h0=None,
+                  return_state=False, y=None):
+    """Multi-head chunked scan (``multihead_ssm_kernel.py:19-187``).
+
+    mode="ssd": outer-product state h[b,h,p,n] on tcgen05 tensor cores.
+      u [Bt,L,H*P] bf16; A_log [H] f32 (log(-A_h)); B, C [Bt,L,H,N] bf16;
+      dt [Bt,L,H] f32; D [H*P] f32; h0 [Bt,H,P,N] f32 or None.
+      Returns y [Bt,L,H*P] bf16, or (y, h_last [Bt,H,P,N] f32) when
+      ``return_state``.  P = 64, N in {64, 128}.
+    ``BLK_L`` is accepted for signature compatibility (the kernel's chunk is
+    64 tokens; results do not depend on it beyond rounding).
+    """
+    del BLK_L
+    if mode != "ssd":
+        raise ValueError("multihead_ssm: mode %r is not available" % (mode,))
+    if bdisc not in _BDISC:
+        raise ValueError("multihead_ssm: bdisc must be 'euler' or 'zoh'")
+    _cuda(u, A_log, B, C, dt, D, h0)
+    _need(u, (torch.bfloat16,), "u")
+    _need(B, (torch.bfloat16,), "B")
+    _need(C, (torch.bfloat16,), "C")
+    Bt, L, HP = u.shape
+    if B.dim() != 4:
+        raise ValueError("multihead_ssm: B must be [Bt,L,H,N]")
+    H, N = B.shape[2], B.shape[3]
+    if HP % H:
+        raise ValueError("multihead_ssm: u's last dim must be H*P")
+    P = HP // H
+    if tuple(B.shape) != (Bt, L, H, N) or tuple(C.shape) != (Bt, L, H, N) or \
+            tuple(dt.shape) != (Bt, L, H) or tuple(A_log.shape) != (H,) or tuple(D.shape) != (HP,):
+        raise ValueError("multihead_ssm: shape mismatch")
+    if h0 is not None and tuple(h0.shape) != (Bt, H, P, N):
+        raise ValueError("multihead_ssm: h0 must be [Bt,H,P,N]")
+    u, B, C = (t.contiguous() for t in (u, B, C))
+    dt, A_log, D = (t.float().contiguous() for t in (dt, A_log, D))
+    h0 = h0.float().contiguous() if h0 is not None else None
+    if y is None:
+        y = torch.empty_like(u)
+    hl = torch.empty(Bt, H, P, N, device=u.device, dtype=torch.float32) if return_state else None
+    call("tssm_multihead_ssd", ptr(u), ptr(dt), ptr(A_log), ptr(B), ptr(C), ptr(D), ptr(y), ptr(h0),
+         ptr(hl), Bt, L, H, P, N, _BDISC[bdisc], stream_of(u))
+    return (y, hl) if return_state else y
+
+
+def check_device_status(device=None):
+    """Synchronise the current stream and raise ``TimeoutError`` if a kernel's
+    bounded device-side wait gave up since the last check."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    s = torch.cuda.current_stream(dev)
+    import ctypes
+    call("tssm_check_device_status", ctypes.c_void_p(s.cuda_stream))
