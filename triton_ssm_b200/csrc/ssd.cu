@@ -9,18 +9,23 @@
 // One CTA walks one (b, h) stream in chunks of Q = 64 tokens; nothing is
 // written to HBM but y (and the optional final state).  Per chunk, with
 // s_i = sum_{k<=i} dt_k*A_h (inclusive, within the chunk):
-//   MMA1  G    = C B^T                         [Q x Q]  (K = N)
+//   MMA1  G    = C B^T                                   [Q x Q]  (K = N)
 //   mask  M    = G o exp(s_i - s_j) beta_j [j<=i]  -> bf16 smem
-//   MMA2  Y1   = M X                            [Q x P]  (K = Q)
-//   MMA3  Y2   = C H^T   (H = carried state, bf16) [Q x P]  (K = N)
-//   MMA4  S^T  = (diag(exp(s_last - s_j) beta_j) B)^T X   [N x P] (K = Q)
+//   MMA2  Y1   = M X                                     [Q x P]  (K = Q)
+//   MMA4  S^T  = (diag(exp(s_last - s_j) beta_j) B)^T X  [N x P]  (K = Q)
+//   MMA3  Y2   = C H^T   (H = state after the previous chunk, bf16)  (K = N)
 //   y_i = Y1_i + exp(s_i) Y2_i + D x_i ;  H <- exp(s_last) H + S   (f32 in registers)
-// Roles: warp 4 lane 0 issues TMA loads of X, B, C (128B-swizzled, one
-// STAGES-deep mbarrier ring); warps 0-3 (one warpgroup, TMEM lanes 0-127) do
-// the element-wise work, thread 0 issues the MMAs, and y leaves through a TMA
-// store.  All accumulators live in TMEM (256 columns).  Every mbarrier wait is
-// time-bounded; a wait that gives up sets the device status word and the CTA
-// exits cleanly.
+//
+// Warp roles (320 threads), with two chunks in flight:
+//   warp 8      producer: TMA loads of X, B, C (128B swizzle) into a STAGES-deep
+//               ring, plus the chunk's dt prefix sums / input coefficients;
+//   warp 9      MMA issuer (one thread): MMA1(c) runs ahead of MMA2/4/3(c-1);
+//   warps 4-7   mask group: G -> M (bf16) and B -> diag(w) B, for chunk c;
+//   warps 0-3   state/epilogue group: carried state update, y, TMA store.
+// G, Y1, Y2 and S are double-buffered in TMEM (8 x 64 = 512 columns), M and
+// the bf16 state tile in shared memory.  Only the state recurrence (64 FMAs per
+// thread per chunk) is serial.  Every mbarrier wait is time-bounded; a wait that
+// gives up sets the device status word and the CTA exits cleanly.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -33,22 +38,29 @@ using namespace sm100;
 constexpr int Q = 64;          // tokens per chunk
 constexpr int P = 64;          // head dim
 constexpr int TILE = 8192;     // bytes of a [64 x 64] bf16 tile
-constexpr int NTHREADS = 160;  // 4 consumer warps + 1 producer warp
-constexpr uint32_t COL_G = 0, COL_Y1 = 64, COL_Y2 = 128, COL_S = 192, TMEM_COLS = 256;
+constexpr int NTHREADS = 320;  // EPI 0-3, MSK 4-7, producer 8, MMA 9
+constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
+__host__ __device__ constexpr uint32_t col_g(int k) { return 0u + 64u * k; }
+__host__ __device__ constexpr uint32_t col_y1(int k) { return 128u + 64u * k; }
+__host__ __device__ constexpr uint32_t col_y2(int k) { return 256u + 64u * k; }
+__host__ __device__ constexpr uint32_t col_s(int k) { return 384u + 64u * k; }
 
 template <int NST>
 struct Layout {
-  static constexpr int NB = NST / 64;                 // 64-wide blocks along n
+  static constexpr int NB = NST / 64;                  // 64-wide blocks of B and C along n
   static constexpr int STAGE_BYTES = TILE * (1 + 2 * NB);
   static constexpr int STAGES = NST == 64 ? 4 : 3;
-  static constexpr int OFF_MT = STAGES * STAGE_BYTES;
-  static constexpr int OFF_HS = OFF_MT + TILE;
-  static constexpr int OFF_YS = OFF_HS + NB * TILE;   // two staging tiles
-  static constexpr int OFF_SMALL = OFF_YS + 2 * TILE; // s2, beta, wdec, dsk: 4 x 64 f32
-  static constexpr int OFF_BAR = OFF_SMALL + 4 * 64 * 4;
-  static constexpr int NBAR = 2 * STAGES + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem slot, abort flag, counters
+  static constexpr int HS_BYTES = NST * 128;           // state tile: NST rows (n) x 64 p, MN-major
+  static constexpr int OFF_MT = STAGES * STAGE_BYTES;  // 2 mask tiles
+  static constexpr int OFF_HS = OFF_MT + 2 * TILE;     // 2 state tiles
+  static constexpr int OFF_YS = OFF_HS + 2 * HS_BYTES; // 2 output staging tiles
+  static constexpr int OFF_SMALL = OFF_YS + 2 * TILE;  // per stage: s2, beta, wdec [64] + elast
+  static constexpr int SMALL_STRIDE = 4 * 64 * 4;
+  static constexpr int OFF_DSK = OFF_SMALL + STAGES * SMALL_STRIDE;
+  static constexpr int OFF_BAR = OFF_DSK + 64 * 4;
+  static constexpr int NBAR = 2 * STAGES + 14;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem slot, abort flag, issued, consumed
   static constexpr int BYTES = OFF_MISC + 32 + 1024;   // + slack to align the base to 1024
 };
 
@@ -74,33 +86,41 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const float* __restrict__ h0, float* __restrict__ h_last, int* __restrict__ status, int L, int H) {
   using LY = Layout<NST>;
   constexpr int NB = LY::NB;
-  constexpr int STAGES = LY::STAGES;
+  constexpr int ST = LY::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, b = blockIdx.y;
   const int nchunks = (L + Q - 1) / Q;
-  float* s2 = reinterpret_cast<float*>(smem + LY::OFF_SMALL);
-  float* beta = s2 + 64;
-  float* wdec = beta + 64;
-  float* dsk = wdec + 64;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
-  uint64_t* empty = full + STAGES;
-  uint64_t* mmab = empty + STAGES;
+  float* dsk = reinterpret_cast<float*>(smem + LY::OFF_DSK);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
+  uint64_t* full = bars;              // [ST]  TMA bytes + dt data
+  uint64_t* empty = bars + ST;        // [ST]  stage released by the epilogue group
+  uint64_t* gfull = bars + 2 * ST;    // [2]   MMA1 done
+  uint64_t* gfree = gfull + 2;        // [2]   G read by the mask group
+  uint64_t* mready = gfull + 4;       // [2]   M and diag(w) B written
+  uint64_t* yfull = gfull + 6;        // [2]   MMA2 + MMA4 done
+  uint64_t* hready = gfull + 8;       // [2]   bf16 state tile for the next MMA3 written
+  uint64_t* y2full = gfull + 10;      // [2]   MMA3 done
+  uint64_t* tfree = gfull + 12;       // [2]   Y1, Y2, S read by the epilogue group
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_MISC + 4);
   int* issued = reinterpret_cast<int*>(smem + LY::OFF_MISC + 8);
   int* consumed = reinterpret_cast<int*>(smem + LY::OFF_MISC + 12);
-  uint8_t* Mt = smem + LY::OFF_MT;
-  uint8_t* Hs = smem + LY::OFF_HS;
+
+  auto stage_ptr = [&](int s) { return smem + s * LY::STAGE_BYTES; };
+  auto small_ptr = [&](int s) { return reinterpret_cast<float*>(smem + LY::OFF_SMALL + s * LY::SMALL_STRIDE); };
+  auto mt_ptr = [&](int k) { return smem + LY::OFF_MT + k * TILE; };
+  auto hs_ptr = [&](int k) { return smem + LY::OFF_HS + k * LY::HS_BYTES; };
+  auto ys_ptr = [&](int k) { return smem + LY::OFF_YS + k * TILE; };
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&full[s], 2);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(mmab, 1);
+    for (int k = 0; k < 14; ++k) mbar_init(&gfull[k], 1);
     *abort_flag = 0;
     *issued = 0;
     *consumed = 0;
@@ -122,21 +142,35 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     atomicExch(status, code);
   };
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
+  if (warp == 8) {
+    // ================================================================ producer
+    const float* dtp = dt + (int64_t)b * L * H + h;
+    float dn0 = 0.f, dn1 = 0.f;
+    auto load_dt = [&](int c) {
+      const int t = c * Q + 2 * lane;
+      dn0 = t < L ? __ldg(dtp + (int64_t)t * H) : 0.f;
+      dn1 = t + 1 < L ? __ldg(dtp + (int64_t)(t + 1) * H) : 0.f;
+    };
     if (lane == 0) {
       prefetch_tmap(&tm_x);
       prefetch_tmap(&tm_b);
       prefetch_tmap(&tm_c);
-      int c = 0;
-      for (; c < nchunks; ++c) {
-        const int s = c % STAGES, k = c / STAGES;
-        if (c >= STAGES && !mbar_wait(&empty[s], (k - 1) & 1, abort_flag)) {
+    }
+    load_dt(0);
+    int c = 0;
+    for (; c < nchunks; ++c) {
+      const int s = c % ST, k = c / ST;
+      int bad = 0;   // decided by lane 0, broadcast so the warp stays converged
+      if (lane == 0) {
+        if (c >= ST && !mbar_wait(&empty[s], (k - 1) & 1, abort_flag)) {
           if (!*abort_flag) fail(1001);
-          break;
+          bad = 1;
         }
-        if (*abort_flag) break;
-        uint8_t* st = smem + s * LY::STAGE_BYTES;
+        bad |= *abort_flag;
+      }
+      if (__shfl_sync(0xffffffffu, bad, 0)) break;
+      uint8_t* st = stage_ptr(s);
+      if (lane == 0) {
         mbar_arrive_expect_tx(&full[s], LY::STAGE_BYTES);
         tma_load_3d(st, &tm_x, h * P, c * Q, b, &full[s]);
 #pragma unroll
@@ -145,231 +179,271 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
           tma_load_3d(st + TILE * (1 + NB + nb), &tm_c, h * NST + nb * 64, c * Q, b, &full[s]);
         }
       }
-      *issued = c;
+      // decay prefix sums (log2 domain) and input coefficients of chunk c
+      const float d0 = dn0, d1 = dn1;
+      if (c + 1 < nchunks) load_dt(c + 1);
+      const float l0 = d0 * a2, l1 = d1 * a2;
+      const float pair = l0 + l1;
+      float incl = pair;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+      }
+      const float s0 = incl - pair + l0, s1 = incl;
+      const float slast = __shfl_sync(0xffffffffu, incl, 31);
+      float b0, b1;
+      if (ZOH) {
+        const float x0 = d0 * a, x1 = d1 * a;
+        b0 = zoh_coeff(x0, expf(x0), a);
+        b1 = zoh_coeff(x1, expf(x1), a);
+      } else {
+        b0 = d0;
+        b1 = d1;
+      }
+      float* sm = small_ptr(s);
+      sm[2 * lane] = s0;
+      sm[2 * lane + 1] = s1;
+      sm[64 + 2 * lane] = b0;
+      sm[64 + 2 * lane + 1] = b1;
+      sm[128 + 2 * lane] = exp2f(slast - s0) * b0;
+      sm[128 + 2 * lane + 1] = exp2f(slast - s1) * b1;
+      if (lane == 0) sm[192] = exp2f(slast);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
     }
-  } else {
-    // ------------------------------------------------------------ consumers
-    const bool rowthr = lane < 16;             // owns row (warp*16+lane) of an M=64 accumulator
-    const int row = warp * 16 + lane;
-    const bool owner = NST == 128 ? true : rowthr;
-    const int n_own = NST == 128 ? tid : row;  // state column owned by this thread
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    float hreg[P];
+    if (lane == 0) *issued = c;
+  } else if (warp == 9) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_KK = make_idesc_bf16(64, 64, false, false);
+      constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
+      constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
+      for (int c = 0; c <= nchunks; ++c) {
+        if (c < nchunks) {
+          const int s = c % ST, kb = c & 1;
+          if (!mbar_wait(&full[s], (c / ST) & 1, abort_flag)) { if (!*abort_flag) fail(1002); break; }
+          if (c >= 2 && !mbar_wait(&gfree[kb], ((c - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1003); break; }
+          tc_fence_after();
+          const uint32_t X = smem_u32(stage_ptr(s));
+          const uint32_t Bt = X + TILE, Ct = X + TILE * (1 + NB);
 #pragma unroll
-    for (int p = 0; p < P; ++p) hreg[p] = 0.f;
-    if (owner && h0) {
-      const float* src = h0 + (((int64_t)b * H + h) * P) * NST + n_own;
-#pragma unroll
-      for (int p = 0; p < P; ++p) hreg[p] = src[(int64_t)p * NST];
-    }
-    if (owner) {
-#pragma unroll
-      for (int p = 0; p < P; ++p)
-        *reinterpret_cast<__nv_bfloat16*>(Hs + (n_own >> 6) * TILE + sw128_off(p, n_own & 63)) =
-            __float2bfloat16_rn(hreg[p]);
-    }
-    fence_proxy_async_smem();
-    named_bar_sync(1, 128);
-
-    const float* dtp = dt + (int64_t)b * L * H + h;
-    float dn0 = 0.f, dn1 = 0.f;
-    auto load_dt = [&](int c) {
-      const int t = c * Q + 2 * lane;
-      dn0 = t < L ? __ldg(dtp + (int64_t)t * H) : 0.f;
-      dn1 = t + 1 < L ? __ldg(dtp + (int64_t)(t + 1) * H) : 0.f;
-    };
-    if (warp == 0) load_dt(0);
-    constexpr uint32_t ID_KK = make_idesc_bf16(64, 64, false, false);
-    constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
-    constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
-    uint32_t mma_cnt = 0;
-    int c = 0;
-    for (; c < nchunks; ++c) {
-      const int s = c % STAGES, k = c / STAGES;
-      uint8_t* X = smem + s * LY::STAGE_BYTES;
-      uint8_t* Bt = X + TILE;
-      uint8_t* Ct = X + TILE * (1 + NB);
-
-      // (1) decay prefix sums and input coefficients of this chunk (warp 0)
-      if (warp == 0) {
-        const float d0 = dn0, d1 = dn1;
-        if (c + 1 < nchunks) load_dt(c + 1);
-        const float l0 = d0 * a2, l1 = d1 * a2;
-        const float pair = l0 + l1;
-        float incl = pair;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float v = __shfl_up_sync(0xffffffffu, incl, off);
-          if (lane >= off) incl += v;
+          for (int kk = 0; kk < NST / 16; ++kk) {
+            const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
+            umma_bf16(tmem + col_g(kb), make_desc_sw128(Ct + koff, 16), make_desc_sw128(Bt + koff, 16), ID_KK,
+                      kk > 0);
+          }
+          umma_commit(&gfull[kb]);
         }
-        s2[2 * lane] = incl - pair + l0;
-        s2[2 * lane + 1] = incl;
-        if (ZOH) {
-          const float x0 = d0 * a, x1 = d1 * a;
-          beta[2 * lane] = zoh_coeff(x0, expf(x0), a);
-          beta[2 * lane + 1] = zoh_coeff(x1, expf(x1), a);
-        } else {
-          beta[2 * lane] = d0;
-          beta[2 * lane + 1] = d1;
+        if (c >= 1) {
+          const int k = c - 1, s = k % ST, kb = k & 1;
+          if (!mbar_wait(&mready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1004); break; }
+          if (k >= 2 && !mbar_wait(&tfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1005); break; }
+          tc_fence_after();
+          const uint32_t X = smem_u32(stage_ptr(s));
+          const uint32_t Bt = X + TILE, Ct = X + TILE * (1 + NB);
+          const uint32_t Mt = smem_u32(mt_ptr(kb));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + col_y1(kb), make_desc_sw128(Mt + kk * 32, 16), make_desc_sw128(X + kk * 2048, TILE),
+                      ID_KM, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + col_s(kb), make_desc_sw128(Bt + kk * 2048, TILE), make_desc_sw128(X + kk * 2048, TILE),
+                      ID_MM, kk > 0);
+          umma_commit(&yfull[kb]);
+          if (!mbar_wait(&hready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1006); break; }
+          tc_fence_after();
+          const uint32_t Hs = smem_u32(hs_ptr(kb));
+#pragma unroll
+          for (int kk = 0; kk < NST / 16; ++kk) {
+            const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
+            umma_bf16(tmem + col_y2(kb), make_desc_sw128(Ct + koff, 16), make_desc_sw128(Hs + kk * 2048, TILE),
+                      ID_KM, kk > 0);
+          }
+          umma_commit(&y2full[kb]);
         }
       }
-      // (2) wait for this chunk's tiles (tid 0 decides; everyone then observes the phase)
+    }
+  } else if (warp >= 4) {
+    // ================================================================ mask group
+    const int t = tid - 128;
+    const int w = warp - 4;
+    const int row = w * 16 + (lane & 15);   // token i of the M=64 accumulator rows held by this thread
+    const int half = lane >> 4;             // which 32 columns
+    const uint32_t lane_base = (uint32_t)(w * 32) << 16;
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c % ST, kb = c & 1;
       bool bad = false;
-      if (tid == 0) {
-        bad = !mbar_wait(&full[s], k & 1, abort_flag) || *abort_flag;
-        if (bad) fail(1002);
+      if (t == 0) {
+        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag) ||
+              (c >= 2 && !mbar_wait(&yfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
+        if (bad && !*abort_flag) fail(1007);
       }
-      if (named_bar_or(1, 128, bad)) break;
-      mbar_wait(&full[s], k & 1);
-
-      // (3) MMA1: G = C B^T
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < NST / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
-          umma_bf16(tmem + COL_G, make_desc_sw128(smem_u32(Ct) + koff, 16),
-                    make_desc_sw128(smem_u32(Bt) + koff, 16), ID_KK, kk > 0);
-        }
-        umma_commit(mmab);
-      }
-      if (tid < 64) wdec[tid] = exp2f(s2[63] - s2[tid]) * beta[tid];
-      const float e_last = exp2f(s2[63]);
-      if (tid == 0) {
-        bad = !mbar_wait(mmab, mma_cnt & 1, abort_flag);
-        if (bad) fail(1003);
-      }
-      if (named_bar_or(1, 128, bad)) break;
-      mbar_wait(mmab, mma_cnt & 1);
-      ++mma_cnt;
+      if (named_bar_or(2, 128, bad)) break;
+      mbar_wait(&full[s], (c / ST) & 1);
+      mbar_wait(&gfull[kb], (c >> 1) & 1);
       tc_fence_after();
-
-      // (4a) B_hat = diag(wdec) B, in place (B is no longer read by MMA1)
+      const float* sm = small_ptr(s);
+      uint8_t* X = stage_ptr(s);
+      uint8_t* Bt = X + TILE;
+      // M row `row`, columns [32*half, 32*half+32)
+      float g[32];
+      tmem_ld16x2_32(tmem + lane_base + col_g(kb), g);
+      tmem_wait_ld();
+      {
+        const float si = sm[row];
+        uint8_t* Mt = mt_ptr(kb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int jj = q * 8 + 2 * e;
+            const int j0 = half * 32 + jj;
+            const float m0 = j0 <= row ? g[jj] * exp2f(si - sm[j0]) * sm[64 + j0] : 0.f;
+            const float m1 = j0 + 1 <= row ? g[jj + 1] * exp2f(si - sm[j0 + 1]) * sm[64 + j0 + 1] : 0.f;
+            w4[e] = pack_bf16x2(m0, m1);
+          }
+          *reinterpret_cast<uint4*>(Mt + sw128_chunk(row, half * 4 + q)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+      // B <- diag(w) B in place (MMA1 of this chunk is complete)
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
-          const int idx = tid + it * 128;            // 16-byte chunk index; row = idx / 8
+          const int idx = t + it * 128;            // 16-byte chunk; row j = idx / 8
           uint4* pch = reinterpret_cast<uint4*>(Bt + nb * TILE + idx * 16);
           float f[8];
           unpack_bf16x8(*pch, f);
-          const float w = wdec[idx >> 3];
+          const float wj = sm[128 + (idx >> 3)];
           uint4 o;
-          o.x = pack_bf16x2(f[0] * w, f[1] * w);
-          o.y = pack_bf16x2(f[2] * w, f[3] * w);
-          o.z = pack_bf16x2(f[4] * w, f[5] * w);
-          o.w = pack_bf16x2(f[6] * w, f[7] * w);
+          o.x = pack_bf16x2(f[0] * wj, f[1] * wj);
+          o.y = pack_bf16x2(f[2] * wj, f[3] * wj);
+          o.z = pack_bf16x2(f[4] * wj, f[5] * wj);
+          o.w = pack_bf16x2(f[6] * wj, f[7] * wj);
           *pch = o;
         }
       }
-      // (4b) masked decay matrix M (row i = token) from G
-      {
-        const float si = s2[rowthr ? row : 0];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float g[32];
-          tmem_ld32(tmem + lane_base + COL_G + half * 32, g);
-          tmem_wait_ld();
-          if (rowthr) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t w4[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j0 = half * 32 + q * 8 + 2 * e;
-                const float m0 = j0 <= row ? g[q * 8 + 2 * e] * exp2f(si - s2[j0]) * beta[j0] : 0.f;
-                const float m1 = j0 + 1 <= row ? g[q * 8 + 2 * e + 1] * exp2f(si - s2[j0 + 1]) * beta[j0 + 1] : 0.f;
-                w4[e] = pack_bf16x2(m0, m1);
-              }
-              *reinterpret_cast<uint4*>(Mt + sw128_chunk(row, half * 4 + q)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            }
-          }
-        }
-      }
       fence_proxy_async_smem();
       tc_fence_before();
-      named_bar_sync(1, 128);
-
-      // (5) MMA2 (Y1 = M X), MMA3 (Y2 = C H^T), MMA4 (S^T = B_hat^T X)
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + COL_Y1, make_desc_sw128(smem_u32(Mt) + kk * 32, 16),
-                    make_desc_sw128(smem_u32(X) + kk * 2048, TILE), ID_KM, kk > 0);
-#pragma unroll
-        for (int kk = 0; kk < NST / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
-          umma_bf16(tmem + COL_Y2, make_desc_sw128(smem_u32(Ct) + koff, 16),
-                    make_desc_sw128(smem_u32(Hs) + koff, 16), ID_KK, kk > 0);
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem + COL_S, make_desc_sw128(smem_u32(Bt) + kk * 2048, TILE),
-                    make_desc_sw128(smem_u32(X) + kk * 2048, TILE), ID_MM, kk > 0);
-        umma_commit(mmab);
+      named_bar_sync(2, 128);
+      if (t == 0) {
+        mbar_arrive(&gfree[kb]);
+        mbar_arrive(&mready[kb]);
       }
+    }
+  } else {
+    // ================================================================ state / epilogue group
+    const int w = warp;
+    const int half = lane >> 4;
+    const int row = w * 16 + (lane & 15);   // token row of Y1/Y2 (M=64 layout)
+    const uint32_t lane_base = (uint32_t)(w * 32) << 16;
+    // State ownership: NST=64 -> S^T row n = row, p in [32*half, +32);  NST=128 -> n = tid, all p.
+    constexpr int HP = NST == 64 ? 32 : 64;
+    const int n_own = NST == 64 ? row : tid;
+    const int p0 = NST == 64 ? 32 * half : 0;
+    float hreg[HP];
+#pragma unroll
+    for (int j = 0; j < HP; ++j) hreg[j] = 0.f;
+    if (h0) {
+      const float* src = h0 + (((int64_t)b * H + h) * P) * NST + n_own;
+#pragma unroll
+      for (int j = 0; j < HP; ++j) hreg[j] = src[(int64_t)(p0 + j) * NST];
+    }
+    // bf16 state tile for MMA3: row n, 64 p contiguous (MN-major B operand), 128B swizzle.
+    auto write_hs = [&](uint8_t* Hs) {
+#pragma unroll
+      for (int q = 0; q < HP / 8; ++q) {
+        uint4 o;
+        o.x = pack_bf16x2(hreg[8 * q + 0], hreg[8 * q + 1]);
+        o.y = pack_bf16x2(hreg[8 * q + 2], hreg[8 * q + 3]);
+        o.z = pack_bf16x2(hreg[8 * q + 4], hreg[8 * q + 5]);
+        o.w = pack_bf16x2(hreg[8 * q + 6], hreg[8 * q + 7]);
+        *reinterpret_cast<uint4*>(Hs + sw128_chunk(n_own, p0 / 8 + q)) = o;
+      }
+    };
+    write_hs(hs_ptr(0));
+    fence_proxy_async_smem();
+    named_bar_sync(1, 128);
+    if (tid == 0) mbar_arrive(&hready[0]);
+    int c = 0;
+    for (; c < nchunks; ++c) {
+      const int s = c % ST, kb = c & 1;
+      bool bad = false;
       if (tid == 0) {
-        bad = !mbar_wait(mmab, mma_cnt & 1, abort_flag);
-        if (bad) fail(1004);
+        bad = !mbar_wait(&yfull[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
+        if (bad && !*abort_flag) fail(1008);
       }
       if (named_bar_or(1, 128, bad)) break;
-      mbar_wait(mmab, mma_cnt & 1);
-      ++mma_cnt;
+      mbar_wait(&full[s], (c / ST) & 1);
+      mbar_wait(&yfull[kb], (c >> 1) & 1);
       tc_fence_after();
-
-      // (6) epilogue: y rows -> staging tile (same swizzled layout as X) -> TMA store
-      uint8_t* Ys = smem + LY::OFF_YS + (c & 1) * TILE;
-      {
-        const float ei = exp2f(s2[rowthr ? row : 0]);
+      const float* sm = small_ptr(s);
+      const float e_last = sm[192];
+      // ---- carried state: H <- exp(s_last) H + S ; bf16 copy for MMA3 of chunk c+1
+      if (NST == 64) {
+        float sv[32];
+        tmem_ld16x2_32(tmem + lane_base + col_s(kb), sv);
+        tmem_wait_ld();
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float y1[32], y2[32];
-          tmem_ld32(tmem + lane_base + COL_Y1 + half * 32, y1);
-          tmem_ld32(tmem + lane_base + COL_Y2 + half * 32, y2);
+        for (int j = 0; j < 32; ++j) hreg[j] = e_last * hreg[j] + sv[j];
+      } else {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float sv[32];
+          tmem_ld32(tmem + lane_base + col_s(kb) + hh * 32, sv);
           tmem_wait_ld();
-          if (rowthr) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int cc = half * 4 + q;
-              float xf[8];
-              unpack_bf16x8(*reinterpret_cast<const uint4*>(X + sw128_chunk(row, cc)), xf);
-              uint32_t w4[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int p0 = cc * 8 + 2 * e;
-                const float o0 = y1[q * 8 + 2 * e] + ei * y2[q * 8 + 2 * e] + dsk[p0] * xf[2 * e];
-                const float o1 = y1[q * 8 + 2 * e + 1] + ei * y2[q * 8 + 2 * e + 1] + dsk[p0 + 1] * xf[2 * e + 1];
-                w4[e] = pack_bf16x2(o0, o1);
-              }
-              *reinterpret_cast<uint4*>(Ys + sw128_chunk(row, cc)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            }
-          }
+          for (int j = 0; j < 32; ++j) hreg[hh * 32 + j] = e_last * hreg[hh * 32 + j] + sv[j];
         }
       }
-      // (7) state: H <- exp(s_last) H + S ; bf16 copy for the next chunk's MMA3
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float sv[32];
-        tmem_ld32(tmem + lane_base + COL_S + half * 32, sv);
+      write_hs(hs_ptr((c + 1) & 1));
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
+      if (tid == 0) mbar_arrive(&hready[(c + 1) & 1]);
+      // ---- output rows
+      if (tid == 0) {
+        bad = !mbar_wait(&y2full[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
+        if (bad && !*abort_flag) fail(1009);
+      }
+      if (named_bar_or(1, 128, bad)) break;
+      mbar_wait(&y2full[kb], (c >> 1) & 1);
+      tc_fence_after();
+      {
+        float y1[32], y2[32];
+        tmem_ld16x2_32(tmem + lane_base + col_y1(kb), y1);
+        tmem_ld16x2_32(tmem + lane_base + col_y2(kb), y2);
         tmem_wait_ld();
-        if (owner) {
+        const float ei = exp2f(sm[row]);
+        const uint8_t* X = stage_ptr(s);
+        uint8_t* Ys = ys_ptr(kb);
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int p = half * 32 + jj;
-            hreg[p] = e_last * hreg[p] + sv[jj];
-            *reinterpret_cast<__nv_bfloat16*>(Hs + (n_own >> 6) * TILE + sw128_off(p, n_own & 63)) =
-                __float2bfloat16_rn(hreg[p]);
+        for (int q = 0; q < 4; ++q) {
+          const int cc = half * 4 + q;
+          float xf[8];
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(X + sw128_chunk(row, cc)), xf);
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int jj = q * 8 + 2 * e;
+            const int pp = cc * 8 + 2 * e;
+            const float o0 = y1[jj] + ei * y2[jj] + dsk[pp] * xf[2 * e];
+            const float o1 = y1[jj + 1] + ei * y2[jj + 1] + dsk[pp + 1] * xf[2 * e + 1];
+            w4[e] = pack_bf16x2(o0, o1);
           }
+          *reinterpret_cast<uint4*>(Ys + sw128_chunk(row, cc)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       named_bar_sync(1, 128);
       if (tid == 0) {
-        tma_store_3d(&tm_y, Ys, h * P, c * Q, b);
+        tma_store_3d(&tm_y, ys_ptr(kb), h * P, c * Q, b);
         bulk_commit();
         bulk_wait_read<1>();
+        mbar_arrive(&tfree[kb]);
         mbar_arrive(&empty[s]);
       }
     }
@@ -377,18 +451,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       *consumed = c;
       bulk_wait<0>();
     }
-    if (h_last && owner && !*abort_flag) {
+    if (h_last && !*abort_flag) {
       float* dst = h_last + (((int64_t)b * H + h) * P) * NST + n_own;
 #pragma unroll
-      for (int p = 0; p < P; ++p) dst[(int64_t)p * NST] = hreg[p];
+      for (int j = 0; j < HP; ++j) dst[(int64_t)(p0 + j) * NST] = hreg[j];
     }
   }
-  // ------------------------------------------------------------ teardown
+  // ================================================================ teardown
   tc_fence_before();
   __syncthreads();
   if (tid == 0 && *abort_flag) {
     // Drain loads that were issued but never consumed before the CTA exits.
-    for (int c = *consumed; c < *issued; ++c) mbar_wait(&full[c % STAGES], (c / STAGES) & 1, nullptr, 100000000ull);
+    for (int c = *consumed; c < *issued; ++c) mbar_wait(&full[c % ST], (c / ST) & 1, nullptr, 100000000ull);
   }
   __syncthreads();
   if (warp == 0) {
