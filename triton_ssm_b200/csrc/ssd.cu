@@ -16,12 +16,17 @@
 //   MMA3  Y2   = C H^T   (H = state after the previous chunk, bf16)  (K = N)
 //   y_i = Y1_i + exp(s_i) Y2_i + D x_i ;  H <- exp(s_last) H + S   (f32 in registers)
 //
-// Warp roles (320 threads), with two chunks in flight:
-//   warp 8      producer: TMA loads of X, B, C (128B swizzle) into a STAGES-deep
-//               ring, plus the chunk's dt prefix sums / input coefficients;
-//   warp 9      MMA issuer (one thread): MMA1(c) runs ahead of MMA2/4/3(c-1);
+// Warp roles (384 threads), with two chunks in flight:
+//   warp 8      producer: TMA loads of X, B, C (128B swizzle) into a STAGES-deep ring,
+//               and, in the same non-blocking event loop, the MMA1 issue;
+//   warp 11     decay: streams dt (cp.async, STAGES-1 chunks ahead) and writes the
+//               chunk's decay prefix sums and input coefficients next to the stage;
+//   warps 9,10  MMA issuers (one thread each: MMA2+MMA4 | MMA3); issuing a
+//               tcgen05.mma costs the issuing thread tens of cycles, so the issue
+//               work is spread over three threads and each MMA goes out as soon as
+//               its own inputs are ready;
 //   warps 4-7   mask group: G -> M (bf16) and B -> diag(w) B, for chunk c;
-//   warps 0-3   state/epilogue group: carried state update, y, TMA store.
+//   warps 0-3   state/epilogue group: carried state update, y (16-byte global stores).
 // G, Y1, Y2 and S are double-buffered in TMEM (8 x 64 = 512 columns), M and
 // the bf16 state tile in shared memory.  Only the state recurrence (64 FMAs per
 // thread per chunk) is serial.  Every mbarrier wait is time-bounded; a wait that
@@ -32,13 +37,25 @@
 #include "tcgen05.cuh"
 
 namespace tssm {
+#ifdef TSSM_SSD_TRACE
+// Debug-only phase timestamps (clock64) of CTA (0,0): [chunk][event].
+__device__ unsigned long long g_ssd_trace[64 * 24];
+#define SSD_TRACE(chunk, ev)                                                         \
+  do {                                                                               \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (chunk) < 64) g_ssd_trace[(chunk) * 24 + (ev)] = clock64(); \
+  } while (0)
+#else
+#define SSD_TRACE(chunk, ev) \
+  do {                       \
+  } while (0)
+#endif
 namespace {
 using namespace sm100;
 
 constexpr int Q = 64;          // tokens per chunk
 constexpr int P = 64;          // head dim
 constexpr int TILE = 8192;     // bytes of a [64 x 64] bf16 tile
-constexpr int NTHREADS = 320;  // EPI 0-3, MSK 4-7, producer 8, MMA 9
+constexpr int NTHREADS = 384;  // EPI 0-3, MSK 4-7, TMA+MMA1 8, MMA2+4 9, MMA3 10, decay 11
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
 __host__ __device__ constexpr uint32_t col_g(int k) { return 0u + 64u * k; }
@@ -54,9 +71,8 @@ struct Layout {
   static constexpr int HS_BYTES = NST * 128;           // state tile: NST rows (n) x 64 p, MN-major
   static constexpr int OFF_MT = STAGES * STAGE_BYTES;  // 2 mask tiles
   static constexpr int OFF_HS = OFF_MT + 2 * TILE;     // 2 state tiles
-  static constexpr int OFF_YS = OFF_HS + 2 * HS_BYTES; // 2 output staging tiles
-  static constexpr int OFF_SMALL = OFF_YS + 2 * TILE;  // per stage: s2, beta, wdec [64] + elast
-  static constexpr int SMALL_STRIDE = 4 * 64 * 4;
+  static constexpr int OFF_SMALL = OFF_HS + 2 * HS_BYTES;  // per stage: s, s', w [64] + exp(s_last)
+  static constexpr int SMALL_STRIDE = 5 * 64 * 4;     // s, s', w, [e_last], raw dt
   static constexpr int OFF_DSK = OFF_SMALL + STAGES * SMALL_STRIDE;
   static constexpr int OFF_BAR = OFF_DSK + 64 * 4;
   static constexpr int NBAR = 2 * STAGES + 14;
@@ -81,7 +97,7 @@ __device__ __forceinline__ void unpack_bf16x8(uint4 v, float (&f)[8]) {
 template <int NST, bool ZOH>
 __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
-    const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_y,
+    const __grid_constant__ CUtensorMap tm_c, __nv_bfloat16* __restrict__ y,
     const float* __restrict__ dt, const float* __restrict__ A_log, const float* __restrict__ Dskip,
     const float* __restrict__ h0, float* __restrict__ h_last, int* __restrict__ status, int L, int H) {
   using LY = Layout<NST>;
@@ -93,6 +109,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, b = blockIdx.y;
   const int nchunks = (L + Q - 1) / Q;
+  const int64_t HPtot = (int64_t)H * P;
   float* dsk = reinterpret_cast<float*>(smem + LY::OFF_DSK);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
   uint64_t* full = bars;              // [ST]  TMA bytes + dt data
@@ -113,7 +130,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   auto small_ptr = [&](int s) { return reinterpret_cast<float*>(smem + LY::OFF_SMALL + s * LY::SMALL_STRIDE); };
   auto mt_ptr = [&](int k) { return smem + LY::OFF_MT + k * TILE; };
   auto hs_ptr = [&](int k) { return smem + LY::OFF_HS + k * LY::HS_BYTES; };
-  auto ys_ptr = [&](int k) { return smem + LY::OFF_YS + k * TILE; };
 
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -144,44 +160,97 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
 
   if (warp == 8) {
     // ================================================================ producer
-    const float* dtp = dt + (int64_t)b * L * H + h;
-    float dn0 = 0.f, dn1 = 0.f;
-    auto load_dt = [&](int c) {
-      const int t = c * Q + 2 * lane;
-      dn0 = t < L ? __ldg(dtp + (int64_t)t * H) : 0.f;
-      dn1 = t + 1 < L ? __ldg(dtp + (int64_t)(t + 1) * H) : 0.f;
-    };
     if (lane == 0) {
       prefetch_tmap(&tm_x);
       prefetch_tmap(&tm_b);
       prefetch_tmap(&tm_c);
+      constexpr uint32_t ID_KK = make_idesc_bf16(64, 64, false, false);
+      int pc = 0;   // next chunk to load
+      int mc = 0;   // next chunk whose MMA1 (G = C B^T) is issued
+      uint64_t t_prog = globaltimer_ns();
+      while (mc < nchunks) {
+        bool prog = false;
+        if (pc < nchunks && (pc < ST || mbar_test(&empty[pc % ST], ((pc / ST) - 1) & 1))) {
+          const int s = pc % ST;
+          SSD_TRACE(pc, 0);
+          uint8_t* st = stage_ptr(s);
+          mbar_arrive_expect_tx(&full[s], LY::STAGE_BYTES);
+          tma_load_3d(st, &tm_x, h * P, pc * Q, b, &full[s]);
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) {
+            tma_load_3d(st + TILE * (1 + nb), &tm_b, h * NST + nb * 64, pc * Q, b, &full[s]);
+            tma_load_3d(st + TILE * (1 + NB + nb), &tm_c, h * NST + nb * 64, pc * Q, b, &full[s]);
+          }
+          ++pc;
+          prog = true;
+        }
+        if (mc < pc && mbar_test(&full[mc % ST], (mc / ST) & 1) &&
+            (mc < 2 || mbar_test(&gfree[mc & 1], ((mc - 2) >> 1) & 1))) {
+          const int s = mc % ST, kb = mc & 1;
+          tc_fence_after();
+          SSD_TRACE(mc, 2);
+          const uint32_t X = smem_u32(stage_ptr(s));
+          const uint64_t dB = make_desc_sw128(X + TILE, 16), dC = make_desc_sw128(X + TILE * (1 + NB), 16);
+#pragma unroll
+          for (int kk = 0; kk < NST / 16; ++kk) {
+            const uint64_t ko = ((kk >> 2) * TILE + (kk & 3) * 32) >> 4;   // descriptor units of 16 bytes
+            umma_bf16(tmem + col_g(kb), dC + ko, dB + ko, ID_KK, kk > 0);
+          }
+          umma_commit(&gfull[kb]);
+          ++mc;
+          prog = true;
+        }
+        if (prog) {
+          t_prog = globaltimer_ns();
+        } else {
+          if (*abort_flag) break;
+          if (globaltimer_ns() - t_prog > 2000000000ull) {
+            fail(1001);
+            break;
+          }
+          __nanosleep(32);   // leave issue slots to the compute warps on this sub-partition
+        }
+      }
+      *issued = pc;
     }
-    load_dt(0);
-    int c = 0;
-    for (; c < nchunks; ++c) {
+  } else if (warp == 11) {
+    // ================================================================ decay warp
+    // dt of chunk i streams into the raw-dt slot of stage i % ST with cp.async,
+    // ST-1 chunks ahead, so the per-chunk work never waits on global latency.
+    const float* dtp = dt + (int64_t)b * L * H + h;
+    auto issue_dt = [&](int i) {
+      if (i < nchunks) {
+        float* slot = small_ptr(i % ST) + 256;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = i * Q + 2 * lane + e;
+          if (t < L)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(slot + 2 * lane + e)),
+                         "l"(dtp + (int64_t)t * H)
+                         : "memory");
+          else
+            slot[2 * lane + e] = 0.f;
+        }
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int i = 0; i < ST - 1; ++i) issue_dt(i);
+    for (int c = 0; c < nchunks; ++c) {
       const int s = c % ST, k = c / ST;
       int bad = 0;   // decided by lane 0, broadcast so the warp stays converged
       if (lane == 0) {
         if (c >= ST && !mbar_wait(&empty[s], (k - 1) & 1, abort_flag)) {
-          if (!*abort_flag) fail(1001);
+          if (!*abort_flag) fail(1010);
           bad = 1;
         }
         bad |= *abort_flag;
       }
       if (__shfl_sync(0xffffffffu, bad, 0)) break;
-      uint8_t* st = stage_ptr(s);
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], LY::STAGE_BYTES);
-        tma_load_3d(st, &tm_x, h * P, c * Q, b, &full[s]);
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-          tma_load_3d(st + TILE * (1 + nb), &tm_b, h * NST + nb * 64, c * Q, b, &full[s]);
-          tma_load_3d(st + TILE * (1 + NB + nb), &tm_c, h * NST + nb * 64, c * Q, b, &full[s]);
-        }
-      }
+      issue_dt(c + ST - 1);
+      asm volatile("cp.async.wait_group %0;" ::"n"(ST - 1) : "memory");
+      if (lane == 0) SSD_TRACE(c, 12);
+      const float d0 = small_ptr(s)[256 + 2 * lane], d1 = small_ptr(s)[256 + 2 * lane + 1];
       // decay prefix sums (log2 domain) and input coefficients of chunk c
-      const float d0 = dn0, d1 = dn1;
-      if (c + 1 < nchunks) load_dt(c + 1);
       const float l0 = d0 * a2, l1 = d1 * a2;
       const float pair = l0 + l1;
       float incl = pair;
@@ -201,68 +270,65 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         b0 = d0;
         b1 = d1;
       }
+      // per token: s_j (log2 domain), s'_j = s_j - log2(beta_j) (beta = 0 -> +inf, so the
+      // mask entry exp2(s_i - s'_j) is exactly 0), and the state weight w_j = exp2(s_last - s_j) beta_j
       float* sm = small_ptr(s);
       sm[2 * lane] = s0;
       sm[2 * lane + 1] = s1;
-      sm[64 + 2 * lane] = b0;
-      sm[64 + 2 * lane + 1] = b1;
+      sm[64 + 2 * lane] = b0 > 0.f ? s0 - __log2f(b0) : INFINITY;
+      sm[64 + 2 * lane + 1] = b1 > 0.f ? s1 - __log2f(b1) : INFINITY;
       sm[128 + 2 * lane] = exp2f(slast - s0) * b0;
       sm[128 + 2 * lane + 1] = exp2f(slast - s1) * b1;
       if (lane == 0) sm[192] = exp2f(slast);
+      if (lane == 0) SSD_TRACE(c, 13);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full[s]);
+      if (lane == 0) {
+        SSD_TRACE(c, 1);
+        mbar_arrive(&full[s]);
+      }
     }
-    if (lane == 0) *issued = c;
+    asm volatile("cp.async.wait_all;" ::: "memory");   // no copy may outlive the loop
   } else if (warp == 9) {
-    // ================================================================ MMA issuer
+    // ================================================================ MMA2 + MMA4 issuer
     if (lane == 0) {
-      constexpr uint32_t ID_KK = make_idesc_bf16(64, 64, false, false);
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
       constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
-      for (int c = 0; c <= nchunks; ++c) {
-        if (c < nchunks) {
-          const int s = c % ST, kb = c & 1;
-          if (!mbar_wait(&full[s], (c / ST) & 1, abort_flag)) { if (!*abort_flag) fail(1002); break; }
-          if (c >= 2 && !mbar_wait(&gfree[kb], ((c - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1003); break; }
-          tc_fence_after();
-          const uint32_t X = smem_u32(stage_ptr(s));
-          const uint32_t Bt = X + TILE, Ct = X + TILE * (1 + NB);
+      for (int k = 0; k < nchunks; ++k) {
+        const int s = k % ST, kb = k & 1;
+        if (!mbar_wait(&mready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1004); break; }
+        if (k >= 2 && !mbar_wait(&tfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1005); break; }
+        mbar_wait(&full[s], (k / ST) & 1);
+        tc_fence_after();
+        SSD_TRACE(k, 3);
+        const uint32_t X = smem_u32(stage_ptr(s));
+        const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
+        const uint64_t dX = make_desc_sw128(X, TILE), dBh = make_desc_sw128(X + TILE, TILE);
 #pragma unroll
-          for (int kk = 0; kk < NST / 16; ++kk) {
-            const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
-            umma_bf16(tmem + col_g(kb), make_desc_sw128(Ct + koff, 16), make_desc_sw128(Bt + koff, 16), ID_KK,
-                      kk > 0);
-          }
-          umma_commit(&gfull[kb]);
+        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_y1(kb), dM + 2 * kk, dX + 128 * kk, ID_KM, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_s(kb), dBh + 128 * kk, dX + 128 * kk, ID_MM, kk > 0);
+        umma_commit(&yfull[kb]);
+      }
+    }
+  } else if (warp == 10) {
+    // ================================================================ MMA3 issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
+      for (int k = 0; k < nchunks; ++k) {
+        const int s = k % ST, kb = k & 1;
+        if (!mbar_wait(&hready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1006); break; }
+        if (k >= 2 && !mbar_wait(&tfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1011); break; }
+        if (!mbar_wait(&full[s], (k / ST) & 1, abort_flag)) { if (!*abort_flag) fail(1012); break; }
+        tc_fence_after();
+        SSD_TRACE(k, 4);
+        const uint64_t dC = make_desc_sw128(smem_u32(stage_ptr(s)) + TILE * (1 + NB), 16);
+        const uint64_t dH = make_desc_sw128(smem_u32(hs_ptr(kb)), TILE);
+#pragma unroll
+        for (int kk = 0; kk < NST / 16; ++kk) {
+          const uint64_t ko = ((kk >> 2) * TILE + (kk & 3) * 32) >> 4;
+          umma_bf16(tmem + col_y2(kb), dC + ko, dH + 128 * kk, ID_KM, kk > 0);
         }
-        if (c >= 1) {
-          const int k = c - 1, s = k % ST, kb = k & 1;
-          if (!mbar_wait(&mready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1004); break; }
-          if (k >= 2 && !mbar_wait(&tfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1005); break; }
-          tc_fence_after();
-          const uint32_t X = smem_u32(stage_ptr(s));
-          const uint32_t Bt = X + TILE, Ct = X + TILE * (1 + NB);
-          const uint32_t Mt = smem_u32(mt_ptr(kb));
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + col_y1(kb), make_desc_sw128(Mt + kk * 32, 16), make_desc_sw128(X + kk * 2048, TILE),
-                      ID_KM, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + col_s(kb), make_desc_sw128(Bt + kk * 2048, TILE), make_desc_sw128(X + kk * 2048, TILE),
-                      ID_MM, kk > 0);
-          umma_commit(&yfull[kb]);
-          if (!mbar_wait(&hready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1006); break; }
-          tc_fence_after();
-          const uint32_t Hs = smem_u32(hs_ptr(kb));
-#pragma unroll
-          for (int kk = 0; kk < NST / 16; ++kk) {
-            const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
-            umma_bf16(tmem + col_y2(kb), make_desc_sw128(Ct + koff, 16), make_desc_sw128(Hs + kk * 2048, TILE),
-                      ID_KM, kk > 0);
-          }
-          umma_commit(&y2full[kb]);
-        }
+        umma_commit(&y2full[kb]);
       }
     }
   } else if (warp >= 4) {
@@ -276,60 +342,68 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       const int s = c % ST, kb = c & 1;
       bool bad = false;
       if (t == 0) {
-        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag) ||
-              (c >= 2 && !mbar_wait(&yfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
+        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag);
+        SSD_TRACE(c, 14);
+        bad = bad || (c >= 2 && !mbar_wait(&yfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
         if (bad && !*abort_flag) fail(1007);
       }
       if (named_bar_or(2, 128, bad)) break;
+      if (t == 0) SSD_TRACE(c, 5);
       mbar_wait(&full[s], (c / ST) & 1);
       mbar_wait(&gfull[kb], (c >> 1) & 1);
       tc_fence_after();
       const float* sm = small_ptr(s);
       uint8_t* X = stage_ptr(s);
       uint8_t* Bt = X + TILE;
-      // M row `row`, columns [32*half, 32*half+32)
+      // M row `row`, columns [32*half, 32*half+32): M_ij = G_ij * exp2(s_i - s'_j) for j <= i
       float g[32];
       tmem_ld16x2_32(tmem + lane_base + col_g(kb), g);
-      tmem_wait_ld();
       {
         const float si = sm[row];
+        const float4* spv = reinterpret_cast<const float4*>(sm + 64 + half * 32);
+        const int nvalid = row - half * 32;      // columns jj <= nvalid are kept
         uint8_t* Mt = mt_ptr(kb);
+        tmem_wait_ld();
+        if (t == 0) SSD_TRACE(c, 15);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint32_t w4[4];
+          const float4 sa = spv[2 * q], sb = spv[2 * q + 1];
+          const float sp[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+          float m[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int jj = q * 8 + 2 * e;
-            const int j0 = half * 32 + jj;
-            const float m0 = j0 <= row ? g[jj] * exp2f(si - sm[j0]) * sm[64 + j0] : 0.f;
-            const float m1 = j0 + 1 <= row ? g[jj + 1] * exp2f(si - sm[j0 + 1]) * sm[64 + j0 + 1] : 0.f;
-            w4[e] = pack_bf16x2(m0, m1);
+          for (int e = 0; e < 8; ++e) {
+            const int jj = q * 8 + e;
+            const float v = g[jj] * fast_exp2(si - sp[e]);
+            m[e] = jj <= nvalid ? v : 0.f;
           }
-          *reinterpret_cast<uint4*>(Mt + sw128_chunk(row, half * 4 + q)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          *reinterpret_cast<uint4*>(Mt + sw128_chunk(row, half * 4 + q)) =
+              make_uint4(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]), pack_bf16x2(m[4], m[5]),
+                         pack_bf16x2(m[6], m[7]));
         }
       }
-      // B <- diag(w) B in place (MMA1 of this chunk is complete)
+      if (t == 0) SSD_TRACE(c, 16);
+      // B <- diag(w) B in place, bf16x2 arithmetic (MMA1 of this chunk is complete)
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
           const int idx = t + it * 128;            // 16-byte chunk; row j = idx / 8
           uint4* pch = reinterpret_cast<uint4*>(Bt + nb * TILE + idx * 16);
-          float f[8];
-          unpack_bf16x8(*pch, f);
-          const float wj = sm[128 + (idx >> 3)];
-          uint4 o;
-          o.x = pack_bf16x2(f[0] * wj, f[1] * wj);
-          o.y = pack_bf16x2(f[2] * wj, f[3] * wj);
-          o.z = pack_bf16x2(f[4] * wj, f[5] * wj);
-          o.w = pack_bf16x2(f[6] * wj, f[7] * wj);
-          *pch = o;
+          const __nv_bfloat162 w2 = __float2bfloat162_rn(sm[128 + (idx >> 3)]);
+          uint4 v = *pch;
+          __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v);
+          hv[0] = __hmul2(hv[0], w2);
+          hv[1] = __hmul2(hv[1], w2);
+          hv[2] = __hmul2(hv[2], w2);
+          hv[3] = __hmul2(hv[3], w2);
+          *pch = v;
         }
       }
       fence_proxy_async_smem();
       tc_fence_before();
       named_bar_sync(2, 128);
       if (t == 0) {
+        SSD_TRACE(c, 6);
         mbar_arrive(&gfree[kb]);
         mbar_arrive(&mready[kb]);
       }
@@ -374,83 +448,92 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       bool bad = false;
       if (tid == 0) {
         bad = !mbar_wait(&yfull[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
+        SSD_TRACE(c, 17);
         if (bad && !*abort_flag) fail(1008);
       }
       if (named_bar_or(1, 128, bad)) break;
+      if (tid == 0) SSD_TRACE(c, 7);
       mbar_wait(&full[s], (c / ST) & 1);
       mbar_wait(&yfull[kb], (c >> 1) & 1);
       tc_fence_after();
       const float* sm = small_ptr(s);
       const float e_last = sm[192];
-      // ---- carried state: H <- exp(s_last) H + S ; bf16 copy for MMA3 of chunk c+1
+      // ---- carried state: H <- exp(s_last) H + S ; bf16 copy for MMA3 of chunk c+1.
+      // Y1 (ready together with S) is fetched in the same TMEM round trip.
+      float y1[32];
       if (NST == 64) {
         float sv[32];
         tmem_ld16x2_32(tmem + lane_base + col_s(kb), sv);
+        tmem_ld16x2_32(tmem + lane_base + col_y1(kb), y1);
         tmem_wait_ld();
+        if (tid == 0) SSD_TRACE(c, 18);
 #pragma unroll
         for (int j = 0; j < 32; ++j) hreg[j] = e_last * hreg[j] + sv[j];
       } else {
+        float sv[32];
+        tmem_ld32(tmem + lane_base + col_s(kb), sv);
+        tmem_ld16x2_32(tmem + lane_base + col_y1(kb), y1);
+        tmem_wait_ld();
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float sv[32];
-          tmem_ld32(tmem + lane_base + col_s(kb) + hh * 32, sv);
-          tmem_wait_ld();
+        for (int j = 0; j < 32; ++j) hreg[j] = e_last * hreg[j] + sv[j];
+        tmem_ld32(tmem + lane_base + col_s(kb) + 32, sv);
+        tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) hreg[hh * 32 + j] = e_last * hreg[hh * 32 + j] + sv[j];
-        }
+        for (int j = 0; j < 32; ++j) hreg[32 + j] = e_last * hreg[32 + j] + sv[j];
       }
       write_hs(hs_ptr((c + 1) & 1));
       fence_proxy_async_smem();
       named_bar_sync(1, 128);
-      if (tid == 0) mbar_arrive(&hready[(c + 1) & 1]);
+      if (tid == 0) {
+        SSD_TRACE(c, 8);
+        mbar_arrive(&hready[(c + 1) & 1]);
+      }
       // ---- output rows
       if (tid == 0) {
         bad = !mbar_wait(&y2full[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
         if (bad && !*abort_flag) fail(1009);
       }
       if (named_bar_or(1, 128, bad)) break;
+      if (tid == 0) SSD_TRACE(c, 9);
       mbar_wait(&y2full[kb], (c >> 1) & 1);
       tc_fence_after();
       {
-        float y1[32], y2[32];
-        tmem_ld16x2_32(tmem + lane_base + col_y1(kb), y1);
+        float y2[32];
         tmem_ld16x2_32(tmem + lane_base + col_y2(kb), y2);
-        tmem_wait_ld();
         const float ei = exp2f(sm[row]);
         const uint8_t* X = stage_ptr(s);
-        uint8_t* Ys = ys_ptr(kb);
+        const int tok = c * Q + row;
+        uint4* dst = reinterpret_cast<uint4*>(y + ((int64_t)b * L + tok) * HPtot + h * P + half * 32);
+        tmem_wait_ld();
+        if (tid == 0) SSD_TRACE(c, 19);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int cc = half * 4 + q;
           float xf[8];
           unpack_bf16x8(*reinterpret_cast<const uint4*>(X + sw128_chunk(row, cc)), xf);
+          const float4 da = *reinterpret_cast<const float4*>(dsk + cc * 8);
+          const float4 db = *reinterpret_cast<const float4*>(dsk + cc * 8 + 4);
+          const float d8[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
           uint32_t w4[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int jj = q * 8 + 2 * e;
-            const int pp = cc * 8 + 2 * e;
-            const float o0 = y1[jj] + ei * y2[jj] + dsk[pp] * xf[2 * e];
-            const float o1 = y1[jj + 1] + ei * y2[jj + 1] + dsk[pp + 1] * xf[2 * e + 1];
+            const float o0 = y1[jj] + ei * y2[jj] + d8[2 * e] * xf[2 * e];
+            const float o1 = y1[jj + 1] + ei * y2[jj + 1] + d8[2 * e + 1] * xf[2 * e + 1];
             w4[e] = pack_bf16x2(o0, o1);
           }
-          *reinterpret_cast<uint4*>(Ys + sw128_chunk(row, cc)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          if (tok < L) dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       named_bar_sync(1, 128);
       if (tid == 0) {
-        tma_store_3d(&tm_y, ys_ptr(kb), h * P, c * Q, b);
-        bulk_commit();
-        bulk_wait_read<1>();
+        SSD_TRACE(c, 10);
         mbar_arrive(&tfree[kb]);
         mbar_arrive(&empty[s]);
       }
     }
-    if (tid == 0) {
-      *consumed = c;
-      bulk_wait<0>();
-    }
+    if (tid == 0) *consumed = c;
     if (h_last && !*abort_flag) {
       float* dst = h_last + (((int64_t)b * H + h) * P) * NST + n_own;
 #pragma unroll
@@ -497,7 +580,7 @@ bool map3d_bf16(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint
 }
 
 template <int NST, bool ZOH>
-int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& my,
+int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& mc, __nv_bfloat16* y,
                const float* dt, const float* A_log, const float* Dskip, const float* h0, float* h_last,
                int64_t Bsz, int64_t L, int64_t H, cudaStream_t st) {
   constexpr int bytes = Layout<NST>::BYTES;
@@ -511,7 +594,7 @@ int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& 
     return TSSM_ERR_CUDA;
   }
   dim3 grid((unsigned)H, (unsigned)Bsz);
-  kern<<<grid, NTHREADS, bytes, st>>>(mx, mb, mc, my, dt, A_log, Dskip, h0, h_last, status, (int)L, (int)H);
+  kern<<<grid, NTHREADS, bytes, st>>>(mx, mb, mc, y, dt, A_log, Dskip, h0, h_last, status, (int)L, (int)H);
   return check_launch("ssd_chunk_scan");
 }
 
@@ -533,11 +616,10 @@ extern "C" int tssm_multihead_ssd(const void* x, const void* dt, const void* A_l
                "multihead_ssd: x, B, C, y must be 16-byte aligned");
   TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31) && H * N < (int64_t(1) << 31),
                "multihead_ssd: size out of range");
-  CUtensorMap mx, mb, mc, my;
+  CUtensorMap mx, mb, mc;
   if (!map3d_bf16(&mx, x, (uint64_t)(H * P), (uint64_t)L, (uint64_t)Bsz) ||
       !map3d_bf16(&mb, B, (uint64_t)(H * N), (uint64_t)L, (uint64_t)Bsz) ||
-      !map3d_bf16(&mc, C, (uint64_t)(H * N), (uint64_t)L, (uint64_t)Bsz) ||
-      !map3d_bf16(&my, y, (uint64_t)(H * P), (uint64_t)L, (uint64_t)Bsz)) {
+      !map3d_bf16(&mc, C, (uint64_t)(H * N), (uint64_t)L, (uint64_t)Bsz)) {
     set_error("multihead_ssd: cuTensorMapEncodeTiled failed");
     return TSSM_ERR_CUDA;
   }
@@ -547,9 +629,17 @@ extern "C" int tssm_multihead_ssd(const void* x, const void* dt, const void* A_l
   const float* dk = (const float*)Dskip;
   const float* hi = (const float*)h0;
   float* ho = (float*)h_last;
+  __nv_bfloat16* my = (__nv_bfloat16*)y;
   if (N == 64)
     return bdisc ? launch_ssd<64, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st)
                  : launch_ssd<64, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st);
   return bdisc ? launch_ssd<128, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st)
                : launch_ssd<128, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st);
 }
+
+#ifdef TSSM_SSD_TRACE
+extern "C" int tssm_debug_read_ssd_trace(unsigned long long* out, int n) {
+  return cudaMemcpyFromSymbol(out, tssm::g_ssd_trace, sizeof(unsigned long long) * (n < 1536 ? n : 1536)) ==
+                 cudaSuccess ? 0 : 3;
+}
+#endif
