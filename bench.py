@@ -202,40 +202,181 @@ def run_reference(args, rank, world):
     }
 
 
+def _timed(args, world, dev, step):
+    """Warm-up, >= 1 s of untimed load (so the clock samples see the GPU busy),
+    then exactly args.steps timed steps; returns (seconds per step, clocks).
+    With --graph the step is captured once in a CUDA graph and the timed loop
+    replays it, so host-side Python overhead is not what gets measured."""
+    import triton_ssm_b200 as ts
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    ts.check_device_status()
+    if args.graph:
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        step = graph.replay
+        step()
+        torch.cuda.synchronize()
+    barrier(world)
+    t_end = time.perf_counter() + (0.0 if args.no_soak else 1.0)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        while time.perf_counter() < t_end:
+            for _ in range(5):
+                step()
+            torch.cuda.synchronize()
+        barrier(world)
+        el = time_loop(step, args.steps, stream)
+    ts.check_device_status()
+    return max_over_ranks(el, world) / args.steps, clk.summary()
+
+
+def _line(args, world, metric, value, t_step, dtype, cfg, alg_bytes, kernel, profile, clocks, cpu=None,
+          e2e=None, launches=None, extra=None):
+    peak, peak_kind = peaks()
+    achieved = alg_bytes / t_step / 1e9
+    out = {
+        "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": cfg,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": alg_bytes,
+                     "traffic": read_profile_traffic(profile) if profile else None, "kernel": kernel},
+        "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": launches if launches is not None else args.steps, "clocks": clocks,
+    }
+    if extra:
+        out.update(extra)
+    return out
+
+
+def run_ours_c3(args, rank, world, local):
+    """Config 3: fused interpolation + SSM, B32 L_obs 2048 -> L_q 4096, D256 N16, f32."""
+    import triton_ssm_b200 as ts
+    from triton_ssm_b200 import workloads
+    dev = torch.device("cuda", local)
+    c = workloads.C3
+    Bt, T, Lq, Dm, N = args.batch or c["Bt"], c["T"], c["Lq"], c["D"], c["N"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    V = torch.randn(Bt, T, Dm, device=dev, generator=g)
+    M = (torch.rand(Bt, T, Dm, device=dev, generator=g) < 0.7).to(torch.uint8)
+    tau = torch.cumsum(torch.empty(Bt, T, device=dev).exponential_(1.0, generator=g), 1)
+    A_log = torch.log(torch.arange(1, N + 1, device=dev, dtype=torch.float32)).repeat(Dm, 1)
+    B = torch.randn(Dm, N, device=dev, generator=g) / math.sqrt(N)
+    C = torch.randn(Dm, N, device=dev, generator=g) / math.sqrt(N)
+    q = ts.linspace_queries(tau, Lq)
+    dt = ((tau[:, -1] - tau[:, 0]) / (Lq - 1)).contiguous()
+    ws = torch.empty(ts.interp_ssm_workspace_bytes(Bt, T, Dm, Lq), dtype=torch.uint8, device=dev)
+    step = lambda: ts.fused_interp_ssm(V, M, tau, A_log, B, C, q=q, dt=dt, workspace=ws, return_state=True)
+    t_step, clocks = _timed(args, world, dev, step)
+    upd = Bt * Lq * Dm * N
+    alg = Bt * T * Dm * 4 + Bt * T * Dm + Bt * T * 4 + Bt * Lq * Dm * 4 + Bt * Dm * N * 4 + 3 * Dm * N * 4
+    cfg = {"workload": "config3: interpolation of irregular obs onto a regular query grid fused with an "
+                       "N-state ZOH scan, B%d L_obs %d -> L_q %d, D %d, N %d, f32, mask Bernoulli(0.7) u8" %
+                       (Bt, T, Lq, Dm, N),
+           "global_batch": Bt * world, "seq_len": Lq, "parallelism": "batch, %d rank(s)" % world}
+    return _line(args, world, METRIC, world * upd / t_step, t_step, "f32", cfg, alg,
+                 "interp_flags + interp_neighbors + interp_ssm_scan", "interp_ssm_c3.md", clocks,
+                 launches=3 * args.steps)
+
+
+def run_ours_c5(args, rank, world, local):
+    """Config 5: streaming single-step update, 4096 streams, H16 P64 N64, f32 state."""
+    import triton_ssm_b200 as ts
+    from triton_ssm_b200 import workloads
+    dev = torch.device("cuda", local)
+    c = workloads.C5
+    S = args.batch or c["S"]
+    H, P, N = c["H"], c["P"], c["N"]
+    w = workloads.stream_inputs(S, H, P, N, dev, seed=5 + rank)
+    ev = w["events"]
+    y = torch.empty(S, H, P, device=dev, dtype=torch.bfloat16)
+    k = [0]
+
+    def step():
+        e = ev[k[0] % len(ev)]
+        k[0] += 1
+        ts.streaming_step(e["x"], e["dt"], w["h"], w["A_log"], e["B"], e["C"], w["D"], y=y)
+    t_step, clocks = _timed(args, world, dev, step)
+    # per-step latency distribution (event pairs around single steps)
+    lat = []
+    for _ in range(min(200, max(20, args.steps))):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        e1.synchronize()
+        lat.append(e0.elapsed_time(e1))
+    lat.sort()
+    upd = S * H * P * N
+    cfg = {"workload": "config5: streaming ZOH step, %d streams x H%d P%d N%d, f32 state in HBM, "
+                       "bf16 events cycled from 16 sets" % (S, H, P, N),
+           "global_batch": S * world, "seq_len": 1, "parallelism": "streams, %d rank(s)" % world,
+           "l2": "state (%d MB) larger than the 126 MB L2" % (S * H * P * N * 4 // 2**20)}
+    return _line(args, world, METRIC, world * upd / t_step, t_step, "f32", cfg,
+                 workloads.stream_bytes(S, H, P, N), "streaming_step_kernel<bf16,16,2>", "streaming_step_c5.md",
+                 clocks, extra={"steps_per_sec": 1.0 / t_step, "p50_step_ms": lat[len(lat) // 2],
+                                "p99_step_ms": lat[int(len(lat) * 0.99) - 1]})
+
+
+def run_ours_c1(args, rank, world, local):
+    """Config 1: ZOH discretize + diagonal scan, B4 L1024 D64 N16 f32: the drop-in
+    pair (zoh_discretize -> ssm_forward over H' = D*N) and the fused kernel."""
+    import triton_ssm_b200 as ts
+    dev = torch.device("cuda", local)
+    Bt, L, Dm, N = 4, 1024, 64, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+    x = torch.randn(Bt, L, Dm, device=dev, generator=g)
+    dt = torch.empty(Bt, L, device=dev).exponential_(1.0, generator=g).clamp_(1e-3, 10.0)
+    A_log = torch.log(torch.arange(1, N + 1, device=dev, dtype=torch.float32)).repeat(Dm, 1)
+    Bs = torch.randn(Bt, L, N, device=dev, generator=g) / math.sqrt(N)
+    Cs = torch.randn(Bt, L, N, device=dev, generator=g) / math.sqrt(N)
+    D = torch.randn(Dm, device=dev, generator=g)
+    Hp = Dm * N
+    B_exp = Bs[:, :, None, :].expand(Bt, L, Dm, N).reshape(Bt, L, Hp).contiguous()
+    C_exp = Cs[:, :, None, :].expand(Bt, L, Dm, N).reshape(Bt, L, Hp).contiguous()
+    u_exp = x[:, :, :, None].expand(Bt, L, Dm, N).reshape(Bt, L, Hp).contiguous()
+    Al = A_log.reshape(-1).contiguous()
+    Dz = torch.zeros(Hp, device=dev)
+    if args.c1_mode == "pair":
+        def step():
+            Ab, Bb = ts.zoh_discretize(Al, B_exp, dt)
+            ts.ssm_forward(u_exp, Ab, Bb, C_exp, Dz)
+        alg = 151019520
+        kern = "zoh_discretize_kernel + ssm_forward_kernel"
+        launches = 2 * args.steps
+    else:
+        step = lambda: ts.selective_scan(x, dt, A_log, Bs, Cs, D)
+        alg = 2642176
+        kern = "selective_scan_kernel"
+        launches = args.steps
+    t_step, clocks = _timed(args, world, dev, step)
+    upd = Bt * L * Dm * N
+    cfg = {"workload": "config1 (%s): ZOH discretize + selective scan B4 L1024 D64 N16 f32" % args.c1_mode,
+           "global_batch": Bt * world, "seq_len": L, "parallelism": "batch, %d rank(s)" % world}
+    return _line(args, world, METRIC, world * upd / t_step, t_step, "f32", cfg, alg, kern, None, clocks,
+                 launches=launches)
+
+
 def run_ours_c2(args, rank, world, local):
     import triton_ssm_b200 as ts
     from triton_ssm_b200 import workloads
-    from triton_ssm_b200.host import SSDHostPipeline
     ts.load_library()
     dev = torch.device("cuda", local)
     c = workloads.C2
     Bt, L, H, P, N = args.batch or c["Bt"], c["L"], c["H"], c["P"], c["N"]
     inp = workloads.ssd_inputs(Bt, L, H, P, N, dev, seed=1234 + rank)
     y = torch.empty_like(inp["x"])
-    stream = torch.cuda.current_stream(dev)
     step = lambda: ts.multihead_ssm(inp["x"], inp["A_log"], inp["B"], inp["C"], inp["dt"], inp["D"], y=y)
-
-    for _ in range(args.warmup):
-        step()
-    ts.check_device_status()
-    barrier(world)
-    # keep the GPU busy for >= 1 s before timing so the clock samples reflect load
-    t_end = time.perf_counter() + (0.0 if args.no_soak else 1.0)
-    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
-        while time.perf_counter() < t_end:
-            for _ in range(20):
-                step()
-            torch.cuda.synchronize()
-        barrier(world)
-        el = time_loop(step, args.steps, stream)
-    ts.check_device_status()
-    el = max_over_ranks(el, world)
-    t_step = el / args.steps
+    t_step, clocks = _timed(args, world, dev, step)
     upd = workloads.ssd_updates(Bt, L, H, P, N)
     value = world * upd / t_step
     alg_bytes = workloads.ssd_bytes(Bt, L, H, P, N)
-    peak, peak_kind = peaks()
-    achieved = alg_bytes / t_step / 1e9
 
     # ---- end to end through the public host-buffer API (pinned host memory)
     e2e = None
@@ -246,26 +387,13 @@ def run_ours_c2(args, rank, world, local):
     if rank == 0 and world == 1 and not args.no_cpu:
         r, thr, sample = cpu_ssd_rate(Bt, H, P, N, 512, args.cpu_seconds)
         cpu = {"value": r, "unit": UNIT, "cores": thr, "kind": "port", "sample": sample}
-
-    return {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t_step * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config2: multi-head chunked scan (SSD state) B%d H8 P64 N64 L8192, "
-                               "chunk 256 (kernel tile 64), Euler B, bf16 in / f32 state" % Bt,
-                   "global_batch": Bt * world, "seq_len": L, "heads": H, "head_dim": P, "d_state": N,
-                   "parallelism": "batch x head, %d independent rank(s)" % world,
-                   "l2": "inputs (%d MB/step) larger than the 126 MB L2; no flush" % (alg_bytes // 2**20)},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_launch": alg_bytes,
-                     "traffic": read_profile_traffic("ssd_chunk_scan_c2.md"),
-                     "kernel": "ssd_chunk_scan_kernel<64,false>"},
-        "cpu_baseline": cpu,
-        "e2e": e2e,
-        "gpu_launches": args.steps,
-        "clocks": clk.summary(),
-    }
+    cfg = {"workload": "config2: multi-head chunked scan (SSD state) B%d H8 P64 N64 L8192, "
+                       "chunk 256 (kernel tile 64), Euler B, bf16 in / f32 state" % Bt,
+           "global_batch": Bt * world, "seq_len": L, "heads": H, "head_dim": P, "d_state": N,
+           "parallelism": "batch x head, %d independent rank(s)" % world,
+           "l2": "inputs (%d MB/step) larger than the 126 MB L2; no flush" % (alg_bytes // 2**20)}
+    return _line(args, world, METRIC, value, t_step, "bf16", cfg, alg_bytes, "ssd_chunk_scan_kernel<64,false>",
+                 "ssd_chunk_scan_c2.md", clocks, cpu=cpu, e2e=e2e)
 
 
 def run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd):
@@ -308,6 +436,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s pre-timing load")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c5"], default="c2",
+                    help="workload (default c2, the headline; the others are for measurement notes)")
+    ap.add_argument("--c1-mode", choices=["pair", "fused"], default="pair")
+    ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays of the step")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_env()
@@ -325,7 +457,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        out = run_ours_c2(args, rank, world, local)
+        runner = {"c1": run_ours_c1, "c2": run_ours_c2, "c3": run_ours_c3, "c5": run_ours_c5}[args.config]
+        out = runner(args, rank, world, local)
         if rank == 0:
             print(json.dumps(out), flush=True)
     finally:

@@ -34,6 +34,10 @@ SIGNATURES = {
     "tssm_streaming_step": ([P] * 8 + [I64] * 4 + [I32, P], I32),
     "tssm_multihead_ssd": ([P] * 9 + [I64] * 5 + [I32, P], I32),
     "tssm_check_device_status": ([P], I32),
+    "tssm_time_aware_interp": ([P] * 4 + [I64] * 3 + [I64] * 7 + [I64] * 2 + [I32, I32, P], I32),
+    "tssm_interp_ssm_step": ([P] * 8 + [I64] * 3 + [I64] * 9 + [I64] * 3 + [I32, P], I32),
+    "tssm_interp_ssm_workspace_size": ([I64] * 5, I64),
+    "tssm_interp_ssm": ([P] * 13 + [I64] + [I64] * 7 + [I32, P], I32),
 }
 
 _lib = None

@@ -1,0 +1,697 @@
+// Time-aware interpolation of irregular observations, alone and fused with the
+// SSM (replaces fused_interp_kernel.py:9-257 and fused_ssm_interp.py:11-101).
+//
+// Reference semantics (kept exactly): neighbours are searched per (b, t, tile
+// of FTILE features); the previous neighbour is the nearest of t-1..t-K whose
+// tile holds ANY observation (sum of mask values > 0.5), the next one the
+// nearest of t+1..t+K; w = clamp((tau_t - tau_p)/(tau_n - tau_p), 0, 1), or 0.5
+// when the denominator is <= 1e-9; priority both -> lerp, prev only -> v_prev,
+// next only -> v_next, none -> the current value.  The lerp is evaluated as
+// round((1-w)*v_p) + round(w*v_n) in IEEE fp32, as the reference does.
+//
+// Query (time) mode generalises "t" to an arbitrary sorted query time q:
+// lo = #{tau < q}, hi = #{tau <= q}; previous candidates are obs lo-1..lo-K,
+// next candidates hi..hi+K-1, and the fallback value is obs hi-1 when hi > lo
+// (an observation at exactly q), else 0.
+#include "common.cuh"
+
+namespace tssm {
+#ifdef TSSM_INTERP_TRACE
+// Debug-only per-block phase timestamps (clock64) of CTA (0,0), thread 0.
+__device__ unsigned long long g_interp_trace[128 * 8];
+#define IT_TRACE(blk, ev)                                                                          \
+  do {                                                                                             \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && (blk) < 128)                    \
+      g_interp_trace[(blk) * 8 + (ev)] = clock64();                                                \
+  } while (0)
+#else
+#define IT_TRACE(blk, ev) \
+  do {                    \
+  } while (0)
+#endif
+namespace {
+
+template <typename M>
+__device__ __forceinline__ float mval(const M* p) { return ldf(p); }
+template <>
+__device__ __forceinline__ float mval<uint8_t>(const uint8_t* p) { return (float)*p; }
+
+__device__ __forceinline__ float lerp_ref(float w, float vp, float vn) {
+  return __fadd_rn(__fmul_rn(1.0f - w, vp), __fmul_rn(w, vn));
+}
+__device__ __forceinline__ float weight_ref(float tq, float tp, float tn) {
+  const float denom = tn - tp;
+  float w = denom > 1e-9f ? __fdiv_rn(tq - tp, denom) : 0.5f;
+  return fminf(fmaxf(w, 0.0f), 1.0f);
+}
+
+// ---------------------------------------------------------------------------
+// Standalone interpolation, index mode (fused_time_aware_interp_kernel and its
+// bf16/fp16 twins).  CTA = (tile, b, block of TB time steps); the tile flags of
+// rows [t0-K, t0+TB+K) are computed once into shared memory.
+constexpr int TB = 64;
+
+template <typename V, typename M>
+__global__ void __launch_bounds__(128) time_aware_interp_kernel(
+    const V* __restrict__ Vp, const M* __restrict__ Mp, const float* __restrict__ tau, V* __restrict__ out,
+    int T, int F, int64_t svb, int64_t svt, int64_t smb, int64_t smt, int64_t stb, int64_t sob, int64_t sot,
+    int K, int FTILE) {
+  extern __shared__ uint8_t sh[];
+  const int tile = blockIdx.x, b = blockIdx.y, t0 = blockIdx.z * TB;
+  const int f0 = tile * FTILE;
+  const int r0 = max(0, t0 - K), r1 = min(T, t0 + TB + K);   // flag rows [r0, r1)
+  uint8_t* flag = sh;                                        // [r1 - r0]
+  __shared__ int s_prev[TB], s_next[TB];
+  __shared__ float s_w[TB];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = r0 + warp; r < r1; r += 4) {
+    float acc = 0.f;
+    for (int f = lane; f < FTILE; f += 32)
+      if (f0 + f < F) acc += mval(Mp + b * smb + (int64_t)r * smt + f0 + f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) flag[r - r0] = acc > 0.5f;
+  }
+  __syncthreads();
+  if (threadIdx.x < TB) {
+    const int t = t0 + threadIdx.x;
+    int prev = -1, next = -1;
+    if (t < T) {
+      for (int k = 1; k <= K && prev < 0; ++k)
+        if (t - k >= 0 && flag[t - k - r0]) prev = t - k;
+      for (int k = 1; k <= K && next < 0; ++k)
+        if (t + k < T && flag[t + k - r0]) next = t + k;
+      const float tp = prev >= 0 ? tau[b * stb + prev] : 0.f;
+      const float tn = next >= 0 ? tau[b * stb + next] : 0.f;
+      s_w[threadIdx.x] = weight_ref(tau[b * stb + t], tp, tn);
+    }
+    s_prev[threadIdx.x] = prev;
+    s_next[threadIdx.x] = next;
+  }
+  __syncthreads();
+  const int tend = min(TB, T - t0);
+  for (int f = threadIdx.x; f < FTILE; f += blockDim.x) {
+    if (f0 + f >= F) break;
+    const int64_t fo = f0 + f;
+    for (int i = 0; i < tend; ++i) {
+      const int t = t0 + i, prev = s_prev[i], next = s_next[i];
+      float v = ldf(Vp + b * svb + (int64_t)t * svt + fo);
+      if (prev >= 0 && next >= 0)
+        v = lerp_ref(s_w[i], ldf(Vp + b * svb + (int64_t)prev * svt + fo), ldf(Vp + b * svb + (int64_t)next * svt + fo));
+      else if (prev >= 0)
+        v = ldf(Vp + b * svb + (int64_t)prev * svt + fo);
+      else if (next >= 0)
+        v = ldf(Vp + b * svb + (int64_t)next * svt + fo);
+      stf(out + b * sob + (int64_t)t * sot + fo, v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused interpolation at one time index + one SSM step (fused_interp_ssm_step_kernel).
+template <typename M>
+__global__ void __launch_bounds__(128) interp_step_kernel(
+    const float* __restrict__ Vp, const M* __restrict__ Mp, const float* __restrict__ tau,
+    const float* __restrict__ Abar, const float* __restrict__ Bbar, const float* __restrict__ h_in,
+    float* __restrict__ Vhat, float* __restrict__ h_out, int T, int F, int64_t svb, int64_t svt, int64_t smb,
+    int64_t smt, int64_t stb, int64_t sob, int64_t sot, int64_t shb, int64_t shob, int t_cur, int K, int FTILE) {
+  __shared__ uint8_t flag[2 * 64 + 1];
+  __shared__ int s_pn[2];
+  __shared__ float s_w;
+  const int tile = blockIdx.x, b = blockIdx.y, f0 = tile * FTILE;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int k = -K + warp; k <= K; k += 4) {
+    const int r = t_cur + k;
+    float acc = 0.f;
+    if (r >= 0 && r < T)
+      for (int f = lane; f < FTILE; f += 32)
+        if (f0 + f < F) acc += mval(Mp + b * smb + (int64_t)r * smt + f0 + f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) flag[k + K] = (r >= 0 && r < T) && acc > 0.5f;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int prev = -1, next = -1;
+    for (int k = 1; k <= K && prev < 0; ++k)
+      if (flag[K - k]) prev = t_cur - k;
+    for (int k = 1; k <= K && next < 0; ++k)
+      if (flag[K + k]) next = t_cur + k;
+    const float tp = prev >= 0 ? tau[b * stb + prev] : 0.f;
+    const float tn = next >= 0 ? tau[b * stb + next] : 0.f;
+    s_w = weight_ref(tau[b * stb + t_cur], tp, tn);
+    s_pn[0] = prev;
+    s_pn[1] = next;
+  }
+  __syncthreads();
+  const int prev = s_pn[0], next = s_pn[1];
+  for (int f = threadIdx.x; f < FTILE; f += blockDim.x) {
+    const int64_t fo = f0 + f;
+    if (fo >= F) break;
+    float v = Vp[b * svb + (int64_t)t_cur * svt + fo];
+    if (prev >= 0 && next >= 0)
+      v = lerp_ref(s_w, Vp[b * svb + (int64_t)prev * svt + fo], Vp[b * svb + (int64_t)next * svt + fo]);
+    else if (prev >= 0)
+      v = Vp[b * svb + (int64_t)prev * svt + fo];
+    else if (next >= 0)
+      v = Vp[b * svb + (int64_t)next * svt + fo];
+    if (Vhat) Vhat[b * sob + (int64_t)t_cur * sot + fo] = v;
+    h_out[b * shob + fo] = __fadd_rn(__fmul_rn(Abar[fo], h_in[b * shb + fo]), __fmul_rn(Bbar[fo], v));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused interpolation onto queries + N-state diagonal scan (config 3).
+//
+// Kernel 1: tile flags, flags[b][tile][t] = (sum of the tile's mask values > 0.5).
+template <typename M>
+__global__ void __launch_bounds__(256) interp_flags_kernel(const M* __restrict__ Mp, uint8_t* __restrict__ flags,
+                                                           int T, int F, int FTILE, int ntiles) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y;
+  const int64_t rows = (int64_t)T * ntiles;
+  for (int64_t r = warp; r < rows; r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int t = (int)(r / ntiles), tile = (int)(r - (int64_t)t * ntiles);
+    const M* row = Mp + ((int64_t)b * T + t) * F + (int64_t)tile * FTILE;
+    const int n = min(FTILE, F - tile * FTILE);
+    float acc = 0.f;
+    if (sizeof(M) == 1 && n == 128 && (F & 15) == 0 && (FTILE & 15) == 0) {
+      const uint32_t wv = reinterpret_cast<const uint32_t*>(row)[lane];
+      acc = (float)((wv & 0xFF) + ((wv >> 8) & 0xFF) + ((wv >> 16) & 0xFF) + (wv >> 24));
+    } else {
+      for (int f = lane; f < n; f += 32) acc += mval(row + f);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) flags[((int64_t)b * ntiles + tile) * T + t] = acc > 0.5f;
+  }
+}
+
+// Vectorised flags for byte masks with F and FTILE multiples of 16: each thread
+// sums the 16 bytes of one 16-byte word, the FTILE/16 words of a (row, tile)
+// are combined with shuffles inside their lane group.
+__global__ void __launch_bounds__(256) interp_flags_u8x16_kernel(const uint4* __restrict__ Mv,
+                                                                 uint8_t* __restrict__ flags, int64_t nwords,
+                                                                 int T, int wpr, int wpt, int ntiles) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // word index
+  uint32_t sum = 0;
+  if (i < nwords) {
+    const uint4 v = __ldcs(Mv + i);
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) sum += __dp4a(w4[k], 0x01010101u, 0u);   // unsigned byte sum
+  }
+  for (int o = wpt >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o, wpt);
+  if (i < nwords && (i % wpt) == 0) {
+    const int64_t row = i / wpr;                 // b*T + t
+    const int tile = (int)((i - row * wpr) / wpt);
+    const int64_t b = row / T, t = row - b * T;
+    flags[(b * ntiles + tile) * T + t] = sum > 0;
+  }
+}
+
+// Neighbour entry of one query for one tile.
+struct Nbr {
+  int prev, next, cur;
+  float w;
+};
+
+// Kernel 2: per (tile, b, query slice): last/next flagged index scans in shared
+// memory, then one entry per query.  Each thread walks a contiguous run of
+// sorted queries with two monotone pointers (lo = #{tau < q}, hi = #{tau <= q}).
+constexpr int NB_THREADS = 256;
+__global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint8_t* __restrict__ flags,
+                                                                      const float* __restrict__ tau,
+                                                                      const float* __restrict__ q,
+                                                                      Nbr* __restrict__ tab, int T, int Lq, int K,
+                                                                      int ntiles) {
+  extern __shared__ int shi[];
+  int* lastf = shi;          // [T] largest j <= i with flag[j], else -1
+  int* nextf = shi + T;      // [T] smallest j >= i with flag[j], else T (none)
+  float* stau = reinterpret_cast<float*>(shi + 2 * T);
+  __shared__ int agg_l[NB_THREADS], agg_n[NB_THREADS];
+  const int tile = blockIdx.x, b = blockIdx.y;
+  const uint8_t* fl = flags + ((int64_t)b * ntiles + tile) * T;
+  const float* tb = tau + (int64_t)b * T;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < T; i += NB_THREADS) {
+    lastf[i] = fl[i] ? i : -1;
+    nextf[i] = fl[i] ? i : T;
+    stau[i] = tb[i];
+  }
+  __syncthreads();
+  const int seg = (T + NB_THREADS - 1) / NB_THREADS;
+  const int s0 = min(T, tid * seg), s1 = min(T, s0 + seg);
+  int runl = -1, runn = T;
+  for (int i = s0; i < s1; ++i) runl = max(runl, lastf[i]);
+  for (int i = s1 - 1; i >= s0; --i) runn = min(runn, nextf[i]);
+  // exclusive max over earlier segments / min over later segments: warp scans + per-warp carries
+  int incl_l = runl, incl_n = runn;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int vl = __shfl_up_sync(0xffffffffu, incl_l, o);
+    const int vn = __shfl_down_sync(0xffffffffu, incl_n, o);
+    if (lane >= o) incl_l = max(incl_l, vl);
+    if (lane + o < 32) incl_n = min(incl_n, vn);
+  }
+  if (lane == 31) agg_l[warp] = incl_l;
+  if (lane == 0) agg_n[warp] = incl_n;
+  __syncthreads();
+  int cl = -1, cn = T;
+  for (int w = 0; w < warp; ++w) cl = max(cl, agg_l[w]);
+  for (int w = NB_THREADS / 32 - 1; w > warp; --w) cn = min(cn, agg_n[w]);
+  int excl_l = __shfl_up_sync(0xffffffffu, incl_l, 1);
+  int excl_n = __shfl_down_sync(0xffffffffu, incl_n, 1);
+  excl_l = lane == 0 ? cl : max(cl, excl_l);
+  excl_n = lane == 31 ? cn : min(cn, excl_n);
+  __syncthreads();
+  runl = excl_l;
+  for (int i = s0; i < s1; ++i) { runl = max(runl, lastf[i]); lastf[i] = runl; }
+  runn = excl_n;
+  for (int i = s1 - 1; i >= s0; --i) { runn = min(runn, nextf[i]); nextf[i] = runn; }
+  __syncthreads();
+
+  Nbr* out = tab + ((int64_t)b * ntiles + tile) * Lq;
+  const float* qb = q ? q + (int64_t)b * Lq : nullptr;
+  const int per_cta = (Lq + gridDim.z - 1) / gridDim.z;
+  const int qa = blockIdx.z * per_cta, qe = min(Lq, qa + per_cta);
+  const int per_thr = (qe - qa + NB_THREADS - 1) / NB_THREADS;
+  const int j0 = qa + tid * per_thr, j1 = min(qe, j0 + per_thr);
+  int lo = 0, hiq = 0;
+  if (qb && j0 < j1) {   // binary searches for the first query of the run
+    const float t0q = qb[j0];
+    int l = 0, h = T;
+    while (l < h) { const int m = (l + h) >> 1; if (stau[m] < t0q) l = m + 1; else h = m; }
+    lo = l;
+    h = T;
+    while (l < h) { const int m = (l + h) >> 1; if (stau[m] <= t0q) l = m + 1; else h = m; }
+    hiq = l;
+  }
+  for (int j = j0; j < j1; ++j) {
+    int prev = -1, next = -1, cur = -1;
+    float tq;
+    if (!qb) {   // index mode: query j is observation j
+      cur = j;
+      tq = stau[j];
+      if (j >= 1) {
+        const int p = lastf[j - 1];
+        if (p >= 0 && p >= j - K) prev = p;
+      }
+      if (j + 1 < T) {
+        const int n = nextf[j + 1];
+        if (n < T && n <= j + K) next = n;
+      }
+    } else {
+      tq = qb[j];
+      while (lo < T && stau[lo] < tq) ++lo;
+      if (hiq < lo) hiq = lo;
+      while (hiq < T && stau[hiq] <= tq) ++hiq;
+      if (hiq > lo) cur = hiq - 1;
+      if (lo >= 1) {
+        const int p = lastf[lo - 1];
+        if (p >= 0 && p >= lo - K) prev = p;
+      }
+      if (hiq < T) {
+        const int n = nextf[hiq];
+        if (n < T && n <= hiq + K - 1) next = n;
+      }
+    }
+    const float tp = prev >= 0 ? stau[prev] : 0.f;
+    const float tn = next >= 0 ? stau[next] : 0.f;
+    out[j] = Nbr{prev, next, cur, weight_ref(tq, tp, tn)};
+  }
+}
+
+// Kernel 3: CTA = (32 features, b); warp w owns states [w*NPT, (w+1)*NPT) of every
+// feature (lane = feature).  Queries go in blocks of QB:
+//   * the block's neighbour-table entries arrive by cp.async two blocks ahead;
+//   * from them the block's contiguous range of observation rows is known, and
+//     those rows (32 features each) are copied by cp.async into a shared-memory
+//     tile one block ahead, so interpolation reads only shared memory (a block
+//     whose range exceeds the tile gathers from global memory instead);
+//   * (A) interpolated inputs -> vh, (B) the rescaled recurrence g <- Abar*g + v
+//     with the readout partial sum_n (C*Bbar)[n] g[n] (two states per packed
+//     instruction), (C) partials summed across warps, + D*v, stored.
+// h = Bbar*g, so the final state is Bbar*g.
+constexpr int QB = 64;
+constexpr int RMAX = 96;   // observation rows per staged tile
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int NPT>
+__global__ void __launch_bounds__(128) interp_ssm_scan_kernel(
+    const float* __restrict__ Vp, const Nbr* __restrict__ tab, const float* __restrict__ A_log,
+    const float* __restrict__ Bp, const float* __restrict__ Cp, const float* __restrict__ Dskip,
+    const float* __restrict__ dt, float* __restrict__ y, float* __restrict__ h_last, float* __restrict__ vhat_out,
+    int T, int Dm, int N, int Lq, int FTILE, int ntiles) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  float (*vt)[RMAX][32] = reinterpret_cast<float (*)[RMAX][32]>(dsm);                 // [2][RMAX][32]
+  Nbr (*nb)[QB] = reinterpret_cast<Nbr (*)[QB]>(dsm + 2 * RMAX * 32 * 4);              // [3][QB]
+  float (*vh)[33] = reinterpret_cast<float (*)[33]>(dsm + 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr));
+  float (*yp)[QB][33] = reinterpret_cast<float (*)[QB][33]>(reinterpret_cast<uint8_t*>(vh) + QB * 33 * 4);
+  __shared__ int s_rlo[2], s_direct[2];   // per staged block: first row, row count (-1: gather directly)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
+  const int d0 = blockIdx.x * 32, b = blockIdx.y;
+  const int d = d0 + lane;
+  const bool dvalid = d < Dm;
+  // one tile per CTA when the 32 features lie in one tile (the staged path); otherwise direct gathers
+  const int tile0 = d0 / FTILE;
+  const bool one_tile = (min(Dm, d0 + 32) - 1) / FTILE == tile0;
+  const bool vec_rows = one_tile && (Dm % 4 == 0) && (d0 + 32 <= Dm);
+  const Nbr* tb = tab + ((int64_t)b * ntiles + (dvalid ? d : d0) / FTILE) * Lq;
+  const Nbr* tb0 = tab + ((int64_t)b * ntiles + tile0) * Lq;
+  const float* Vb = Vp + (int64_t)b * T * Dm;
+  const float dtb = dt[b];
+  static_assert(NPT % 2 == 0, "states per thread come in pairs");
+  constexpr int NP2 = NPT / 2;
+  float2 a2[NP2], c2[NP2], g2[NP2], b2[NP2];
+#pragma unroll
+  for (int k = 0; k < NPT; ++k) {
+    const int n = warp * NPT + k;
+    float ab = 0.f, bb = 0.f, cb = 0.f;
+    if (dvalid && n < N) {
+      const float a = -expf(A_log[(int64_t)d * N + n]);
+      const float x = dtb * a;
+      const float e = expf(x);
+      ab = e;
+      bb = zoh_coeff(x, e, a) * Bp[(int64_t)d * N + n];
+      cb = Cp[(int64_t)d * N + n] * bb;
+    }
+    if (k & 1) { a2[k / 2].y = ab; b2[k / 2].y = bb; c2[k / 2].y = cb; }
+    else { a2[k / 2].x = ab; b2[k / 2].x = bb; c2[k / 2].x = cb; }
+  }
+#pragma unroll
+  for (int k = 0; k < NP2; ++k) g2[k] = make_float2(0.f, 0.f);
+  const float dsk = (Dskip && dvalid) ? Dskip[d] : 0.f;
+  const int nblk = (Lq + QB - 1) / QB;
+
+  // table entries of block `blk` -> nb[blk % 3] (one 16-byte copy per query)
+  auto issue_table = [&](int blk) {
+    if (blk < nblk) {
+      const int qs = blk * QB, nq = min(QB, Lq - qs);
+      if (tid < nq) cp_async16(&nb[blk % 3][tid], tb0 + qs + tid);
+    }
+    cp_async_commit();
+  };
+  // row range of block `blk` (its table must be resident) and, when it fits,
+  // the copies of those rows into vt[blk & 1]; one committed group either way
+  auto issue_rows = [&](int blk) {
+    if (blk < nblk && vec_rows) {
+      const int qs = blk * QB, nq = min(QB, Lq - qs);
+      const Nbr* e = nb[blk % 3];
+      // warp 0 reduces the range; broadcast through shared memory
+      if (warp == 0) {
+        int lo = 1 << 30, hi = -1;
+        for (int i = lane; i < nq; i += 32) {
+          const Nbr x = e[i];
+          if (x.prev >= 0) { lo = min(lo, x.prev); hi = max(hi, x.prev); }
+          if (x.next >= 0) { lo = min(lo, x.next); hi = max(hi, x.next); }
+          if (x.cur >= 0) { lo = min(lo, x.cur); hi = max(hi, x.cur); }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+          hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        }
+        if (lane == 0) {
+          // rows to stage (0: none needed; -1: range too wide, gather directly)
+          s_rlo[blk & 1] = hi >= lo ? lo : 0;
+          s_direct[blk & 1] = hi >= lo ? (hi - lo + 1 > RMAX ? -1 : hi - lo + 1) : 0;
+        }
+      }
+      __syncwarp();
+    }
+  };
+  auto copy_rows = [&](int blk) {
+    if (blk < nblk && vec_rows) {
+      const int nrows = s_direct[blk & 1];
+      const int lo = s_rlo[blk & 1];
+      for (int c = tid; c < nrows * 8; c += 128) {
+        const int r = c >> 3, part = c & 7;
+        cp_async16(&vt[blk & 1][r][part * 4], Vb + (int64_t)(lo + r) * Dm + d0 + part * 4);
+      }
+    }
+    cp_async_commit();
+  };
+
+  issue_table(0);
+  issue_table(1);
+  cp_async_wait<1>();          // table of block 0 landed
+  __syncthreads();
+  issue_rows(0);
+  __syncthreads();
+  copy_rows(0);
+  for (int blk = 0; blk < nblk; ++blk) {
+    const int q0 = blk * QB, nq = min(QB, Lq - q0);
+    // groups in flight: table(blk+1), rows(blk) -> wait for both
+    cp_async_wait<0>();
+    __syncthreads();
+    // next block's range (its table is resident now), then the next table + rows go out
+    issue_rows(blk + 1);
+    IT_TRACE(blk, 0);
+    // (A) interpolated inputs of this block
+    {
+      const Nbr* e = nb[blk % 3];
+      const int nrows = vec_rows ? s_direct[blk & 1] : -1;
+      const int lo = vec_rows ? s_rlo[blk & 1] : 0;
+      for (int i = warp; i < nq; i += 4) {
+        const Nbr x = e[i];
+        float v = 0.f;
+        if (dvalid) {
+          if (nrows >= 0) {
+            const float* row = &vt[blk & 1][0][lane];
+            if (x.prev >= 0 && x.next >= 0) v = lerp_ref(x.w, row[(x.prev - lo) * 32], row[(x.next - lo) * 32]);
+            else if (x.prev >= 0) v = row[(x.prev - lo) * 32];
+            else if (x.next >= 0) v = row[(x.next - lo) * 32];
+            else if (x.cur >= 0) v = row[(x.cur - lo) * 32];
+          } else {
+            const Nbr xx = tb[q0 + i];   // this lane's own tile
+            if (xx.prev >= 0 && xx.next >= 0)
+              v = lerp_ref(xx.w, Vb[(int64_t)xx.prev * Dm + d], Vb[(int64_t)xx.next * Dm + d]);
+            else if (xx.prev >= 0) v = Vb[(int64_t)xx.prev * Dm + d];
+            else if (xx.next >= 0) v = Vb[(int64_t)xx.next * Dm + d];
+            else if (xx.cur >= 0) v = Vb[(int64_t)xx.cur * Dm + d];
+          }
+        }
+        vh[i][lane] = v;
+      }
+    }
+    __syncthreads();   // vh ready; vt[blk & 1] and nb[blk % 3] free after this point
+    issue_table(blk + 2);
+    copy_rows(blk + 1);
+    IT_TRACE(blk, 1);
+    IT_TRACE(blk, 2);
+    // (B) recurrence, packed two states per instruction, 8 queries per step
+    {
+      auto one = [&](float v, int i) {
+        const float2 v2 = make_float2(v, v);
+        float2 acc;
+#pragma unroll
+        for (int k = 0; k < NP2; ++k) {
+          g2[k] = ffma2(a2[k], g2[k], v2);
+          acc = k == 0 ? fmul2(c2[k], g2[k]) : ffma2(c2[k], g2[k], acc);
+        }
+        yp[warp][i][lane] = acc.x + acc.y;
+      };
+      int i0 = 0;
+      for (; i0 + 8 <= nq; i0 += 8) {
+        float vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) vv[u] = vh[i0 + u][lane];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) one(vv[u], i0 + u);
+      }
+      for (; i0 < nq; ++i0) one(vh[i0][lane], i0);
+    }
+    IT_TRACE(blk, 3);
+    __syncthreads();
+    IT_TRACE(blk, 4);
+    // (C) readout
+    if (dvalid) {
+      float* yrow = y + ((int64_t)b * Lq + q0) * Dm + d;
+      float* vrow = vhat_out ? vhat_out + ((int64_t)b * Lq + q0) * Dm + d : nullptr;
+      for (int i = warp; i < nq; i += 4) {
+        const float v = vh[i][lane];
+        yrow[(int64_t)i * Dm] = (yp[0][i][lane] + yp[1][i][lane]) + (yp[2][i][lane] + yp[3][i][lane]) + dsk * v;
+        if (vrow) vrow[(int64_t)i * Dm] = v;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (h_last && dvalid) {
+#pragma unroll
+    for (int k = 0; k < NPT; ++k) {
+      const int n = warp * NPT + k;
+      const float gk = (k & 1) ? g2[k / 2].y : g2[k / 2].x;
+      const float bk = (k & 1) ? b2[k / 2].y : b2[k / 2].x;
+      if (n < N) h_last[((int64_t)b * Dm + d) * N + n] = bk * gk;
+    }
+  }
+}
+
+constexpr size_t kScanSmem = 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr) + QB * 33 * 4 + 4 * QB * 33 * 4;
+
+size_t ws_flags_bytes(int64_t Bsz, int64_t T, int64_t ntiles) { return (size_t)((Bsz * ntiles * T + 255) / 256 * 256); }
+size_t ws_table_bytes(int64_t Bsz, int64_t Lq, int64_t ntiles) { return (size_t)(Bsz * ntiles * Lq * sizeof(Nbr)); }
+
+}  // namespace
+}  // namespace tssm
+
+using namespace tssm;
+
+extern "C" int tssm_time_aware_interp(const void* V, const void* Mk, const void* tau, void* Vhat, int64_t Bsz,
+                                      int64_t T, int64_t F, int64_t stride_vb, int64_t stride_vt,
+                                      int64_t stride_mb, int64_t stride_mt, int64_t stride_tb,
+                                      int64_t stride_ob, int64_t stride_ot, int64_t K, int64_t FTILE,
+                                      int v_dtype, int m_dtype, tssm_stream_t stream) {
+  TSSM_REQUIRE(Bsz >= 0 && T >= 0 && F >= 0, "time_aware_interp: negative size");
+  if (Bsz * T * F == 0) return TSSM_OK;
+  TSSM_REQUIRE(V && Mk && tau && Vhat, "time_aware_interp: null pointer");
+  TSSM_REQUIRE(K >= 1 && K <= 64 && FTILE >= 1 && FTILE <= 4096, "time_aware_interp: K in [1,64], FTILE in [1,4096]");
+  TSSM_REQUIRE(Bsz <= 65535 && T < (1 << 30) && F < (1 << 30), "time_aware_interp: size out of range");
+  const int ntiles = (int)cdiv(F, FTILE);
+  dim3 grid((unsigned)ntiles, (unsigned)Bsz, (unsigned)cdiv(T, TB));
+  const size_t shm = (size_t)(TB + 2 * K);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define INTERP_LAUNCH(VT, MT)                                                                                   \
+  time_aware_interp_kernel<VT, MT><<<grid, 128, shm, st>>>(                                                     \
+      (const VT*)V, (const MT*)Mk, (const float*)tau, (VT*)Vhat, (int)T, (int)F, stride_vb, stride_vt, stride_mb, \
+      stride_mt, stride_tb, stride_ob, stride_ot, (int)K, (int)FTILE)
+  const bool mu8 = m_dtype == TSSM_U8;
+  TSSM_REQUIRE(mu8 || m_dtype == TSSM_F32, "time_aware_interp: mask dtype must be u8 or f32");
+  if (v_dtype == TSSM_F32) {
+    if (mu8) INTERP_LAUNCH(float, uint8_t); else INTERP_LAUNCH(float, float);
+  } else if (v_dtype == TSSM_BF16) {
+    if (mu8) INTERP_LAUNCH(__nv_bfloat16, uint8_t); else INTERP_LAUNCH(__nv_bfloat16, float);
+  } else if (v_dtype == TSSM_F16) {
+    if (mu8) INTERP_LAUNCH(__half, uint8_t); else INTERP_LAUNCH(__half, float);
+  } else {
+    set_error("time_aware_interp: value dtype must be f32, bf16 or f16");
+    return TSSM_ERR_INVALID;
+  }
+#undef INTERP_LAUNCH
+  return check_launch("time_aware_interp");
+}
+
+extern "C" int tssm_interp_ssm_step(const void* V, const void* Mk, const void* tau, const void* Abar,
+                                    const void* Bbar, const void* h_in, void* Vhat, void* h_out, int64_t Bsz,
+                                    int64_t T, int64_t F, int64_t stride_vb, int64_t stride_vt, int64_t stride_mb,
+                                    int64_t stride_mt, int64_t stride_tb, int64_t stride_ob, int64_t stride_ot,
+                                    int64_t stride_hib, int64_t stride_hob, int64_t t_cur, int64_t K,
+                                    int64_t FTILE, int m_dtype, tssm_stream_t stream) {
+  TSSM_REQUIRE(Bsz >= 0 && T >= 0 && F >= 0, "interp_ssm_step: negative size");
+  if (Bsz * F == 0) return TSSM_OK;
+  TSSM_REQUIRE(V && Mk && tau && Abar && Bbar && h_in && h_out, "interp_ssm_step: null pointer");
+  TSSM_REQUIRE(t_cur >= 0 && t_cur < T, "interp_ssm_step: t_cur out of range");
+  TSSM_REQUIRE(K >= 1 && K <= 64 && FTILE >= 1 && FTILE <= 4096, "interp_ssm_step: K in [1,64], FTILE in [1,4096]");
+  dim3 grid((unsigned)cdiv(F, FTILE), (unsigned)Bsz);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (m_dtype == TSSM_U8)
+    interp_step_kernel<uint8_t><<<grid, 128, 0, st>>>(
+        (const float*)V, (const uint8_t*)Mk, (const float*)tau, (const float*)Abar, (const float*)Bbar,
+        (const float*)h_in, (float*)Vhat, (float*)h_out, (int)T, (int)F, stride_vb, stride_vt, stride_mb, stride_mt,
+        stride_tb, stride_ob, stride_ot, stride_hib, stride_hob, (int)t_cur, (int)K, (int)FTILE);
+  else if (m_dtype == TSSM_F32)
+    interp_step_kernel<float><<<grid, 128, 0, st>>>(
+        (const float*)V, (const float*)Mk, (const float*)tau, (const float*)Abar, (const float*)Bbar,
+        (const float*)h_in, (float*)Vhat, (float*)h_out, (int)T, (int)F, stride_vb, stride_vt, stride_mb, stride_mt,
+        stride_tb, stride_ob, stride_ot, stride_hib, stride_hob, (int)t_cur, (int)K, (int)FTILE);
+  else {
+    set_error("interp_ssm_step: mask dtype must be u8 or f32");
+    return TSSM_ERR_INVALID;
+  }
+  return check_launch("interp_ssm_step");
+}
+
+extern "C" int64_t tssm_interp_ssm_workspace_size(int64_t Bsz, int64_t T, int64_t Dm, int64_t Lq, int64_t FTILE) {
+  if (Bsz <= 0 || T <= 0 || Dm <= 0 || Lq <= 0 || FTILE <= 0) return 0;
+  const int64_t nt = cdiv(Dm, FTILE);
+  return (int64_t)(ws_flags_bytes(Bsz, T, nt) + ws_table_bytes(Bsz, Lq, nt));
+}
+
+extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, const void* q, const void* A_log,
+                               const void* B, const void* C, const void* Dskip, const void* dt, void* y,
+                               void* h_last, void* vhat, void* workspace, int64_t workspace_bytes, int64_t Bsz,
+                               int64_t T, int64_t Dm, int64_t N, int64_t Lq, int64_t K, int64_t FTILE, int m_dtype,
+                               tssm_stream_t stream) {
+  TSSM_REQUIRE(Bsz >= 0 && T >= 0 && Dm >= 0 && N >= 1 && Lq >= 0, "interp_ssm: bad size");
+  if (Bsz * Dm * Lq == 0) return TSSM_OK;
+  TSSM_REQUIRE(T >= 1, "interp_ssm: at least one observation is required");
+  TSSM_REQUIRE(V && Mk && tau && A_log && B && C && dt && y, "interp_ssm: null pointer");
+  TSSM_REQUIRE(q || Lq == T, "interp_ssm: index mode (q == NULL) needs Lq == T");
+  TSSM_REQUIRE(N <= 64, "interp_ssm: N=%lld > 64 is not supported", (long long)N);
+  TSSM_REQUIRE(K >= 1 && K <= 4096 && FTILE >= 1, "interp_ssm: bad K or FTILE");
+  TSSM_REQUIRE(T <= 8192, "interp_ssm: T=%lld exceeds 8192 observations per row", (long long)T);
+  TSSM_REQUIRE(Bsz <= 65535 && Lq < (1 << 30) && Dm < (1 << 30), "interp_ssm: size out of range");
+  const int64_t need = tssm_interp_ssm_workspace_size(Bsz, T, Dm, Lq, FTILE);
+  TSSM_REQUIRE(workspace && workspace_bytes >= need, "interp_ssm: workspace of %lld bytes needed",
+               (long long)need);
+  TSSM_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "interp_ssm: workspace must be 256-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int ntiles = (int)cdiv(Dm, FTILE);
+  uint8_t* flags = static_cast<uint8_t*>(workspace);
+  Nbr* tab = reinterpret_cast<Nbr*>(flags + ws_flags_bytes(Bsz, T, ntiles));
+  {
+    const int64_t rows = T * ntiles;   // one warp per (t, tile) row, 8 warps per block
+    dim3 grid((unsigned)std::max<int64_t>(1, cdiv(rows, 8)), (unsigned)Bsz);
+    const bool vec = m_dtype == TSSM_U8 && Dm % 16 == 0 && FTILE % 16 == 0 && FTILE / 16 <= 32 &&
+                     ((FTILE / 16) & (FTILE / 16 - 1)) == 0 && (reinterpret_cast<uintptr_t>(Mk) & 15) == 0;
+    if (vec) {
+      const int64_t nwords = Bsz * T * Dm / 16;
+      interp_flags_u8x16_kernel<<<(unsigned)cdiv(nwords, 256), 256, 0, st>>>(
+          (const uint4*)Mk, flags, nwords, (int)T, (int)(Dm / 16), (int)(FTILE / 16), ntiles);
+    } else if (m_dtype == TSSM_U8)
+      interp_flags_kernel<uint8_t><<<grid, 256, 0, st>>>((const uint8_t*)Mk, flags, (int)T, (int)Dm, (int)FTILE, ntiles);
+    else if (m_dtype == TSSM_F32)
+      interp_flags_kernel<float><<<grid, 256, 0, st>>>((const float*)Mk, flags, (int)T, (int)Dm, (int)FTILE, ntiles);
+    else {
+      set_error("interp_ssm: mask dtype must be u8 or f32");
+      return TSSM_ERR_INVALID;
+    }
+  }
+  {
+    const size_t shm = (size_t)T * 12;
+    if (shm > 48 * 1024 &&
+        cudaFuncSetAttribute(interp_neighbors_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm) != cudaSuccess)
+      return check_launch("interp_ssm: neighbour smem");
+    const int qsplit = (int)std::max<int64_t>(1, std::min<int64_t>(8, cdiv(Lq, 512)));
+    interp_neighbors_kernel<<<dim3((unsigned)ntiles, (unsigned)Bsz, (unsigned)qsplit), NB_THREADS, shm, st>>>(
+        flags, (const float*)tau, (const float*)q, tab, (int)T, (int)Lq, (int)K, ntiles);
+  }
+  dim3 grid((unsigned)cdiv(Dm, 32), (unsigned)Bsz);
+  const int npt = (int)cdiv(N, 4);
+  const float* Vf = (const float*)V;
+  const float* al = (const float*)A_log;
+  const float* bp = (const float*)B;
+  const float* cp = (const float*)C;
+  const float* dk = (const float*)Dskip;
+  const float* dtp = (const float*)dt;
+#define SCAN_LAUNCH(NP)                                                                                    \
+  do {                                                                                                     \
+    if (cudaFuncSetAttribute(interp_ssm_scan_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                             (int)kScanSmem) != cudaSuccess)                                               \
+      return check_launch("interp_ssm: scan smem");                                                        \
+    interp_ssm_scan_kernel<NP><<<grid, 128, kScanSmem, st>>>(Vf, tab, al, bp, cp, dk, dtp, (float*)y,      \
+                                                             (float*)h_last, (float*)vhat, (int)T, (int)Dm, \
+                                                             (int)N, (int)Lq, (int)FTILE, ntiles);          \
+  } while (0)
+  if (npt <= 2) SCAN_LAUNCH(2);
+  else if (npt <= 4) SCAN_LAUNCH(4);
+  else if (npt <= 8) SCAN_LAUNCH(8);
+  else SCAN_LAUNCH(16);
+#undef SCAN_LAUNCH
+  return check_launch("interp_ssm");
+}
+
+#ifdef TSSM_INTERP_TRACE
+extern "C" int tssm_debug_read_interp_trace(unsigned long long* out, int n) {
+  return cudaMemcpyFromSymbol(out, tssm::g_interp_trace, sizeof(unsigned long long) * (n < 1024 ? n : 1024)) ==
+                 cudaSuccess ? 0 : 3;
+}
+#endif

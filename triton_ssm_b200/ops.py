@@ -12,7 +12,8 @@ from . import _lib
 from ._lib import call, dtype_code, ptr, stream_of
 
 __all__ = ["zoh_discretize", "ssm_forward", "selective_scan", "streaming_ssm_inplace",
-           "streaming_step", "multihead_ssm", "check_device_status"]
+           "streaming_step", "multihead_ssm", "check_device_status", "fused_time_aware_interp",
+           "fused_interp_ssm_step", "fused_interp_ssm", "linspace_queries", "interp_ssm_workspace_bytes"]
 
 
 def _cuda(*ts):
@@ -220,3 +221,132 @@ def check_device_status(device=None):
     s = torch.cuda.current_stream(dev)
     import ctypes
     call("tssm_check_device_status", ctypes.c_void_p(s.cuda_stream))
+
+
+def _mask_code(M):
+    if M.dtype in (torch.uint8, torch.bool):
+        return _lib.U8
+    if M.dtype == torch.float32:
+        return _lib.F32
+    raise ValueError("mask dtype must be uint8, bool or float32 (got %s)" % M.dtype)
+
+
+def _mask(M):
+    return M.view(torch.uint8) if M.dtype == torch.bool else M
+
+
+def fused_time_aware_interp(V, M, tau, K=10, FTILE=128, out=None):
+    """Time-aware interpolation (``fused_interp_kernel.py:9-257``).
+
+    V [Bt,T,F] f32/bf16/f16; M [Bt,T,F] uint8/bool/f32 (observed where > 0.5);
+    tau [Bt,T] f32.  Returns Vhat in V's dtype.
+    """
+    _cuda(V, M, tau)
+    _need(V, (torch.float32, torch.bfloat16, torch.float16), "V")
+    if V.dim() != 3 or M.shape != V.shape or tuple(tau.shape) != tuple(V.shape[:2]):
+        raise ValueError("fused_time_aware_interp: expected V, M [Bt,T,F] and tau [Bt,T]")
+    M = _mask(M)
+    tau = tau.float()
+    for t, n in ((V, "V"), (M, "M"), (tau, "tau")):
+        _lastdim(t, n)
+    out = torch.empty_like(V) if out is None else out
+    Bt, T, F = V.shape
+    call("tssm_time_aware_interp", ptr(V), ptr(M), ptr(tau), ptr(out), Bt, T, F, V.stride(0), V.stride(1),
+         M.stride(0), M.stride(1), tau.stride(0), out.stride(0), out.stride(1), int(K), int(FTILE),
+         dtype_code(V), _mask_code(M), stream_of(V))
+    return out
+
+
+def fused_interp_ssm_step(V, M, tau, A_bar, B_bar, h_in, Vhat=None, h_out=None, t_cur=0, K=10, FTILE=128):
+    """Interpolation at ``t_cur`` fused with one SSM step
+    (``fused_ssm_interp.py:11-101``): writes Vhat[:, t_cur] (when given) and
+    returns h_out = A_bar*h_in + B_bar*vhat.  All f32 except the mask."""
+    _cuda(V, M, tau, A_bar, B_bar, h_in, Vhat, h_out)
+    for t, n in ((V, "V"), (tau, "tau"), (A_bar, "A_bar"), (B_bar, "B_bar"), (h_in, "h_in")):
+        _need(t, (torch.float32,), n)
+    Bt, T, F = V.shape
+    if M.shape != V.shape or tuple(h_in.shape) != (Bt, F) or tuple(A_bar.shape) != (F,) or \
+            tuple(B_bar.shape) != (F,):
+        raise ValueError("fused_interp_ssm_step: shape mismatch")
+    M = _mask(M)
+    A_bar, B_bar = A_bar.contiguous(), B_bar.contiguous()
+    h_out = torch.empty_like(h_in) if h_out is None else h_out
+    so = (Vhat.stride(0), Vhat.stride(1)) if Vhat is not None else (0, 0)
+    call("tssm_interp_ssm_step", ptr(V), ptr(M), ptr(tau), ptr(A_bar), ptr(B_bar), ptr(h_in), ptr(Vhat),
+         ptr(h_out), Bt, T, F, V.stride(0), V.stride(1), M.stride(0), M.stride(1), tau.stride(0), so[0], so[1],
+         h_in.stride(0), h_out.stride(0), int(t_cur), int(K), int(FTILE), _mask_code(M), stream_of(V))
+    return h_out
+
+
+def linspace_queries(tau, L_q):
+    """Regular query grid per batch row over [tau[:,0], tau[:,-1]], end points exact."""
+    t0 = tau[:, :1].float()
+    t1 = tau[:, -1:].float()
+    step = (t1 - t0) / max(1, L_q - 1)
+    q = t0 + torch.arange(L_q, device=tau.device, dtype=torch.float32)[None, :] * step
+    q[:, -1:] = t1
+    return q.contiguous()
+
+
+def interp_ssm_workspace_bytes(Bt, T, D, L_q, FTILE=128):
+    _lib.load_library()
+    return int(_lib.load_library().tssm_interp_ssm_workspace_size(Bt, T, D, L_q, FTILE))
+
+
+def fused_interp_ssm(V, M, tau, A_log, B, C, L_q=None, q=None, dt=None, D=None, K=10, FTILE=128,
+                     return_state=False, return_vhat=False, workspace=None):
+    """Interpolation of irregular observations onto query times fused with an
+    N-state diagonal scan (config 3): the composition of
+    ``fused_time_aware_interp_kernel`` and the step of
+    ``fused_interp_ssm_step_kernel`` at every query, in one pass.
+
+    V [Bt,T,D] f32; M [Bt,T,D] uint8/bool/f32; tau [Bt,T] f32 (sorted);
+    A_log, B, C [D,N] f32; D [D] f32 or None.
+    Queries: ``q`` [Bt,L_q] sorted times; or ``L_q`` for a regular grid over
+    each row's [tau_0, tau_last]; or neither for index mode (the queries are the
+    observations, the reference's own semantics).
+    dt [Bt] f32: discretisation step per row; defaults to the regular query spacing.
+    Returns y [Bt,L_q,D] f32 (+ h_last [Bt,D,N], + vhat [Bt,L_q,D]).
+    """
+    _cuda(V, M, tau, A_log, B, C, q, dt, D)
+    _need(V, (torch.float32,), "V")
+    Bt, T, Dm = V.shape
+    N = A_log.shape[-1]
+    if M.shape != V.shape or tuple(tau.shape) != (Bt, T) or tuple(A_log.shape) != (Dm, N) or \
+            tuple(B.shape) != (Dm, N) or tuple(C.shape) != (Dm, N) or (D is not None and tuple(D.shape) != (Dm,)):
+        raise ValueError("fused_interp_ssm: shape mismatch")
+    if q is None and L_q is not None:
+        q = linspace_queries(tau, int(L_q))
+    if q is not None:
+        q = q.float().contiguous()
+        if q.dim() != 2 or q.shape[0] != Bt:
+            raise ValueError("fused_interp_ssm: q must be [Bt,L_q]")
+        Lq = q.shape[1]
+    else:
+        Lq = T
+    if dt is None:
+        if q is None:
+            raise ValueError("fused_interp_ssm: index mode needs an explicit dt [Bt]")
+        dt = ((tau[:, -1] - tau[:, 0]).float() / max(1, Lq - 1)).contiguous()
+    if tuple(dt.shape) != (Bt,):
+        raise ValueError("fused_interp_ssm: dt must be [Bt]")
+    M = _mask(M).contiguous()
+    V, tau = V.contiguous(), tau.float().contiguous()
+    A_log, B, C = (t.float().contiguous() for t in (A_log, B, C))
+    D = D.float().contiguous() if D is not None else None
+    dt = dt.float().contiguous()
+    need = int(_lib.load_library().tssm_interp_ssm_workspace_size(Bt, T, Dm, Lq, int(FTILE)))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=V.device)
+    y = torch.empty(Bt, Lq, Dm, device=V.device, dtype=torch.float32)
+    hl = torch.empty(Bt, Dm, N, device=V.device, dtype=torch.float32) if return_state else None
+    vh = torch.empty(Bt, Lq, Dm, device=V.device, dtype=torch.float32) if return_vhat else None
+    call("tssm_interp_ssm", ptr(V), ptr(M), ptr(tau), ptr(q), ptr(A_log), ptr(B), ptr(C), ptr(D), ptr(dt),
+         ptr(y), ptr(hl), ptr(vh), ptr(workspace), workspace.numel(), Bt, T, Dm, N, Lq, int(K), int(FTILE),
+         _mask_code(M), stream_of(V))
+    out = [y]
+    if return_state:
+        out.append(hl)
+    if return_vhat:
+        out.append(vh)
+    return out[0] if len(out) == 1 else tuple(out)
