@@ -363,6 +363,38 @@ def run_ours_c1(args, rank, world, local):
                  launches=launches)
 
 
+def run_ours_c4(args, rank, world, local):
+    """Config 4: B4 H32 P64 N128 L=1,048,576 bf16, sequence sharded over the ranks
+    (strong scaling): local scan from a zero state, one all-gather of
+    (state, decay) per rank, carry fix-up."""
+    import triton_ssm_b200 as ts
+    from triton_ssm_b200 import parallel, workloads
+    dev = torch.device("cuda", local)
+    c = workloads.C4
+    Bt, H, P, N = c["Bt"], c["H"], c["P"], c["N"]
+    L = args.seq_len or c["L"]
+    a, b = parallel.shard_range(L // (1 << 14), rank, world)
+    L0, Ls = a * (1 << 14), (b - a) * (1 << 14)
+    inp = workloads.ssd_inputs_slice(Bt, L0, Ls, H, P, N, dev, seed=4)
+    y = torch.empty_like(inp["x"])
+    group = None
+    step = lambda: parallel.ssd_sequence_parallel(inp["x"], inp["dt"], inp["A_log"], inp["B"], inp["C"], inp["D"],
+                                                  group=group, y=y)
+    t_step, clocks = _timed(args, world, dev, step)
+    upd = Bt * L * H * P * N
+    alg = workloads.ssd_bytes(Bt, L, H, P, N)
+    cfg = {"workload": "config4: sequence-parallel multi-head scan B%d H%d P%d N%d L=%d bf16, A_h=-(1+h%%16), "
+                       "L sharded over %d rank(s) with one all-gather of slice carries" % (Bt, H, P, N, L, world),
+           "global_batch": Bt, "seq_len": L, "parallelism": "sequence (L) x %d" % world,
+           "nvlink_bytes_per_rank": Bt * H * P * N * 4 + Bt * H * 4}
+    out = _line(args, world, METRIC, upd / t_step, t_step, "bf16", cfg, alg // world,
+                "ssd_chunk_scan_kernel<128,false> + ssd_carry_fixup_kernel<128>", None, clocks,
+                launches=(2 if world > 1 else 1) * args.steps)
+    out["scaling"] = "strong"
+    out["roofline"]["note"] = "algorithmic bytes per rank (1/world of the whole sequence)"
+    return out
+
+
 def run_ours_c2(args, rank, world, local):
     import triton_ssm_b200 as ts
     from triton_ssm_b200 import workloads
@@ -436,10 +468,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s pre-timing load")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c5"], default="c2",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c2",
                     help="workload (default c2, the headline; the others are for measurement notes)")
     ap.add_argument("--c1-mode", choices=["pair", "fused"], default="pair")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays of the step")
+    ap.add_argument("--seq-len", type=int, default=None, help="config 4: override L (multiple of 16384)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_env()
@@ -457,7 +490,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     try:
-        runner = {"c1": run_ours_c1, "c2": run_ours_c2, "c3": run_ours_c3, "c5": run_ours_c5}[args.config]
+        runner = {"c1": run_ours_c1, "c2": run_ours_c2, "c3": run_ours_c3, "c4": run_ours_c4,
+                  "c5": run_ours_c5}[args.config]
         out = runner(args, rank, world, local)
         if rank == 0:
             print(json.dumps(out), flush=True)

@@ -130,15 +130,91 @@ int tssm_streaming_step(const void* x, const void* dt, void* h, const void* A_lo
  *            expm1*(dt_t*a)/(a+1e-12) (bdisc 1, ZOH, discretize_kernel.py:50-54), a = -exp(A_log[h]).
  *   x [Bsz,L,H*P] bf16; dt [Bsz,L,H] f32; A_log [H] f32; B, C [Bsz,L,H,N] bf16;
  *   Dskip [H*P] f32; y [Bsz,L,H*P] bf16; h0 [Bsz,H,P,N] f32 or NULL (zero
- *   initial state); h_last [Bsz,H,P,N] f32 or NULL.
+ *   initial state); h_last [Bsz,H,P,N] f32 or NULL; decay_log2 [Bsz,H] f32 or
+ *   NULL: log2 of the whole-sequence decay, sum_t dt_t*A_h*log2(e) (used to
+ *   chain sequence slices, see tssm_ssd_carry_fixup).
  * P = 64 and N in {64, 128}; all tensors contiguous; x, B, C, y 16-byte
  * aligned.  Device-side waits are bounded: a wait that gives up is reported
  * by tssm_check_device_status.
  */
 int tssm_multihead_ssd(const void* x, const void* dt, const void* A_log, const void* B,
                        const void* C, const void* Dskip, void* y, const void* h0, void* h_last,
-                       int64_t Bsz, int64_t L, int64_t H, int64_t P, int64_t N, int bdisc,
-                       tssm_stream_t stream);
+                       void* decay_log2, int64_t Bsz, int64_t L, int64_t H, int64_t P, int64_t N,
+                       int bdisc, tssm_stream_t stream);
+
+/*
+ * Time-aware interpolation of irregular observations.  Replaces
+ * fused_time_aware_interp_kernel (fused_interp_kernel.py:9-100) for v_dtype
+ * TSSM_F32, fused_interp_bf16_kernel (:103-181) for TSSM_BF16 and
+ * fused_interp_fp16_kernel (:186-257) for TSSM_F16, with the same
+ * neighbour search (per tile of FTILE features, K candidates each way), weights
+ * and priority.
+ *   V, Vhat [Bsz,T,F] (v_dtype); M [Bsz,T,F] (m_dtype TSSM_U8 or TSSM_F32,
+ *   observed where the value is > 0.5); tau [Bsz,T] f32 (t contiguous).
+ *   K in [1,64]; FTILE in [1,4096].
+ */
+int tssm_time_aware_interp(const void* V, const void* M, const void* tau, void* Vhat, int64_t Bsz,
+                           int64_t T, int64_t F, int64_t stride_vb, int64_t stride_vt,
+                           int64_t stride_mb, int64_t stride_mt, int64_t stride_tb,
+                           int64_t stride_ob, int64_t stride_ot, int64_t K, int64_t FTILE,
+                           int v_dtype, int m_dtype, tssm_stream_t stream);
+
+/*
+ * Interpolation at one time index fused with one SSM step.  Replaces
+ * fused_interp_ssm_step_kernel (fused_ssm_interp.py:11-101):
+ *   Vhat[:, t_cur] = interp(...);  h_out = Abar*h_in + Bbar*vhat.
+ *   V, Vhat [Bsz,T,F] f32 (Vhat may be NULL); M [Bsz,T,F] (m_dtype);
+ *   tau [Bsz,T] f32; Abar, Bbar [F] f32; h_in, h_out [Bsz,F] f32.
+ */
+int tssm_interp_ssm_step(const void* V, const void* M, const void* tau, const void* Abar,
+                         const void* Bbar, const void* h_in, void* Vhat, void* h_out, int64_t Bsz,
+                         int64_t T, int64_t F, int64_t stride_vb, int64_t stride_vt, int64_t stride_mb,
+                         int64_t stride_mt, int64_t stride_tb, int64_t stride_ob, int64_t stride_ot,
+                         int64_t stride_hib, int64_t stride_hob, int64_t t_cur, int64_t K,
+                         int64_t FTILE, int m_dtype, tssm_stream_t stream);
+
+/* Bytes of device workspace tssm_interp_ssm needs (tile flags + neighbour table). */
+int64_t tssm_interp_ssm_workspace_size(int64_t Bsz, int64_t T, int64_t Dm, int64_t Lq, int64_t FTILE);
+
+/*
+ * Interpolation of irregular observations onto query times fused with an
+ * N-state diagonal scan, all queries in one pass: the composition of
+ * fused_time_aware_interp_kernel (fused_interp_kernel.py:9-100) and the step
+ * of fused_interp_ssm_step_kernel (fused_ssm_interp.py:95-101) applied at
+ * every query, with ZOH parameters per (b, d, n) (discretize_kernel.py:38-54)
+ * and the readout y = sum_n C*h (+ D*vhat).  The interpolated values never
+ * round-trip through HBM.
+ *   V [Bsz,T,Dm] f32; M [Bsz,T,Dm] (m_dtype); tau [Bsz,T] f32 sorted;
+ *   q [Bsz,Lq] f32 sorted query times, or NULL for index mode (queries are
+ *   the observations themselves, Lq == T: the reference's own semantics);
+ *   A_log, B, C [Dm,N] f32; Dskip [Dm] f32 or NULL; dt [Bsz] f32 (one
+ *   discretisation step per row, e.g. the query spacing);
+ *   y [Bsz,Lq,Dm] f32; h_last [Bsz,Dm,N] f32 or NULL; vhat [Bsz,Lq,Dm] or NULL.
+ *   workspace: >= tssm_interp_ssm_workspace_size(...) bytes, 256-byte aligned.
+ *   All contiguous.  N <= 64, T <= 8192.
+ */
+int tssm_interp_ssm(const void* V, const void* M, const void* tau, const void* q, const void* A_log,
+                    const void* B, const void* C, const void* Dskip, const void* dt, void* y,
+                    void* h_last, void* vhat, void* workspace, int64_t workspace_bytes, int64_t Bsz,
+                    int64_t T, int64_t Dm, int64_t N, int64_t Lq, int64_t K, int64_t FTILE,
+                    int m_dtype, tssm_stream_t stream);
+
+/*
+ * Sequence-parallel chaining of multi-head scan slices (config 4).  The
+ * block-level carry scan of ssm_scan.py:53-98 (ssm_carry_scan_kernel +
+ * ssm_fwd_apply_kernel) lifted from blocks of one GPU to slices of the sequence
+ * held by different ranks: given every rank's final state S_all [nranks,Bsz,H,P,N]
+ * f32 and whole-slice decay decay_log2_all [nranks,Bsz,H] f32 (both from
+ * tssm_multihead_ssd with a zero initial state, gathered over ranks), rank
+ * `rank` forms carry = sum_{j<rank} (prod_{j<k<rank} 2^d_k) S_j and adds its
+ * effect, exp(A_h*cumdt(t)) * sum_n C[t,n] carry[p,n], to its own outputs
+ * y [Bsz,L,H*P] bf16 (in place), for the leading tokens whose decay is not
+ * exactly zero in f32.  C [Bsz,L,H,N] bf16 and dt [Bsz,L,H] f32 are the
+ * rank's own slice.  P = 64, N in {64, 128}.  No-op on rank 0.
+ */
+int tssm_ssd_carry_fixup(const void* S_all, const void* decay_log2_all, int64_t rank, int64_t nranks,
+                         const void* C, const void* dt, const void* A_log, void* y, int64_t Bsz,
+                         int64_t L, int64_t H, int64_t P, int64_t N, tssm_stream_t stream);
 
 /*
  * Synchronise `stream` and report (then clear) this device's status word:

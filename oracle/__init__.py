@@ -13,7 +13,8 @@ the checker or the timed CPU baseline.  The product path
 """
 from .discretize import zoh_discretize, zoh_discretize_bwd, expm1_ref
 from .scan import ssm_forward, ssm_backward, selective_scan
-from .multihead import ssd_scan, ssd_scan_chunked, multihead_diag, ssd_sharded_compose
+from .multihead import (ssd_scan, ssd_scan_chunked, multihead_diag, ssd_sharded_compose,
+                        ssd_slice_scan, ssd_carry_fixup)
 from .interp import (time_aware_interp, interp_neighbors_index, interp_neighbors_time,
                      interp_gather, interp_ssm_step, interp_ssm, linspace_queries)
 from .streaming import (streaming_ssm_inplace, streaming_step, ring_interp_then_ssm)
@@ -21,7 +22,8 @@ from .streaming import (streaming_ssm_inplace, streaming_step, ring_interp_then_
 __all__ = [
     "zoh_discretize", "zoh_discretize_bwd", "expm1_ref",
     "ssm_forward", "ssm_backward", "selective_scan",
-    "ssd_scan", "ssd_scan_chunked", "multihead_diag", "ssd_sharded_compose",
+    "ssd_scan", "ssd_scan_chunked", "multihead_diag", "ssd_sharded_compose", "ssd_slice_scan",
+    "ssd_carry_fixup",
     "time_aware_interp", "interp_neighbors_index", "interp_neighbors_time",
     "interp_gather", "interp_ssm_step", "interp_ssm", "linspace_queries",
     "streaming_ssm_inplace", "streaming_step", "ring_interp_then_ssm",

@@ -134,3 +134,30 @@ def multihead_diag(u, A_log, B, C, dt, D, bdisc="euler", dtype=torch.float32):
         yh = (C[:, t] * h).sum(-1) + (Dv * us[:, t]).sum(-1)
         y[:, t] = yh[..., None].expand(Bt, nh, hd)
     return y.reshape(Bt, L, nh * hd), h
+
+
+def ssd_slice_scan(x, dt, A_log, B, C, D, bdisc="euler"):
+    """Oracle counterpart of one rank's local pass: (y, final state, log2 of the
+    whole-slice decay) from a zero initial state."""
+    y, S = ssd_scan_chunked(x, dt, A_log, B, C, D, chunk=64, bdisc=bdisc)
+    a = -torch.exp(A_log.float())
+    d = (dt.float().sum(1) * a) * 1.4426950408889634
+    return y, S, d
+
+
+def ssd_carry_fixup(S_all, d_all, rank, C, dt, A_log, y):
+    """Oracle counterpart of the slice chaining (in place on y): carry entering
+    slice `rank` from the gathered (S, d), and its exact effect
+    exp(A*cumdt(t)) * sum_n C[t,n] carry[p,n] on every output of the slice."""
+    if rank == 0:
+        return y
+    carry = torch.zeros_like(S_all[0])
+    for j in range(rank):
+        carry = torch.exp2(d_all[j])[..., None, None] * carry + S_all[j]
+    a = -torch.exp(A_log.float())
+    Bt, L, H, N = C.shape
+    P = y.shape[2] // H
+    cum = torch.cumsum(dt.float() * a, dim=1)                       # [Bt,L,H]
+    fix = torch.einsum("blhn,bhpn->blhp", C.float(), carry) * torch.exp(cum)[..., None]
+    y += fix.reshape(Bt, L, H * P).to(y.dtype)
+    return y

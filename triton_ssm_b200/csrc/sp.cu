@@ -1,0 +1,140 @@
+// Sequence-parallel (L-sharded) multi-head scan: carry combination and
+// fix-up of a shard's outputs (config 4).
+//
+// Rank r scans its slice of the sequence from a zero state (ssd.cu) and
+// publishes its final state S_r [B,H,P,N] and the log2 of its whole-slice
+// decay, d_r = log2(exp(A_h * sum dt)).  After an all-gather, the state
+// entering slice r is the exclusive prefix
+//     carry_r = sum_{j<r} (prod_{j<k<r} 2^d_k) S_j,   i.e.  c <- 2^d_j c + S_j for j < r,
+// the block-level form of the reference's carry scan (ssm_scan.py:53-65,
+// :68-98).  Its effect on the slice's outputs is
+//     y[t, p] += exp(A_h * cumdt(t)) * sum_n C[t, n] carry[p, n],
+// which decays monotonically; the fix-up walks 64-token chunks from the slice
+// start and stops at the first chunk whose starting decay is exactly 0 in f32,
+// after which every further term is exactly 0 as well.
+#include "common.cuh"
+
+namespace tssm {
+namespace {
+
+constexpr int FQ = 64;   // tokens per fix-up chunk
+constexpr int FP = 64;   // head dim
+
+template <int NST>
+__global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
+    const float* __restrict__ S_all, const float* __restrict__ d_all, int rank, int Bsz,
+    const __nv_bfloat16* __restrict__ C, const float* __restrict__ dt, const float* __restrict__ A_log,
+    __nv_bfloat16* __restrict__ y, int L, int H) {
+  extern __shared__ __align__(16) float fsm[];
+  float* carry = fsm;                   // [FP][NST + 1] (padded rows: no bank conflicts)
+  float* cs = carry + FP * (NST + 1);   // [FQ][NST + 1]
+  float* es = cs + FQ * (NST + 1);      // [FQ] decay factor per token
+  __shared__ float s_run;
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  // carry entering this slice
+  const int64_t per_rank = (int64_t)Bsz * H * FP * NST;
+  const int64_t base = (((int64_t)b * H + h) * FP) * NST;
+  for (int e = tid; e < FP * NST; e += 256) {
+    float c = 0.f;
+    for (int j = 0; j < rank; ++j) c = exp2f(d_all[(int64_t)j * Bsz * H + (int64_t)b * H + h]) * c + S_all[j * per_rank + base + e];
+    carry[(e / NST) * (NST + 1) + (e % NST)] = c;
+  }
+  if (tid == 0) s_run = 0.f;
+  const float a2 = -expf(A_log[h]) * 1.4426950408889634f;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int tt = tid >> 4, pp = tid & 15;   // 4 tokens x 4 head dims per thread
+  __syncthreads();
+  for (int t0 = 0; t0 < L; t0 += FQ) {
+    // decay factors of this chunk (warp 0) and the chunk's C rows (all)
+    if (warp == 0) {
+      float l[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = t0 + 2 * lane + e;
+        l[e] = t < L ? dt[((int64_t)b * L + t) * H + h] * a2 : 0.f;
+      }
+      const float pair = l[0] + l[1];
+      float incl = pair;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const float run = s_run;
+      es[2 * lane] = exp2f(run + incl - pair + l[0]);
+      es[2 * lane + 1] = exp2f(run + incl);
+      const float tot = __shfl_sync(0xffffffffu, incl, 31);
+      __syncwarp();
+      if (lane == 0) s_run = run + tot;
+    }
+    for (int e = tid; e < FQ * NST / 2; e += 256) {
+      const int r = e / (NST / 2), c2 = e - r * (NST / 2);
+      const int t = t0 + r;
+      float2 v = make_float2(0.f, 0.f);
+      if (t < L) v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(C + (((int64_t)b * L + t) * H + h) * NST)[c2]);
+      cs[r * (NST + 1) + 2 * c2] = v.x;
+      cs[r * (NST + 1) + 2 * c2 + 1] = v.y;
+    }
+    __syncthreads();
+    if (es[0] == 0.f) break;   // uniform: every later decay is exactly 0 too
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int n = 0; n < NST; ++n) {
+      float cv[4], hv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cv[i] = cs[(4 * tt + i) * (NST + 1) + n];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) hv[j] = carry[(4 * pp + j) * (NST + 1) + n];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(cv[i], hv[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = t0 + 4 * tt + i;
+      if (t >= L) break;
+      const float e = es[4 * tt + i];
+      __nv_bfloat16* yr = y + ((int64_t)b * L + t) * H * FP + (int64_t)h * FP + 4 * pp;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) yr[j] = __float2bfloat16_rn(__bfloat162float(yr[j]) + e * acc[i][j]);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+}  // namespace tssm
+
+extern "C" int tssm_ssd_carry_fixup(const void* S_all, const void* decay_log2_all, int64_t rank, int64_t nranks,
+                                    const void* C, const void* dt, const void* A_log, void* y, int64_t Bsz,
+                                    int64_t L, int64_t H, int64_t P, int64_t N, tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(rank >= 0 && rank < nranks, "ssd_carry_fixup: rank out of range");
+  TSSM_REQUIRE(P == 64 && (N == 64 || N == 128), "ssd_carry_fixup: P must be 64 and N 64 or 128");
+  if (rank == 0 || Bsz * L * H == 0) return TSSM_OK;
+  TSSM_REQUIRE(S_all && decay_log2_all && C && dt && A_log && y, "ssd_carry_fixup: null pointer");
+  TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31), "ssd_carry_fixup: size out of range");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)H, (unsigned)Bsz);
+  if (N == 64) {
+    const size_t smem = sizeof(float) * (64 * 65 + 64 * 65 + 64);
+    if (cudaFuncSetAttribute(ssd_carry_fixup_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return check_launch("ssd_carry_fixup: smem");
+    ssd_carry_fixup_kernel<64><<<grid, 256, smem, st>>>((const float*)S_all, (const float*)decay_log2_all, (int)rank,
+                                                        (int)Bsz, (const __nv_bfloat16*)C, (const float*)dt,
+                                                        (const float*)A_log, (__nv_bfloat16*)y, (int)L, (int)H);
+  } else {
+    const size_t smem = sizeof(float) * (64 * 129 + 64 * 129 + 64);
+    if (cudaFuncSetAttribute(ssd_carry_fixup_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return check_launch("ssd_carry_fixup: smem");
+    ssd_carry_fixup_kernel<128><<<grid, 256, smem, st>>>((const float*)S_all, (const float*)decay_log2_all,
+                                                         (int)rank, (int)Bsz, (const __nv_bfloat16*)C,
+                                                         (const float*)dt, (const float*)A_log,
+                                                         (__nv_bfloat16*)y, (int)L, (int)H);
+  }
+  return check_launch("ssd_carry_fixup");
+}

@@ -99,7 +99,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
     const __grid_constant__ CUtensorMap tm_c, __nv_bfloat16* __restrict__ y,
     const float* __restrict__ dt, const float* __restrict__ A_log, const float* __restrict__ Dskip,
-    const float* __restrict__ h0, float* __restrict__ h_last, int* __restrict__ status, int L, int H) {
+    const float* __restrict__ h0, float* __restrict__ h_last, float* __restrict__ decay_log2,
+    int* __restrict__ status, int L, int H) {
   using LY = Layout<NST>;
   constexpr int NB = LY::NB;
   constexpr int ST = LY::STAGES;
@@ -235,6 +236,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
     for (int i = 0; i < ST - 1; ++i) issue_dt(i);
+    float total_log2 = 0.f;   // sum over the sequence of dt*A_h*log2(e): log2 of the whole-sequence decay
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % ST, k = c / ST;
       int bad = 0;   // decided by lane 0, broadcast so the warp stays converged
@@ -261,6 +263,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       }
       const float s0 = incl - pair + l0, s1 = incl;
       const float slast = __shfl_sync(0xffffffffu, incl, 31);
+      total_log2 += slast;
       float b0, b1;
       if (ZOH) {
         const float x0 = d0 * a, x1 = d1 * a;
@@ -288,6 +291,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");   // no copy may outlive the loop
+    if (decay_log2 && lane == 0 && !*abort_flag) decay_log2[(int64_t)b * H + h] = total_log2;
   } else if (warp == 9) {
     // ================================================================ MMA2 + MMA4 issuer
     if (lane == 0) {
@@ -582,7 +586,7 @@ bool map3d_bf16(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint
 template <int NST, bool ZOH>
 int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& mc, __nv_bfloat16* y,
                const float* dt, const float* A_log, const float* Dskip, const float* h0, float* h_last,
-               int64_t Bsz, int64_t L, int64_t H, cudaStream_t st) {
+               float* decay_log2, int64_t Bsz, int64_t L, int64_t H, cudaStream_t st) {
   constexpr int bytes = Layout<NST>::BYTES;
   auto kern = ssd_chunk_scan_kernel<NST, ZOH>;
   // The dynamic shared-memory opt-in is per device; it is cheap, so set it on every launch.
@@ -594,7 +598,8 @@ int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& 
     return TSSM_ERR_CUDA;
   }
   dim3 grid((unsigned)H, (unsigned)Bsz);
-  kern<<<grid, NTHREADS, bytes, st>>>(mx, mb, mc, y, dt, A_log, Dskip, h0, h_last, status, (int)L, (int)H);
+  kern<<<grid, NTHREADS, bytes, st>>>(mx, mb, mc, y, dt, A_log, Dskip, h0, h_last, decay_log2, status, (int)L,
+                                      (int)H);
   return check_launch("ssd_chunk_scan");
 }
 
@@ -603,8 +608,8 @@ int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& 
 
 extern "C" int tssm_multihead_ssd(const void* x, const void* dt, const void* A_log, const void* B,
                                   const void* C, const void* Dskip, void* y, const void* h0, void* h_last,
-                                  int64_t Bsz, int64_t L, int64_t H, int64_t P, int64_t N, int bdisc,
-                                  tssm_stream_t stream) {
+                                  void* decay_log2, int64_t Bsz, int64_t L, int64_t H, int64_t P, int64_t N,
+                                  int bdisc, tssm_stream_t stream) {
   using namespace tssm;
   TSSM_REQUIRE(Bsz >= 0 && L >= 0 && H >= 0, "multihead_ssd: negative size");
   if (Bsz * L * H == 0) return TSSM_OK;
@@ -629,12 +634,13 @@ extern "C" int tssm_multihead_ssd(const void* x, const void* dt, const void* A_l
   const float* dk = (const float*)Dskip;
   const float* hi = (const float*)h0;
   float* ho = (float*)h_last;
+  float* dl = (float*)decay_log2;
   __nv_bfloat16* my = (__nv_bfloat16*)y;
   if (N == 64)
-    return bdisc ? launch_ssd<64, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st)
-                 : launch_ssd<64, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st);
-  return bdisc ? launch_ssd<128, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st)
-               : launch_ssd<128, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, Bsz, L, H, st);
+    return bdisc ? launch_ssd<64, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st)
+                 : launch_ssd<64, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st);
+  return bdisc ? launch_ssd<128, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st)
+               : launch_ssd<128, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st);
 }
 
 #ifdef TSSM_SSD_TRACE

@@ -13,7 +13,8 @@ from ._lib import call, dtype_code, ptr, stream_of
 
 __all__ = ["zoh_discretize", "ssm_forward", "selective_scan", "streaming_ssm_inplace",
            "streaming_step", "multihead_ssm", "check_device_status", "fused_time_aware_interp",
-           "fused_interp_ssm_step", "fused_interp_ssm", "linspace_queries", "interp_ssm_workspace_bytes"]
+           "fused_interp_ssm_step", "fused_interp_ssm", "linspace_queries", "interp_ssm_workspace_bytes",
+           "ssd_carry_fixup"]
 
 
 def _cuda(*ts):
@@ -171,14 +172,15 @@ _BDISC = {"euler": 0, "zoh": 1}
 
 
 def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h0=None,
-                  return_state=False, y=None):
+                  return_state=False, y=None, return_decay=False):
     """Multi-head chunked scan (``multihead_ssm_kernel.py:19-187``).
 
     mode="ssd": outer-product state h[b,h,p,n] on tcgen05 tensor cores.
       u [Bt,L,H*P] bf16; A_log [H] f32 (log(-A_h)); B, C [Bt,L,H,N] bf16;
       dt [Bt,L,H] f32; D [H*P] f32; h0 [Bt,H,P,N] f32 or None.
       Returns y [Bt,L,H*P] bf16, or (y, h_last [Bt,H,P,N] f32) when
-      ``return_state``.  P = 64, N in {64, 128}.
+      ``return_state``; with ``return_decay`` also the log2 of the
+      whole-sequence decay per (b, h), [Bt,H] f32.  P = 64, N in {64, 128}.
     ``BLK_L`` is accepted for signature compatibility (the kernel's chunk is
     64 tokens; results do not depend on it beyond rounding).
     """
@@ -209,9 +211,38 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
     if y is None:
         y = torch.empty_like(u)
     hl = torch.empty(Bt, H, P, N, device=u.device, dtype=torch.float32) if return_state else None
+    dl = torch.empty(Bt, H, device=u.device, dtype=torch.float32) if return_decay else None
     call("tssm_multihead_ssd", ptr(u), ptr(dt), ptr(A_log), ptr(B), ptr(C), ptr(D), ptr(y), ptr(h0),
-         ptr(hl), Bt, L, H, P, N, _BDISC[bdisc], stream_of(u))
-    return (y, hl) if return_state else y
+         ptr(hl), ptr(dl), Bt, L, H, P, N, _BDISC[bdisc], stream_of(u))
+    out = [y]
+    if return_state:
+        out.append(hl)
+    if return_decay:
+        out.append(dl)
+    return out[0] if len(out) == 1 else tuple(out)
+
+
+def ssd_carry_fixup(S_all, decay_log2_all, rank, C, dt, A_log, y):
+    """Chain a sequence slice to the slices before it (in place on ``y``).
+
+    S_all [R,Bt,H,P,N] f32 and decay_log2_all [R,Bt,H] f32 are every rank's
+    final state and whole-slice log2 decay from ``multihead_ssm(...,
+    return_state=True, return_decay=True)``; C [Bt,L,H,N] bf16, dt [Bt,L,H]
+    f32 and y [Bt,L,H*P] bf16 are this rank's slice.  See
+    ``tssm_ssd_carry_fixup`` in include/tssm.h.
+    """
+    _cuda(S_all, decay_log2_all, C, dt, A_log, y)
+    R, Bt, H, P, N = S_all.shape
+    L = C.shape[1]
+    if tuple(decay_log2_all.shape) != (R, Bt, H) or tuple(C.shape) != (Bt, L, H, N) or \
+            tuple(dt.shape) != (Bt, L, H) or tuple(y.shape) != (Bt, L, H * P):
+        raise ValueError("ssd_carry_fixup: shape mismatch")
+    if not (S_all.is_contiguous() and decay_log2_all.is_contiguous() and C.is_contiguous() and
+            dt.is_contiguous() and y.is_contiguous()):
+        raise ValueError("ssd_carry_fixup: tensors must be contiguous")
+    call("tssm_ssd_carry_fixup", ptr(S_all), ptr(decay_log2_all), int(rank), R, ptr(C), ptr(dt),
+         ptr(A_log.float().contiguous()), ptr(y), Bt, L, H, P, N, stream_of(y))
+    return y
 
 
 def check_device_status(device=None):

@@ -76,3 +76,30 @@ def stream_inputs(S, H, P, N, device, seed, nsets=16):
 
 def stream_bytes(S, H, P, N):
     return 2 * S * H * P * N * 4 + 2 * S * H * P * 2 + 2 * S * H * N * 2 + S * 4 + H * 4 + H * P * 4
+
+
+def ssd_inputs_slice(Bt, L0, Ls, H, P, N, device, seed, block=1 << 14, A_mode="config1"):
+    """The [L0, L0+Ls) slice of a long sequence (config 4), generated in blocks
+    of `block` tokens each seeded by its index, so every rank can build its own
+    slice and the slices of any rank count concatenate to the same sequence.
+    A_h = -(1 + h mod 16) ("A as in config 1", per head); dt log-uniform on [1e-3, 1].
+    """
+    assert L0 % block == 0, "slices start on a block boundary"
+    x = torch.empty(Bt, Ls, H * P, device=device, dtype=torch.bfloat16)
+    dt = torch.empty(Bt, Ls, H, device=device)
+    B = torch.empty(Bt, Ls, H, N, device=device, dtype=torch.bfloat16)
+    C = torch.empty(Bt, Ls, H, N, device=device, dtype=torch.bfloat16)
+    s = 1.0 / math.sqrt(N)
+    for o in range(0, Ls, block):
+        n = min(block, Ls - o)
+        g = _gen(device, seed * 1000003 + (L0 + o) // block)
+        x[:, o:o + n] = torch.randn(Bt, n, H * P, device=device, generator=g).to(torch.bfloat16)
+        dt[:, o:o + n] = torch.exp(torch.empty(Bt, n, H, device=device).uniform_(math.log(1e-3), 0.0, generator=g))
+        B[:, o:o + n] = (torch.randn(Bt, n, H, N, device=device, generator=g) * s).to(torch.bfloat16)
+        C[:, o:o + n] = (torch.randn(Bt, n, H, N, device=device, generator=g) * s).to(torch.bfloat16)
+    if A_mode == "config1":
+        A_log = torch.log(1.0 + (torch.arange(H, device=device) % 16).float())
+    else:
+        A_log = torch.empty(H, device=device).uniform_(math.log(0.5), math.log(16.0), generator=_gen(device, seed))
+    D = torch.randn(H * P, device=device, generator=_gen(device, seed + 1))
+    return dict(x=x, dt=dt, A_log=A_log, B=B, C=C, D=D)
