@@ -79,14 +79,18 @@ def make_c3(Bt, T, Dm, N, Lq, seed, p_obs=0.7):
 
 
 @pytest.mark.parametrize("Bt,T,Dm,N,Lq,p_obs", [(2, 300, 256, 16, 600, 0.7), (3, 100, 70, 5, 257, 0.02),
-                                                 (1, 64, 33, 64, 64, 0.3)])
+                                                 (1, 64, 33, 64, 64, 0.3), (4, 300, 64, 16, 500, 0.7),
+                                                 (2, 90, 192, 16, 120, 0.02)])
 def test_interp_ssm_query_grid_vs_oracle(cuda_ops, Bt, T, Dm, N, Lq, p_obs):
     V, M, tau, A_log, B, C, D = make_c3(Bt, T, Dm, N, Lq, seed=T + N, p_obs=p_obs)
     # the same query times on both sides (a device-built grid may differ in the last ulp)
     q = oracle.linspace_queries(tau, Lq)
     dt = (tau[:, -1] - tau[:, 0]) / (Lq - 1)
+    # a workspace holding garbage: every flag and table entry must be written before it is read
+    need = cuda_ops.interp_ssm_workspace_bytes(Bt, T, Dm, Lq)
+    ws = torch.full((need,), 0xA5, dtype=torch.uint8, device=dev)
     y, h, vh = cuda_ops.fused_interp_ssm(cu(V), cu(M), cu(tau), cu(A_log), cu(B), cu(C), q=cu(q), dt=cu(dt),
-                                         D=cu(D), return_state=True, return_vhat=True)
+                                         D=cu(D), return_state=True, return_vhat=True, workspace=ws)
     ry, rh, rvh = oracle.interp_ssm(V, M, tau, A_log, B, C, dt, q=q, D=D, return_vhat=True)
     assert torch.equal(vh.cpu(), rvh)
     assert rel_err(y, ry) < TOL_FP32

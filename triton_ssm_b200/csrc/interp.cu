@@ -640,7 +640,8 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
   {
     const int64_t rows = T * ntiles;   // one warp per (t, tile) row, 8 warps per block
     dim3 grid((unsigned)std::max<int64_t>(1, cdiv(rows, 8)), (unsigned)Bsz);
-    const bool vec = m_dtype == TSSM_U8 && Dm % 16 == 0 && FTILE % 16 == 0 && FTILE / 16 <= 32 &&
+    // the word groups of one (row, tile) line up with the rows only when every tile is full
+    const bool vec = m_dtype == TSSM_U8 && Dm % FTILE == 0 && FTILE % 16 == 0 && FTILE / 16 <= 32 &&
                      ((FTILE / 16) & (FTILE / 16 - 1)) == 0 && (reinterpret_cast<uintptr_t>(Mk) & 15) == 0;
     if (vec) {
       const int64_t nwords = Bsz * T * Dm / 16;
