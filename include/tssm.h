@@ -200,6 +200,28 @@ int tssm_interp_ssm(const void* V, const void* M, const void* tau, const void* q
                     int m_dtype, tssm_stream_t stream);
 
 /*
+ * tssm_interp_ssm for callers that cannot allocate device memory when they
+ * call in (for example a backend running inside another runtime's fixed
+ * memory budget, or a latency-critical streaming loop that must not call
+ * cudaMalloc): the same computation and arguments without `workspace`; the
+ * scratch comes from an 8 MiB array compiled into the library, which every
+ * GPU that loads the library holds until the process exits.  No counterpart
+ * in the reference (the reference always allocates through PyTorch).
+ *   Returns TSSM_ERR_INVALID, with a message, when the problem needs more than
+ *   8 MiB of scratch (tssm_interp_ssm_workspace_size tells how much).
+ *   The first call on a device looks up the array's device address; make that
+ *   first call before any stream capture.
+ *   All calls share the one array: calls that overlap on the GPU (other
+ *   streams, other host threads) race on it and must be serialised by the
+ *   caller.  Nothing in it needs clearing between calls.
+ */
+int tssm_interp_ssm_static_scratch(const void* V, const void* M, const void* tau, const void* q,
+                                   const void* A_log, const void* B, const void* C, const void* Dskip,
+                                   const void* dt, void* y, void* h_last, void* vhat, int64_t Bsz,
+                                   int64_t T, int64_t Dm, int64_t N, int64_t Lq, int64_t K, int64_t FTILE,
+                                   int m_dtype, tssm_stream_t stream);
+
+/*
  * Sequence-parallel chaining of multi-head scan slices (config 4).  The
  * block-level carry scan of ssm_scan.py:53-98 (ssm_carry_scan_kernel +
  * ssm_fwd_apply_kernel) lifted from blocks of one GPU to slices of the sequence

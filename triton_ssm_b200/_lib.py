@@ -39,6 +39,7 @@ SIGNATURES = {
     "tssm_interp_ssm_step": ([P] * 8 + [I64] * 3 + [I64] * 9 + [I64] * 3 + [I32, P], I32),
     "tssm_interp_ssm_workspace_size": ([I64] * 5, I64),
     "tssm_interp_ssm": ([P] * 13 + [I64] + [I64] * 7 + [I32, P], I32),
+    "tssm_interp_ssm_static_scratch": ([P] * 12 + [I64] * 7 + [I32, P], I32),
 }
 
 _lib = None

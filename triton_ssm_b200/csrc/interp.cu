@@ -13,6 +13,8 @@
 // lo = #{tau < q}, hi = #{tau <= q}; previous candidates are obs lo-1..lo-K,
 // next candidates hi..hi+K-1, and the fallback value is obs hi-1 when hi > lo
 // (an observation at exactly q), else 0.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace tssm {
@@ -696,3 +698,59 @@ extern "C" int tssm_debug_read_interp_trace(unsigned long long* out, int n) {
                  cudaSuccess ? 0 : 3;
 }
 #endif
+
+// ---------------------------------------------------------------------------
+// Entry point for callers that cannot allocate device memory when they call in.
+//
+// Some callers own no device allocator at call time: a backend or plugin that
+// runs inside another runtime's fixed memory budget, or a latency-critical
+// streaming loop where cudaMalloc (which synchronises the device and can fail
+// under fragmentation) is not acceptable.  For them the scratch that
+// tssm_interp_ssm takes as `workspace` (tile flags + neighbour table) lives in
+// a fixed array compiled into this library instead.
+namespace {
+constexpr int64_t kStaticScratchBytes = int64_t(8) << 20;   // 8 MiB, held by every device that loads the library
+static __device__ __align__(256) unsigned char g_interp_static_scratch[kStaticScratchBytes];
+
+// Device address of the array for the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device, with that device current, and cached.
+int static_scratch_ptr(void** out) {
+  static std::atomic<void*> cache[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+  void* p = cache[dev].load();
+  if (!p) {
+    e = cudaGetSymbolAddress(&p, g_interp_static_scratch);
+    if (e != cudaSuccess) return (int)e;
+    cache[dev].store(p);
+  }
+  *out = p;
+  return 0;
+}
+}  // namespace
+
+extern "C" int tssm_interp_ssm_static_scratch(const void* V, const void* Mk, const void* tau, const void* q,
+                                              const void* A_log, const void* B, const void* C,
+                                              const void* Dskip, const void* dt, void* y, void* h_last,
+                                              void* vhat, int64_t Bsz, int64_t T, int64_t Dm, int64_t N,
+                                              int64_t Lq, int64_t K, int64_t FTILE, int m_dtype,
+                                              tssm_stream_t stream) {
+  const int64_t need = tssm_interp_ssm_workspace_size(Bsz, T, Dm, Lq, FTILE);
+  TSSM_REQUIRE(need <= kStaticScratchBytes,
+               "interp_ssm_static_scratch: this problem needs %lld bytes of scratch; the library's static "
+               "scratch holds %lld bytes (use tssm_interp_ssm with a caller-provided workspace)",
+               (long long)need, (long long)kStaticScratchBytes);
+  void* scratch = nullptr;
+  const int e = static_scratch_ptr(&scratch);
+  if (e != 0) {
+    set_error("interp_ssm_static_scratch: cudaGetSymbolAddress failed: %s", cudaGetErrorString((cudaError_t)e));
+    return TSSM_ERR_CUDA;
+  }
+  // The flags and the neighbour table are written in full before they are read,
+  // so nothing in the shared array needs clearing between calls.
+  return tssm_interp_ssm(V, Mk, tau, q, A_log, B, C, Dskip, dt, y, h_last, vhat, scratch, kStaticScratchBytes, Bsz,
+                         T, Dm, N, Lq, K, FTILE, m_dtype, stream);
+}
