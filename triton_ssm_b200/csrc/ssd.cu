@@ -69,7 +69,8 @@ struct Layout {
   static constexpr int STAGE_BYTES = TILE * (1 + 2 * NB);
   static constexpr int STAGES = NST == 64 ? 4 : 3;
   static constexpr int HS_BYTES = NST * 128;           // state tile: NST rows (n) x 64 p, MN-major
-  static constexpr int OFF_MT = STAGES * STAGE_BYTES;  // 2 mask tiles
+  static constexpr int OFF_BH = STAGES * STAGE_BYTES;  // 2 tiles of diag(w) B (MMA4's A operand)
+  static constexpr int OFF_MT = OFF_BH + 2 * NB * TILE; // 2 mask tiles
   static constexpr int OFF_HS = OFF_MT + 2 * TILE;     // 2 state tiles
   static constexpr int OFF_SMALL = OFF_HS + 2 * HS_BYTES;  // per stage: s, s', w [64] + exp(s_last)
   static constexpr int SMALL_STRIDE = 5 * 64 * 4;     // s, s', w, [e_last], raw dt
@@ -130,6 +131,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   auto stage_ptr = [&](int s) { return smem + s * LY::STAGE_BYTES; };
   auto small_ptr = [&](int s) { return reinterpret_cast<float*>(smem + LY::OFF_SMALL + s * LY::SMALL_STRIDE); };
   auto mt_ptr = [&](int k) { return smem + LY::OFF_MT + k * TILE; };
+  auto bh_ptr = [&](int k) { return smem + LY::OFF_BH + k * NB * TILE; };
   auto hs_ptr = [&](int k) { return smem + LY::OFF_HS + k * LY::HS_BYTES; };
 
   if (tid == 0) {
@@ -273,13 +275,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         b0 = d0;
         b1 = d1;
       }
-      // per token: s_j (log2 domain), s'_j = s_j - log2(beta_j) (beta = 0 -> +inf, so the
-      // mask entry exp2(s_i - s'_j) is exactly 0), and the state weight w_j = exp2(s_last - s_j) beta_j
+      // per token: s_j (log2 domain), v_j (below), and the state weight w_j = exp2(s_last - s_j) beta_j
       float* sm = small_ptr(s);
       sm[2 * lane] = s0;
       sm[2 * lane + 1] = s1;
-      sm[64 + 2 * lane] = b0 > 0.f ? s0 - __log2f(b0) : INFINITY;
-      sm[64 + 2 * lane + 1] = b1 > 0.f ? s1 - __log2f(b1) : INFINITY;
+      // v_j = exp2(s_ref(j) - s_j) * beta_j with ref(j) the last token of j's 4-token
+      // sub-block: the mask entry is G_ij * exp2(s_i - s_ref(J)) * v_j (both factors bounded)
+      const float sref = __shfl_sync(0xffffffffu, s1, lane | 1);
+      sm[64 + 2 * lane] = exp2f(sref - s0) * b0;
+      sm[64 + 2 * lane + 1] = exp2f(sref - s1) * b1;
       sm[128 + 2 * lane] = exp2f(slast - s0) * b0;
       sm[128 + 2 * lane + 1] = exp2f(slast - s1) * b1;
       if (lane == 0) sm[192] = exp2f(slast);
@@ -306,7 +310,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         SSD_TRACE(k, 3);
         const uint32_t X = smem_u32(stage_ptr(s));
         const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
-        const uint64_t dX = make_desc_sw128(X, TILE), dBh = make_desc_sw128(X + TILE, TILE);
+        const uint64_t dX = make_desc_sw128(X, TILE), dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_y1(kb), dM + 2 * kk, dX + 128 * kk, ID_KM, kk > 0);
 #pragma unroll
@@ -344,41 +348,70 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const uint32_t lane_base = (uint32_t)(w * 32) << 16;
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % ST, kb = c & 1;
+      // (1) tiles and decay data of chunk c landed; M and diag(w)B buffers of chunk c-2 released
       bool bad = false;
       if (t == 0) {
-        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag);
-        SSD_TRACE(c, 14);
-        bad = bad || (c >= 2 && !mbar_wait(&yfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
+        bad = !mbar_wait(&full[s], (c / ST) & 1, abort_flag) ||
+              (c >= 2 && !mbar_wait(&yfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
         if (bad && !*abort_flag) fail(1007);
       }
       if (named_bar_or(2, 128, bad)) break;
-      if (t == 0) SSD_TRACE(c, 5);
       mbar_wait(&full[s], (c / ST) & 1);
+      const float* sm = small_ptr(s);
+      const uint8_t* Bt = stage_ptr(s) + TILE;
+      // (2) diag(w) B into its own tile (bf16x2 arithmetic); overlaps MMA1, which reads B
+      {
+        uint8_t* Bh = bh_ptr(kb);
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int idx = t + it * 128;            // 16-byte chunk; row j = idx / 8
+            const __nv_bfloat162 w2 = __float2bfloat162_rn(sm[128 + (idx >> 3)]);
+            uint4 v = *reinterpret_cast<const uint4*>(Bt + nb * TILE + idx * 16);
+            __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v);
+            hv[0] = __hmul2(hv[0], w2);
+            hv[1] = __hmul2(hv[1], w2);
+            hv[2] = __hmul2(hv[2], w2);
+            hv[3] = __hmul2(hv[3], w2);
+            *reinterpret_cast<uint4*>(Bh + nb * TILE + idx * 16) = v;
+          }
+        }
+      }
+      // (3) G of chunk c
+      if (t == 0) {
+        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
+        SSD_TRACE(c, 14);
+        if (bad && !*abort_flag) fail(1013);
+      }
+      if (named_bar_or(2, 128, bad)) break;
+      if (t == 0) SSD_TRACE(c, 5);
       mbar_wait(&gfull[kb], (c >> 1) & 1);
       tc_fence_after();
-      const float* sm = small_ptr(s);
-      uint8_t* X = stage_ptr(s);
-      uint8_t* Bt = X + TILE;
-      // M row `row`, columns [32*half, 32*half+32): M_ij = G_ij * exp2(s_i - s'_j) for j <= i
+      // (4) M row `row`, columns [32*half, 32*half+32):
+      //     M_ij = G_ij * exp2(s_i - s_ref(J)) * v_j for j <= i (J = 4-token sub-block of j)
       float g[32];
       tmem_ld16x2_32(tmem + lane_base + col_g(kb), g);
       {
         const float si = sm[row];
-        const float4* spv = reinterpret_cast<const float4*>(sm + 64 + half * 32);
+        const float4* vv = reinterpret_cast<const float4*>(sm + 64 + half * 32);
         const int nvalid = row - half * 32;      // columns jj <= nvalid are kept
+        float u[8];
+#pragma unroll
+        for (int J = 0; J < 8; ++J) u[J] = fast_exp2(si - sm[half * 32 + 4 * J + 3]);
         uint8_t* Mt = mt_ptr(kb);
         tmem_wait_ld();
         if (t == 0) SSD_TRACE(c, 15);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float4 sa = spv[2 * q], sb = spv[2 * q + 1];
-          const float sp[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+          const float4 va = vv[2 * q], vb = vv[2 * q + 1];
+          const float v8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
           float m[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int jj = q * 8 + e;
-            const float v = g[jj] * fast_exp2(si - sp[e]);
-            m[e] = jj <= nvalid ? v : 0.f;
+            const float val = (g[jj] * u[jj >> 2]) * v8[e];
+            m[e] = jj <= nvalid ? val : 0.f;
           }
           *reinterpret_cast<uint4*>(Mt + sw128_chunk(row, half * 4 + q)) =
               make_uint4(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]), pack_bf16x2(m[4], m[5]),
@@ -386,23 +419,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         }
       }
       if (t == 0) SSD_TRACE(c, 16);
-      // B <- diag(w) B in place, bf16x2 arithmetic (MMA1 of this chunk is complete)
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-          const int idx = t + it * 128;            // 16-byte chunk; row j = idx / 8
-          uint4* pch = reinterpret_cast<uint4*>(Bt + nb * TILE + idx * 16);
-          const __nv_bfloat162 w2 = __float2bfloat162_rn(sm[128 + (idx >> 3)]);
-          uint4 v = *pch;
-          __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v);
-          hv[0] = __hmul2(hv[0], w2);
-          hv[1] = __hmul2(hv[1], w2);
-          hv[2] = __hmul2(hv[2], w2);
-          hv[3] = __hmul2(hv[3], w2);
-          *pch = v;
-        }
-      }
       fence_proxy_async_smem();
       tc_fence_before();
       named_bar_sync(2, 128);
