@@ -239,6 +239,24 @@ int tssm_ssd_carry_fixup(const void* S_all, const void* decay_log2_all, int64_t 
                          int64_t L, int64_t H, int64_t P, int64_t N, tssm_stream_t stream);
 
 /*
+ * Multi-head scan with the reference's own diagonal state h[b,head,p].
+ * Replaces multihead_ssm_fwd_local_kernel / multihead_ssm_carry_scan_kernel /
+ * multihead_ssm_output_kernel (multihead_ssm_kernel.py:19-187, with the
+ * scalar-index and item-assignment errors at :101 and :151 read as their
+ * evident intent), in one launch:
+ *   Abar = exp(dt[b,t,head]*a[head,p]), a = -exp(A_log[head,p]);
+ *   h = Abar*h + (beta*B[b,t,head,p])*u[b,t,head*hd+p], beta = dt (bdisc 0) or
+ *   the ZOH factor (bdisc 1);  y_head[t] = sum_p C*h + sum_p D*u, written to
+ *   every position of the head's slice of y (:182-187).
+ *   u, y [Bsz,L,n_heads*head_dim] (dtype f32 or bf16); A_log [n_heads,head_dim]
+ *   f32; B, C [Bsz,L,n_heads,head_dim] (dtype); dt [Bsz,L,n_heads] f32;
+ *   Dskip [n_heads*head_dim] f32.  All contiguous, head_dim <= 128.
+ */
+int tssm_multihead_diag(const void* u, const void* A_log, const void* B, const void* C, const void* dt,
+                        const void* Dskip, void* y, int64_t Bsz, int64_t L, int64_t n_heads,
+                        int64_t head_dim, int bdisc, int dtype, tssm_stream_t stream);
+
+/*
  * Synchronise `stream` and report (then clear) this device's status word:
  * TSSM_ERR_TIMEOUT if a kernel's bounded device-side wait gave up since the
  * last check, else TSSM_OK.  No reference counterpart (the reference has no

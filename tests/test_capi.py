@@ -58,3 +58,16 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(2, 3, 4)
     with pytest.raises(ValueError):
         ts.ssm_forward(x, x, x, x, torch.zeros(4))
+
+
+def test_compat_namespaces_mirror_reference_names():
+    from triton_ssm_b200 import compat
+    assert hasattr(compat.discretize_kernel, "zoh_discretize_diag_kernel")
+    assert hasattr(compat.discretize_kernel, "zoh_discretize_diag_bf16_kernel")
+    assert hasattr(compat.fused_interp_kernel, "fused_interp_fp16_kernel")
+    assert hasattr(compat.fused_ssm_interp, "fused_interp_ssm_step_kernel")
+    assert hasattr(compat.streaming_inference_kernel, "streaming_ssm_inplace_bf16_kernel")
+    assert callable(compat.ssm_scan.ssm_forward)
+    # kernel objects are launched with [grid]
+    fn = compat.discretize_kernel.zoh_discretize_diag_kernel[(1, 1, 1)]
+    assert callable(fn)

@@ -84,3 +84,31 @@ def test_ssd_rejects_unsupported(cuda_ops):
     x, dt, A_log, B, C, D = make_inputs(1, 10, 2, 32, 64, seed=0)
     with pytest.raises(ValueError):
         run(cuda_ops, x, dt, A_log, B, C, D)
+
+
+# ---------------------------------------------------------------- diagonal mode
+def test_multihead_diag_golden(cuda_ops):
+    from conftest import TOL_FP32, load_golden
+    g = load_golden("mh_diag_composed")
+    y = cuda_ops.multihead_ssm(g["x"].to(dev), g["A_log"].to(dev), g["B"].to(dev), g["C"].to(dev),
+                               g["dt"].to(dev), g["D"].to(dev), mode="diag")
+    assert rel_err(y, g["y"]) < TOL_FP32
+
+
+@pytest.mark.parametrize("hd,L,dty,bdisc", [(64, 1000, torch.float32, "euler"), (33, 257, torch.float32, "zoh"),
+                                            (128, 300, torch.bfloat16, "euler"), (8, 5, torch.float32, "euler")])
+def test_multihead_diag_vs_oracle(cuda_ops, hd, L, dty, bdisc):
+    from conftest import TOL_FP32
+    gen = torch.Generator().manual_seed(hd + L)
+    Bt, nh = 2, 3
+    u = torch.randn(Bt, L, nh * hd, generator=gen).to(dty)
+    A_log = torch.empty(nh, hd).uniform_(-0.7, 2.7, generator=gen)
+    B = torch.randn(Bt, L, nh, hd, generator=gen).to(dty)
+    C = torch.randn(Bt, L, nh, hd, generator=gen).to(dty)
+    dt = torch.exp(torch.empty(Bt, L, nh).uniform_(-6.9, 0.0, generator=gen))
+    D = torch.randn(nh * hd, generator=gen)
+    y = cuda_ops.multihead_ssm(u.to(dev), A_log.to(dev), B.to(dev), C.to(dev), dt.to(dev), D.to(dev),
+                               mode="diag", bdisc=bdisc)
+    ry, _ = oracle.multihead_diag(u, A_log, B, C, dt, D, bdisc=bdisc)
+    tol = TOL_FP32 if dty == torch.float32 else TOL_BF16
+    assert y.dtype == dty and rel_err(y, ry) < tol

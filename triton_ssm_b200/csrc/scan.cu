@@ -151,6 +151,120 @@ __global__ void __launch_bounds__(NW * 32) selective_scan_kernel(
   if (h_last && warp == 0 && valid) h_last[(b * Dm + d) * N + n] = carry;
 }
 
+
+// Diagonal multi-head scan with the reference's readout (multihead_ssm_kernel.py:
+// 19-187, its compile errors read as their intent): per (b, head, p)
+//   Abar = exp(dt[b,t,head] * a[head,p]),  h = Abar*h + (beta*B[b,t,head,p])*u[b,t,head*hd+p]
+//   y_head[t] = sum_p C*h + sum_p D*u, written to every position of the head slice.
+// CTA = (head, b).  Thread (lane, pg, seg): p = 32*pg + lane, seg = time segment
+// of a super-segment of NSEG*S steps (fold / prefix / replay as in
+// ssm_forward_kernel); the per-step head sum is a warp reduction plus a sum of
+// the PG group partials through shared memory.
+template <typename T, int S, int NSEG, int PG, bool ZOH>
+__global__ void __launch_bounds__(32 * PG * NSEG, 1) multihead_diag_kernel(
+    const T* __restrict__ u, const float* __restrict__ A_log, const T* __restrict__ Bm, const T* __restrict__ Cm,
+    const float* __restrict__ dt, const float* __restrict__ Dskip, T* __restrict__ y, int L, int nh, int hd) {
+  __shared__ float s_a[NSEG][PG][32];
+  __shared__ float s_x[NSEG][PG][32];
+  __shared__ float s_carry[PG][32];
+  __shared__ float s_part[NSEG][S][PG];
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int pg = w % PG, seg = w / PG;
+  const int head = blockIdx.x, b = blockIdx.y;
+  const int p = pg * 32 + lane;
+  const bool valid = p < hd;
+  const int H = nh * hd;
+  const float a = valid ? -expf(A_log[head * hd + p]) : -1.f;
+  const float dsk = valid ? Dskip[head * hd + p] : 0.f;
+  const T* ub = u + (int64_t)b * L * H + head * hd + p;
+  const T* Bb = Bm + (int64_t)b * L * H + head * hd + p;   // [B,L,nh,hd] == [B,L,H]
+  const T* Cb = Cm + (int64_t)b * L * H + head * hd + p;
+  const float* dtb = dt + (int64_t)b * L * nh + head;
+  T* yb = y + (int64_t)b * L * H + head * hd + p;
+  float carry = 0.f;
+  for (int t0 = 0; t0 < L; t0 += NSEG * S) {
+    const int ts = t0 + seg * S;
+    float ab[S], bu[S], uu[S];
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      const int t = ts + i;
+      ab[i] = 1.f;
+      bu[i] = 0.f;
+      uu[i] = 0.f;
+      if (t < L) {
+        const float dv = __ldg(dtb + (int64_t)t * nh);
+        const float x = dv * a;
+        const float e = expf(x);
+        if (valid) {
+          ab[i] = e;
+          uu[i] = ldf(ub + (int64_t)t * H);
+          const float beta = ZOH ? zoh_coeff(x, e, a) : dv;
+          bu[i] = (beta * ldf(Bb + (int64_t)t * H)) * uu[i];
+        }
+      }
+    }
+    float ag_a = 1.f, ag_x = 0.f;
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      ag_x = ab[i] * ag_x + bu[i];
+      ag_a *= ab[i];
+    }
+    s_a[seg][pg][lane] = ag_a;
+    s_x[seg][pg][lane] = ag_x;
+    __syncthreads();
+    float hs = carry;
+    for (int q = 0; q < seg; ++q) hs = s_a[q][pg][lane] * hs + s_x[q][pg][lane];
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      hs = ab[i] * hs + bu[i];
+      const int t = ts + i;
+      float part = (valid && t < L) ? ldf(Cb + (int64_t)t * H) * hs + dsk * uu[i] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0) s_part[seg][i][pg] = part;
+    }
+    if (seg == NSEG - 1) s_carry[pg][lane] = hs;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      const int t = ts + i;
+      if (valid && t < L) {
+        float tot = 0.f;
+#pragma unroll
+        for (int g = 0; g < PG; ++g) tot += s_part[seg][i][g];
+        stf(yb + (int64_t)t * H, tot);
+      }
+    }
+    carry = s_carry[pg][lane];
+    __syncthreads();
+  }
+}
+
+template <typename T, int PG>
+int launch_diag(const void* u, const void* A_log, const void* B, const void* C, const void* dt, const void* D,
+                void* y, int64_t Bsz, int64_t L, int64_t nh, int64_t hd, bool zoh, cudaStream_t st) {
+  constexpr int S = 8, NSEG = PG == 1 ? 16 : (PG == 2 ? 8 : 4);
+  dim3 grid((unsigned)nh, (unsigned)Bsz);
+  if (zoh)
+    multihead_diag_kernel<T, S, NSEG, PG, true><<<grid, 32 * PG * NSEG, 0, st>>>(
+        (const T*)u, (const float*)A_log, (const T*)B, (const T*)C, (const float*)dt, (const float*)D, (T*)y,
+        (int)L, (int)nh, (int)hd);
+  else
+    multihead_diag_kernel<T, S, NSEG, PG, false><<<grid, 32 * PG * NSEG, 0, st>>>(
+        (const T*)u, (const float*)A_log, (const T*)B, (const T*)C, (const float*)dt, (const float*)D, (T*)y,
+        (int)L, (int)nh, (int)hd);
+  return check_launch("multihead_diag");
+}
+
+template <typename T>
+int dispatch_diag(const void* u, const void* A_log, const void* B, const void* C, const void* dt, const void* D,
+                  void* y, int64_t Bsz, int64_t L, int64_t nh, int64_t hd, bool zoh, cudaStream_t st) {
+  if (hd <= 32) return launch_diag<T, 1>(u, A_log, B, C, dt, D, y, Bsz, L, nh, hd, zoh, st);
+  if (hd <= 64) return launch_diag<T, 2>(u, A_log, B, C, dt, D, y, Bsz, L, nh, hd, zoh, st);
+  return launch_diag<T, 4>(u, A_log, B, C, dt, D, y, Bsz, L, nh, hd, zoh, st);
+}
+
 }  // namespace
 }  // namespace tssm
 
@@ -199,4 +313,22 @@ extern "C" int tssm_selective_scan(const void* x, const void* dt, const void* A_
       (const float*)x, (const float*)dt, (const float*)A_log, (const float*)B, (const float*)C,
       (const float*)Dskip, (float*)y, (float*)h_last, L, Dm, (int)N, NP);
   return check_launch("selective_scan");
+}
+
+extern "C" int tssm_multihead_diag(const void* u, const void* A_log, const void* B, const void* C, const void* dt,
+                                   const void* Dskip, void* y, int64_t Bsz, int64_t L, int64_t n_heads,
+                                   int64_t head_dim, int bdisc, int dtype, tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(Bsz >= 0 && L >= 0 && n_heads >= 0 && head_dim >= 0, "multihead_diag: negative size");
+  if (Bsz * L * n_heads * head_dim == 0) return TSSM_OK;
+  TSSM_REQUIRE(u && A_log && B && C && dt && Dskip && y, "multihead_diag: null pointer");
+  TSSM_REQUIRE(head_dim <= 128, "multihead_diag: head_dim=%lld > 128 is not supported", (long long)head_dim);
+  TSSM_REQUIRE(bdisc == 0 || bdisc == 1, "multihead_diag: bdisc must be 0 (euler) or 1 (zoh)");
+  TSSM_REQUIRE(Bsz <= 65535 && n_heads <= 65535 && L < (int64_t(1) << 31), "multihead_diag: size out of range");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == TSSM_F32) return dispatch_diag<float>(u, A_log, B, C, dt, Dskip, y, Bsz, L, n_heads, head_dim, bdisc == 1, st);
+  if (dtype == TSSM_BF16)
+    return dispatch_diag<__nv_bfloat16>(u, A_log, B, C, dt, Dskip, y, Bsz, L, n_heads, head_dim, bdisc == 1, st);
+  set_error("multihead_diag: dtype must be f32 or bf16 (got %d)", dtype);
+  return TSSM_ERR_INVALID;
 }

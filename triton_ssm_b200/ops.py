@@ -175,6 +175,10 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
                   return_state=False, y=None, return_decay=False):
     """Multi-head chunked scan (``multihead_ssm_kernel.py:19-187``).
 
+    mode="diag": the reference's own diagonal state h[b,h,p]
+      (``multihead_ssm_kernel.py:19-187``): u [Bt,L,H*P]; A_log [H,P];
+      B, C [Bt,L,H,P]; dt [Bt,L,H]; D [H*P]; f32 or bf16 (u, B, C alike).
+      Returns y [Bt,L,H*P], each head's readout broadcast over its slice.
     mode="ssd": outer-product state h[b,h,p,n] on tcgen05 tensor cores.
       u [Bt,L,H*P] bf16; A_log [H] f32 (log(-A_h)); B, C [Bt,L,H,N] bf16;
       dt [Bt,L,H] f32; D [H*P] f32; h0 [Bt,H,P,N] f32 or None.
@@ -185,10 +189,14 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
     64 tokens; results do not depend on it beyond rounding).
     """
     del BLK_L
-    if mode != "ssd":
-        raise ValueError("multihead_ssm: mode %r is not available" % (mode,))
     if bdisc not in _BDISC:
         raise ValueError("multihead_ssm: bdisc must be 'euler' or 'zoh'")
+    if mode == "diag":
+        if return_state or return_decay or h0 is not None:
+            raise ValueError("multihead_ssm: mode 'diag' returns y only")
+        return _multihead_diag(u, A_log, B, C, dt, D, bdisc, y)
+    if mode != "ssd":
+        raise ValueError("multihead_ssm: mode must be 'ssd' or 'diag' (got %r)" % (mode,))
     _cuda(u, A_log, B, C, dt, D, h0)
     _need(u, (torch.bfloat16,), "u")
     _need(B, (torch.bfloat16,), "B")
@@ -381,3 +389,21 @@ def fused_interp_ssm(V, M, tau, A_log, B, C, L_q=None, q=None, dt=None, D=None, 
     if return_vhat:
         out.append(vh)
     return out[0] if len(out) == 1 else tuple(out)
+
+
+def _multihead_diag(u, A_log, B, C, dt, D, bdisc, y):
+    _cuda(u, A_log, B, C, dt, D, y)
+    _need(u, (torch.float32, torch.bfloat16), "u")
+    if B.dtype != u.dtype or C.dtype != u.dtype:
+        raise ValueError("multihead_ssm(diag): u, B, C must share a dtype")
+    Bt, L, HP = u.shape
+    nh, hd = A_log.shape
+    if nh * hd != HP or tuple(B.shape) != (Bt, L, nh, hd) or tuple(C.shape) != (Bt, L, nh, hd) or \
+            tuple(dt.shape) != (Bt, L, nh) or tuple(D.shape) != (HP,):
+        raise ValueError("multihead_ssm(diag): shape mismatch")
+    u, B, C = (t.contiguous() for t in (u, B, C))
+    A_log, dt, D = (t.float().contiguous() for t in (A_log, dt, D))
+    y = torch.empty_like(u) if y is None else y
+    call("tssm_multihead_diag", ptr(u), ptr(A_log), ptr(B), ptr(C), ptr(dt), ptr(D), ptr(y), Bt, L, nh, hd,
+         _BDISC[bdisc], dtype_code(u), stream_of(u))
+    return y
