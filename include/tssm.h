@@ -264,6 +264,15 @@ int tssm_multihead_diag(const void* u, const void* A_log, const void* B, const v
  */
 int tssm_check_device_status(tssm_stream_t stream);
 
+/*
+ * Self-test of the failure path: launches one thread that waits, with the
+ * bounded wait the pipelined kernels use, on an mbarrier phase that nothing
+ * completes; after `timeout_ns` (at most 2 s) it gives up and sets the status
+ * word, so the next tssm_check_device_status returns TSSM_ERR_TIMEOUT and the
+ * context stays usable.  No reference counterpart.
+ */
+int tssm_selftest_wait_timeout(int64_t timeout_ns, tssm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

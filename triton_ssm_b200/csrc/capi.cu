@@ -4,6 +4,7 @@
 #include <cstdio>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace tssm {
 
@@ -42,7 +43,31 @@ int* device_status_ptr() {
   return p;
 }
 
+// Self-test of the bounded-wait path: one thread waits on an mbarrier phase
+// that nothing completes, with the same helper the pipelined kernels use; the
+// wait gives up after `timeout_ns` and the code is stored in the status word.
+__global__ void wait_timeout_selftest_kernel(uint64_t timeout_ns, int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    sm100::fence_mbar_init();
+    if (!sm100::mbar_wait(&bar, 0, nullptr, timeout_ns)) atomicExch(status, 9001);
+  }
+}
+
 }  // namespace tssm
+
+extern "C" int tssm_selftest_wait_timeout(int64_t timeout_ns, tssm_stream_t stream) {
+  TSSM_REQUIRE(timeout_ns > 0 && timeout_ns <= 2000000000, "selftest_wait_timeout: timeout in (0, 2 s]");
+  int* status = tssm::device_status_ptr();
+  if (!status) {
+    tssm::set_error("selftest_wait_timeout: device status word unavailable");
+    return TSSM_ERR_CUDA;
+  }
+  tssm::wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((uint64_t)timeout_ns,
+                                                                                          status);
+  return tssm::check_launch("selftest_wait_timeout");
+}
 
 extern "C" int tssm_check_device_status(tssm_stream_t stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
