@@ -16,21 +16,25 @@
 //   MMA3  Y2   = C H^T   (H = state after the previous chunk, bf16)  (K = N)
 //   y_i = Y1_i + exp(s_i) Y2_i + D x_i ;  H <- exp(s_last) H + S   (f32 in registers)
 //
-// Warp roles (384 threads), with two chunks in flight:
-//   warp 8      producer: TMA loads of X, B, C (128B swizzle) into a STAGES-deep ring,
+// Warp roles (512 threads, one CTA per SM):
+//   warp 12     producer: TMA loads of X, B, C (128B swizzle) into a STAGES-deep ring,
 //               and, in the same non-blocking event loop, the MMA1 issue;
-//   warp 11     decay: streams dt (cp.async, STAGES-1 chunks ahead) and writes the
-//               chunk's decay prefix sums and input coefficients next to the stage;
-//   warps 9,10  MMA issuers (one thread each: MMA2+MMA4 | MMA3); issuing a
+//   warp 15     decay: streams dt (cp.async) and writes each chunk's decay prefix
+//               sums and input coefficients into a DSL-slot ring of its own, so it
+//               runs several chunks ahead of the consumers;
+//   warps 13,14 MMA issuers (one thread each: MMA4 then MMA2 | MMA3); issuing a
 //               tcgen05.mma costs the issuing thread tens of cycles, so the issue
 //               work is spread over three threads and each MMA goes out as soon as
-//               its own inputs are ready;
-//   warps 4-7   mask group: G -> M (bf16) and B -> diag(w) B, for chunk c;
-//   warps 0-3   state/epilogue group: carried state update, y (16-byte global stores).
-// G, Y1, Y2 and S are double-buffered in TMEM (8 x 64 = 512 columns), M and
-// the bf16 state tile in shared memory.  Only the state recurrence (64 FMAs per
-// thread per chunk) is serial.  Every mbarrier wait is time-bounded; a wait that
-// gives up sets the device status word and the CTA exits cleanly.
+//               its own inputs are ready (MMA4 needs only diag(w) B, not M);
+//   warps 4-7   mask group: B -> diag(w) B, then G -> M (bf16), for chunk c;
+//   warps 0-3   state group: H <- exp(s_last) H + S in registers and the bf16 copy
+//               of H for the next MMA3 -- the only serial dependence between chunks;
+//   warps 8-11  output group: y = Y1 + exp(s_i) Y2 + D x into a swizzled tile, one
+//               TMA store per chunk.
+// G, Y1, Y2 and S are double-buffered in TMEM (8 x 64 = 512 columns), M, diag(w) B,
+// the bf16 state tile and the y tile in shared memory.  Every mbarrier wait is
+// time-bounded; a wait that gives up sets the device status word and the CTA
+// exits cleanly (after its in-flight MMAs, loads and stores complete).
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -39,12 +43,22 @@
 namespace tssm {
 #ifdef TSSM_SSD_TRACE
 // Debug-only phase timestamps (clock64) of CTA (0,0): [chunk][event].
-__device__ unsigned long long g_ssd_trace[64 * 24];
+__device__ unsigned long long g_ssd_trace[64 * 32];
 #define SSD_TRACE(chunk, ev)                                                         \
   do {                                                                               \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && (chunk) < 64) g_ssd_trace[(chunk) * 24 + (ev)] = clock64(); \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (chunk) < 64) g_ssd_trace[(chunk) * 32 + (ev)] = clock64(); \
+  } while (0)
+// Debug only: spin (bounded) until the barrier phase completes, then stamp it.
+#define SSD_TRACE_DONE(bar, par, chunk, ev)                                          \
+  do {                                                                               \
+    for (int _i = 0; _i < (1 << 22) && !mbar_test((bar), (par)); ++_i) {            \
+    }                                                                                \
+    SSD_TRACE(chunk, ev);                                                            \
   } while (0)
 #else
+#define SSD_TRACE_DONE(bar, par, chunk, ev) \
+  do {                                      \
+  } while (0)
 #define SSD_TRACE(chunk, ev) \
   do {                       \
   } while (0)
@@ -55,7 +69,8 @@ using namespace sm100;
 constexpr int Q = 64;          // tokens per chunk
 constexpr int P = 64;          // head dim
 constexpr int TILE = 8192;     // bytes of a [64 x 64] bf16 tile
-constexpr int NTHREADS = 384;  // EPI 0-3, MSK 4-7, TMA+MMA1 8, MMA2+4 9, MMA3 10, decay 11
+constexpr int NTHREADS = 512;  // STATE 0-3, MSK 4-7, OUT 8-11, TMA+MMA1 12, MMA4+MMA2 13, MMA3 14, decay 15
+constexpr int DT_RING = 4;     // raw dt slots, private to the decay warp
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
 __host__ __device__ constexpr uint32_t col_g(int k) { return 0u + 64u * k; }
@@ -63,22 +78,29 @@ __host__ __device__ constexpr uint32_t col_y1(int k) { return 128u + 64u * k; }
 __host__ __device__ constexpr uint32_t col_y2(int k) { return 256u + 64u * k; }
 __host__ __device__ constexpr uint32_t col_s(int k) { return 384u + 64u * k; }
 
+// Named barriers (0 is __syncthreads).
+constexpr uint32_t BAR_STATE = 1, BAR_MSK = 2, BAR_OUT = 3;
+
 template <int NST>
 struct Layout {
   static constexpr int NB = NST / 64;                  // 64-wide blocks of B and C along n
   static constexpr int STAGE_BYTES = TILE * (1 + 2 * NB);
-  static constexpr int STAGES = NST == 64 ? 4 : 3;
+  static constexpr int STAGES = NST == 64 ? 6 : 3;     // X, B, C ring
+  static constexpr int DSL = NST == 64 ? 8 : 4;        // decay-data ring
   static constexpr int HS_BYTES = NST * 128;           // state tile: NST rows (n) x 64 p, MN-major
-  static constexpr int OFF_BH = STAGES * STAGE_BYTES;  // 2 tiles of diag(w) B (MMA4's A operand)
+  static constexpr int OFF_BH = STAGES * STAGE_BYTES;  // 2 x diag(w) B (MMA4's A operand)
   static constexpr int OFF_MT = OFF_BH + 2 * NB * TILE; // 2 mask tiles
-  static constexpr int OFF_HS = OFF_MT + 2 * TILE;     // 2 state tiles
-  static constexpr int OFF_SMALL = OFF_HS + 2 * HS_BYTES;  // per stage: s, s', w [64] + exp(s_last)
-  static constexpr int SMALL_STRIDE = 5 * 64 * 4;     // s, s', w, [e_last], raw dt
-  static constexpr int OFF_DSK = OFF_SMALL + STAGES * SMALL_STRIDE;
+  static constexpr int OFF_HS = OFF_MT + 2 * TILE;     // 2 bf16 state tiles
+  static constexpr int OFF_YS = OFF_HS + 2 * HS_BYTES; // 2 y tiles (TMA store sources)
+  static constexpr int OFF_SMALL = OFF_YS + 2 * TILE;  // per decay slot: s, v, w [64] + exp2(s_last)
+  static constexpr int SMALL_STRIDE = 224 * 4;        // s [0,72), v [72,144), w [144,208), e_last at 208
+  static constexpr int OFF_RAW = OFF_SMALL + DSL * SMALL_STRIDE;  // DT_RING x 64 raw dt
+  static constexpr int OFF_DSK = OFF_RAW + DT_RING * 64 * 4;
   static constexpr int OFF_BAR = OFF_DSK + 64 * 4;
-  static constexpr int NBAR = 2 * STAGES + 14;
+  static constexpr int NBAR = 2 * STAGES + 2 * DSL + 20 + 3;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem slot, abort flag, issued, consumed
   static constexpr int BYTES = OFF_MISC + 32 + 1024;   // + slack to align the base to 1024
+  static_assert(BYTES <= 232448, "SSD shared-memory layout exceeds the per-CTA limit");
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -98,48 +120,61 @@ __device__ __forceinline__ void unpack_bf16x8(uint4 v, float (&f)[8]) {
 template <int NST, bool ZOH>
 __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
-    const __grid_constant__ CUtensorMap tm_c, __nv_bfloat16* __restrict__ y,
+    const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_y,
     const float* __restrict__ dt, const float* __restrict__ A_log, const float* __restrict__ Dskip,
     const float* __restrict__ h0, float* __restrict__ h_last, float* __restrict__ decay_log2,
     int* __restrict__ status, int L, int H) {
   using LY = Layout<NST>;
   constexpr int NB = LY::NB;
   constexpr int ST = LY::STAGES;
+  constexpr int DSL = LY::DSL;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Offset the __shared__ array itself (no integer round trip), so the compiler
+  // keeps every access below in the shared address space (LDS/STS, not generic).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, b = blockIdx.y;
   const int nchunks = (L + Q - 1) / Q;
-  const int64_t HPtot = (int64_t)H * P;
   float* dsk = reinterpret_cast<float*>(smem + LY::OFF_DSK);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
-  uint64_t* full = bars;              // [ST]  TMA bytes + dt data
-  uint64_t* empty = bars + ST;        // [ST]  stage released by the epilogue group
-  uint64_t* gfull = bars + 2 * ST;    // [2]   MMA1 done
-  uint64_t* gfree = gfull + 2;        // [2]   G read by the mask group
-  uint64_t* mready = gfull + 4;       // [2]   M and diag(w) B written
-  uint64_t* yfull = gfull + 6;        // [2]   MMA2 + MMA4 done
-  uint64_t* hready = gfull + 8;       // [2]   bf16 state tile for the next MMA3 written
-  uint64_t* y2full = gfull + 10;      // [2]   MMA3 done
-  uint64_t* tfree = gfull + 12;       // [2]   Y1, Y2, S read by the epilogue group
+  uint64_t* full = bars;               // [ST]  TMA bytes of X, B, C landed
+  uint64_t* empty = full + ST;         // [ST]  stage released (output group)
+  uint64_t* dfull = empty + ST;        // [DSL] decay data written
+  uint64_t* dempty = dfull + DSL;      // [DSL] decay slot released (state + output groups)
+  uint64_t* gfull = dempty + DSL;      // [2]   MMA1 done
+  uint64_t* gfree = gfull + 2;         // [2]   G read by the mask group
+  uint64_t* bready = gfull + 4;        // [2]   diag(w) B written
+  uint64_t* mready = gfull + 6;        // [2]   M written
+  uint64_t* sfull = gfull + 8;         // [2]   MMA4 done
+  uint64_t* y1full = gfull + 10;       // [2]   MMA2 done (and the MMA4 before it)
+  uint64_t* y2full = gfull + 12;       // [2]   MMA3 done
+  uint64_t* sfree = gfull + 14;        // [2]   S read by the state group
+  uint64_t* yfree = gfull + 16;        // [2]   Y1, Y2 read by the output group
+  uint64_t* hready = gfull + 18;       // [2]   bf16 state tile for MMA3 written
+  uint64_t* drain = gfull + 20;        // [3]   final commit of each MMA issuer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_MISC + 4);
   int* issued = reinterpret_cast<int*>(smem + LY::OFF_MISC + 8);
   int* consumed = reinterpret_cast<int*>(smem + LY::OFF_MISC + 12);
 
   auto stage_ptr = [&](int s) { return smem + s * LY::STAGE_BYTES; };
-  auto small_ptr = [&](int s) { return reinterpret_cast<float*>(smem + LY::OFF_SMALL + s * LY::SMALL_STRIDE); };
+  auto small_ptr = [&](int d) { return reinterpret_cast<float*>(smem + LY::OFF_SMALL + d * LY::SMALL_STRIDE); };
   auto mt_ptr = [&](int k) { return smem + LY::OFF_MT + k * TILE; };
   auto bh_ptr = [&](int k) { return smem + LY::OFF_BH + k * NB * TILE; };
   auto hs_ptr = [&](int k) { return smem + LY::OFF_HS + k * LY::HS_BYTES; };
+  auto ys_ptr = [&](int k) { return smem + LY::OFF_YS + k * TILE; };
 
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
-      mbar_init(&full[s], 2);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int k = 0; k < 14; ++k) mbar_init(&gfull[k], 1);
+    for (int d = 0; d < DSL; ++d) {
+      mbar_init(&dfull[d], 1);
+      mbar_init(&dempty[d], 2);
+    }
+    for (int k = 0; k < 23; ++k) mbar_init(&gfull[k], 1);
     *abort_flag = 0;
     *issued = 0;
     *consumed = 0;
@@ -153,20 +188,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const float a = -expf(__ldg(A_log + h));
-  const float a2 = a * LOG2E;
 
   auto fail = [&](int code) {
     *abort_flag = 1;
     atomicExch(status, code);
   };
+  // Waits for this thread's own MMAs before the CTA tears down (bounded).
+  auto drain_mmas = [&](uint64_t* bar) {
+    umma_commit(bar);
+    mbar_wait(bar, 0, nullptr, 100000000ull);
+  };
 
-  if (warp == 8) {
-    // ================================================================ producer
+  if (warp == 12) {
+    // ================================================================ producer + MMA1
     if (lane == 0) {
       prefetch_tmap(&tm_x);
       prefetch_tmap(&tm_b);
       prefetch_tmap(&tm_c);
+      prefetch_tmap(&tm_y);
       constexpr uint32_t ID_KK = make_idesc_bf16(64, 64, false, false);
       int pc = 0;   // next chunk to load
       int mc = 0;   // next chunk whose MMA1 (G = C B^T) is issued
@@ -200,6 +239,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
             umma_bf16(tmem + col_g(kb), dC + ko, dB + ko, ID_KK, kk > 0);
           }
           umma_commit(&gfull[kb]);
+          SSD_TRACE(mc, 3);
+          SSD_TRACE_DONE(&gfull[kb], (mc >> 1) & 1, mc, 20);
           ++mc;
           prog = true;
         }
@@ -211,19 +252,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
             fail(1001);
             break;
           }
-          __nanosleep(32);   // leave issue slots to the compute warps on this sub-partition
+          __nanosleep(32);
         }
       }
       *issued = pc;
+      drain_mmas(&drain[0]);
     }
-  } else if (warp == 11) {
+  } else if (warp == 15) {
     // ================================================================ decay warp
-    // dt of chunk i streams into the raw-dt slot of stage i % ST with cp.async,
-    // ST-1 chunks ahead, so the per-chunk work never waits on global latency.
+    // dt streams into a private ring with cp.async, DT_RING-1 chunks ahead; the
+    // per-chunk decay data goes to its own DSL-slot ring, so this warp runs up to
+    // DSL chunks ahead of the output group.
     const float* dtp = dt + (int64_t)b * L * H + h;
+    float* raw = reinterpret_cast<float*>(smem + LY::OFF_RAW);
+    const float a = -expf(__ldg(A_log + h));
+    const float a2 = a * LOG2E;
     auto issue_dt = [&](int i) {
       if (i < nchunks) {
-        float* slot = small_ptr(i % ST) + 256;
+        float* slot = raw + (i % DT_RING) * 64;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int t = i * Q + 2 * lane + e;
@@ -237,23 +283,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    for (int i = 0; i < ST - 1; ++i) issue_dt(i);
-    float total_log2 = 0.f;   // sum over the sequence of dt*A_h*log2(e): log2 of the whole-sequence decay
+    for (int i = 0; i < DT_RING - 1; ++i) issue_dt(i);
+    float total_log2 = 0.f;   // log2 of the whole-sequence decay
     for (int c = 0; c < nchunks; ++c) {
-      const int s = c % ST, k = c / ST;
+      const int ds = c % DSL;
       int bad = 0;   // decided by lane 0, broadcast so the warp stays converged
       if (lane == 0) {
-        if (c >= ST && !mbar_wait(&empty[s], (k - 1) & 1, abort_flag)) {
+        if (c >= DSL && !mbar_wait(&dempty[ds], ((c / DSL) - 1) & 1, abort_flag)) {
           if (!*abort_flag) fail(1010);
           bad = 1;
         }
         bad |= *abort_flag;
       }
       if (__shfl_sync(0xffffffffu, bad, 0)) break;
-      issue_dt(c + ST - 1);
-      asm volatile("cp.async.wait_group %0;" ::"n"(ST - 1) : "memory");
-      if (lane == 0) SSD_TRACE(c, 12);
-      const float d0 = small_ptr(s)[256 + 2 * lane], d1 = small_ptr(s)[256 + 2 * lane + 1];
+      if (lane == 0) SSD_TRACE(c, 19);
+      issue_dt(c + DT_RING - 1);
+      asm volatile("cp.async.wait_group %0;" ::"n"(DT_RING - 1) : "memory");
+      const float* rs = raw + (c % DT_RING) * 64;
+      const float d0 = rs[2 * lane], d1 = rs[2 * lane + 1];
       // decay prefix sums (log2 domain) and input coefficients of chunk c
       const float l0 = d0 * a2, l1 = d1 * a2;
       const float pair = l0 + l1;
@@ -275,60 +322,71 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         b0 = d0;
         b1 = d1;
       }
-      // per token: s_j (log2 domain), v_j (below), and the state weight w_j = exp2(s_last - s_j) beta_j
-      float* sm = small_ptr(s);
-      sm[2 * lane] = s0;
-      sm[2 * lane + 1] = s1;
+      // per token: s_j (log2 domain), v_j (below), and the state weight w_j = exp2(s_last - s_j) beta_j;
+      // tokens 32..63 sit 4 floats further on, so the two column halves of a warp read different banks
+      float* sm = small_ptr(ds);
+      const int pad = lane >= 16 ? 4 : 0;
+      sm[2 * lane + pad] = s0;
+      sm[2 * lane + 1 + pad] = s1;
       // v_j = exp2(s_ref(j) - s_j) * beta_j with ref(j) the last token of j's 4-token
-      // sub-block: the mask entry is G_ij * exp2(s_i - s_ref(J)) * v_j (both factors bounded)
+      // sub-block: the mask entry is G_ij * exp2(s_i - s_ref(J)) * v_j
       const float sref = __shfl_sync(0xffffffffu, s1, lane | 1);
-      sm[64 + 2 * lane] = exp2f(sref - s0) * b0;
-      sm[64 + 2 * lane + 1] = exp2f(sref - s1) * b1;
-      sm[128 + 2 * lane] = exp2f(slast - s0) * b0;
-      sm[128 + 2 * lane + 1] = exp2f(slast - s1) * b1;
-      if (lane == 0) sm[192] = exp2f(slast);
-      if (lane == 0) SSD_TRACE(c, 13);
+      sm[72 + 2 * lane + pad] = exp2f(sref - s0) * b0;
+      sm[72 + 2 * lane + 1 + pad] = exp2f(sref - s1) * b1;
+      sm[144 + 2 * lane] = exp2f(slast - s0) * b0;
+      sm[144 + 2 * lane + 1] = exp2f(slast - s1) * b1;
+      if (lane == 0) sm[208] = exp2f(slast);
       __syncwarp();
       if (lane == 0) {
         SSD_TRACE(c, 1);
-        mbar_arrive(&full[s]);
+        mbar_arrive(&dfull[ds]);
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");   // no copy may outlive the loop
     if (decay_log2 && lane == 0 && !*abort_flag) decay_log2[(int64_t)b * H + h] = total_log2;
-  } else if (warp == 9) {
-    // ================================================================ MMA2 + MMA4 issuer
+  } else if (warp == 13) {
+    // ================================================================ MMA4 + MMA2 issuer
     if (lane == 0) {
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
       constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
-        if (!mbar_wait(&mready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1004); break; }
-        if (k >= 2 && !mbar_wait(&tfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1005); break; }
-        mbar_wait(&full[s], (k / ST) & 1);
+        if (!mbar_wait(&bready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1004); break; }
+        if (k >= 2 && !mbar_wait(&sfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1005); break; }
+        if (!mbar_wait(&full[s], (k / ST) & 1, abort_flag)) { if (!*abort_flag) fail(1014); break; }
         tc_fence_after();
-        SSD_TRACE(k, 3);
+        SSD_TRACE(k, 8);
         const uint32_t X = smem_u32(stage_ptr(s));
-        const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
         const uint64_t dX = make_desc_sw128(X, TILE), dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_y1(kb), dM + 2 * kk, dX + 128 * kk, ID_KM, kk > 0);
-#pragma unroll
         for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_s(kb), dBh + 128 * kk, dX + 128 * kk, ID_MM, kk > 0);
-        umma_commit(&yfull[kb]);
+        umma_commit(&sfull[kb]);
+        SSD_TRACE(k, 9);
+        SSD_TRACE_DONE(&sfull[kb], (k >> 1) & 1, k, 21);
+        if (!mbar_wait(&mready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1015); break; }
+        if (k >= 2 && !mbar_wait(&yfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1016); break; }
+        tc_fence_after();
+        SSD_TRACE(k, 10);
+        const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_y1(kb), dM + 2 * kk, dX + 128 * kk, ID_KM, kk > 0);
+        umma_commit(&y1full[kb]);
+        SSD_TRACE(k, 11);
+        SSD_TRACE_DONE(&y1full[kb], (k >> 1) & 1, k, 22);
       }
+      drain_mmas(&drain[1]);
     }
-  } else if (warp == 10) {
+  } else if (warp == 14) {
     // ================================================================ MMA3 issuer
     if (lane == 0) {
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
         if (!mbar_wait(&hready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1006); break; }
-        if (k >= 2 && !mbar_wait(&tfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1011); break; }
+        if (k >= 2 && !mbar_wait(&yfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1011); break; }
         if (!mbar_wait(&full[s], (k / ST) & 1, abort_flag)) { if (!*abort_flag) fail(1012); break; }
         tc_fence_after();
-        SSD_TRACE(k, 4);
+        SSD_TRACE(k, 12);
         const uint64_t dC = make_desc_sw128(smem_u32(stage_ptr(s)) + TILE * (1 + NB), 16);
         const uint64_t dH = make_desc_sw128(smem_u32(hs_ptr(kb)), TILE);
 #pragma unroll
@@ -337,9 +395,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
           umma_bf16(tmem + col_y2(kb), dC + ko, dH + 128 * kk, ID_KM, kk > 0);
         }
         umma_commit(&y2full[kb]);
+        SSD_TRACE(k, 13);
+        SSD_TRACE_DONE(&y2full[kb], (k >> 1) & 1, k, 23);
       }
+      drain_mmas(&drain[2]);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && warp < 8) {
     // ================================================================ mask group
     const int t = tid - 128;
     const int w = warp - 4;
@@ -347,19 +408,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const int half = lane >> 4;             // which 32 columns
     const uint32_t lane_base = (uint32_t)(w * 32) << 16;
     for (int c = 0; c < nchunks; ++c) {
-      const int s = c % ST, kb = c & 1;
-      // (1) tiles and decay data of chunk c landed; M and diag(w)B buffers of chunk c-2 released
+      const int s = c % ST, kb = c & 1, ds = c % DSL;
+      // (1) B tile and decay data of chunk c landed; diag(w)B buffer free (MMA4 of chunk c-2 done)
       bool bad = false;
       if (t == 0) {
-        bad = !mbar_wait(&full[s], (c / ST) & 1, abort_flag) ||
-              (c >= 2 && !mbar_wait(&yfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
+        bad = !mbar_wait(&full[s], (c / ST) & 1, abort_flag) || !mbar_wait(&dfull[ds], (c / DSL) & 1, abort_flag) ||
+              (c >= 2 && !mbar_wait(&sfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
         if (bad && !*abort_flag) fail(1007);
       }
-      if (named_bar_or(2, 128, bad)) break;
+      if (named_bar_or(BAR_MSK, 128, bad)) break;
       mbar_wait(&full[s], (c / ST) & 1);
-      const float* sm = small_ptr(s);
+      mbar_wait(&dfull[ds], (c / DSL) & 1);
+      if (t == 0) SSD_TRACE(c, 4);
+      const float* sm = small_ptr(ds);
       const uint8_t* Bt = stage_ptr(s) + TILE;
-      // (2) diag(w) B into its own tile (bf16x2 arithmetic); overlaps MMA1, which reads B
+      // (2) diag(w) B into its own tile (bf16x2 arithmetic)
       {
         uint8_t* Bh = bh_ptr(kb);
 #pragma unroll
@@ -367,7 +430,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
 #pragma unroll
           for (int it = 0; it < 4; ++it) {
             const int idx = t + it * 128;            // 16-byte chunk; row j = idx / 8
-            const __nv_bfloat162 w2 = __float2bfloat162_rn(sm[128 + (idx >> 3)]);
+            const __nv_bfloat162 w2 = __float2bfloat162_rn(sm[144 + (idx >> 3)]);
             uint4 v = *reinterpret_cast<const uint4*>(Bt + nb * TILE + idx * 16);
             __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v);
             hv[0] = __hmul2(hv[0], w2);
@@ -378,30 +441,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
           }
         }
       }
-      // (3) G of chunk c
+      fence_proxy_async_smem();
+      named_bar_sync(BAR_MSK, 128);
       if (t == 0) {
-        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
-        SSD_TRACE(c, 14);
+        SSD_TRACE(c, 5);
+        mbar_arrive(&bready[kb]);
+      }
+      // (3) G of chunk c; mask buffer free (MMA2 of chunk c-2 done)
+      if (t == 0) {
+        SSD_TRACE(c, 24);
+        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag);
+        SSD_TRACE(c, 25);
+        bad = bad || (c >= 2 && !mbar_wait(&y1full[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
+        SSD_TRACE(c, 26);
         if (bad && !*abort_flag) fail(1013);
       }
-      if (named_bar_or(2, 128, bad)) break;
-      if (t == 0) SSD_TRACE(c, 5);
-      mbar_wait(&gfull[kb], (c >> 1) & 1);
+      if (named_bar_or(BAR_MSK, 128, bad)) break;
+      if (t == 0) SSD_TRACE(c, 6);
       tc_fence_after();
       // (4) M row `row`, columns [32*half, 32*half+32):
       //     M_ij = G_ij * exp2(s_i - s_ref(J)) * v_j for j <= i (J = 4-token sub-block of j)
       float g[32];
       tmem_ld16x2_32(tmem + lane_base + col_g(kb), g);
       {
-        const float si = sm[row];
-        const float4* vv = reinterpret_cast<const float4*>(sm + 64 + half * 32);
+        const float si = sm[row + (row >= 32 ? 4 : 0)];
+        const float4* vv = reinterpret_cast<const float4*>(sm + 72 + half * 36);
         const int nvalid = row - half * 32;      // columns jj <= nvalid are kept
         float u[8];
 #pragma unroll
-        for (int J = 0; J < 8; ++J) u[J] = fast_exp2(si - sm[half * 32 + 4 * J + 3]);
+        for (int J = 0; J < 8; ++J) u[J] = fast_exp2(si - sm[half * 36 + 4 * J + 3]);
         uint8_t* Mt = mt_ptr(kb);
         tmem_wait_ld();
-        if (t == 0) SSD_TRACE(c, 15);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float4 va = vv[2 * q], vb = vv[2 * q + 1];
@@ -418,22 +488,85 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
                          pack_bf16x2(m[6], m[7]));
         }
       }
-      if (t == 0) SSD_TRACE(c, 16);
       fence_proxy_async_smem();
       tc_fence_before();
-      named_bar_sync(2, 128);
+      named_bar_sync(BAR_MSK, 128);
       if (t == 0) {
-        SSD_TRACE(c, 6);
+        SSD_TRACE(c, 7);
         mbar_arrive(&gfree[kb]);
         mbar_arrive(&mready[kb]);
       }
     }
-  } else {
-    // ================================================================ state / epilogue group
-    const int w = warp;
+  } else if (warp >= 8) {
+    // ================================================================ output group (warps 8-11)
+    const int t = tid - 256;
+    const int w = warp - 8;
     const int half = lane >> 4;
     const int row = w * 16 + (lane & 15);   // token row of Y1/Y2 (M=64 layout)
     const uint32_t lane_base = (uint32_t)(w * 32) << 16;
+    int c = 0;
+    for (; c < nchunks; ++c) {
+      const int s = c % ST, kb = c & 1, ds = c % DSL;
+      bool bad = false;
+      if (t == 0) {
+        if (c >= 2) bulk_wait_read<1>();   // the store of chunk c-2 has left y tile kb
+        bad = !mbar_wait(&y1full[kb], (c >> 1) & 1, abort_flag) || !mbar_wait(&y2full[kb], (c >> 1) & 1, abort_flag) ||
+              !mbar_wait(&full[s], (c / ST) & 1, abort_flag) || !mbar_wait(&dfull[ds], (c / DSL) & 1, abort_flag) ||
+              *abort_flag;
+        if (bad && !*abort_flag) fail(1009);
+      }
+      if (named_bar_or(BAR_OUT, 128, bad)) break;
+      mbar_wait(&full[s], (c / ST) & 1);
+      mbar_wait(&dfull[ds], (c / DSL) & 1);
+      if (t == 0) SSD_TRACE(c, 16);
+      tc_fence_after();
+      float y1[32], y2[32];
+      tmem_ld16x2_32(tmem + lane_base + col_y1(kb), y1);
+      tmem_ld16x2_32(tmem + lane_base + col_y2(kb), y2);
+      const float ei = exp2f(small_ptr(ds)[row + (row >= 32 ? 4 : 0)]);
+      const uint8_t* X = stage_ptr(s);
+      uint8_t* Ys = ys_ptr(kb);
+      tmem_wait_ld();
+      if (t == 0) SSD_TRACE(c, 17);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int cc = half * 4 + q;
+        float xf[8];
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(X + sw128_chunk(row, cc)), xf);
+        const float4 da = *reinterpret_cast<const float4*>(dsk + cc * 8);
+        const float4 db = *reinterpret_cast<const float4*>(dsk + cc * 8 + 4);
+        const float d8[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+        uint32_t w4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int jj = q * 8 + 2 * e;
+          const float o0 = y1[jj] + ei * y2[jj] + d8[2 * e] * xf[2 * e];
+          const float o1 = y1[jj + 1] + ei * y2[jj + 1] + d8[2 * e + 1] * xf[2 * e + 1];
+          w4[e] = pack_bf16x2(o0, o1);
+        }
+        *reinterpret_cast<uint4*>(Ys + sw128_chunk(row, cc)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+      fence_proxy_async_smem();   // y tile -> visible to the TMA store
+      tc_fence_before();
+      named_bar_sync(BAR_OUT, 128);
+      if (t == 0) {
+        tma_store_3d(&tm_y, Ys, h * P, c * Q, b);   // rows past L are clipped by the tensor map
+        bulk_commit();
+        SSD_TRACE(c, 18);
+        mbar_arrive(&yfree[kb]);
+        mbar_arrive(&empty[s]);
+        mbar_arrive(&dempty[ds]);
+      }
+    }
+    if (t == 0) {
+      bulk_wait<0>();   // every y store complete before the CTA exits
+      *consumed = c;
+    }
+  } else {
+    // ================================================================ state group (warps 0-3)
+    const int half = lane >> 4;
+    const int row = warp * 16 + (lane & 15);
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     // State ownership: NST=64 -> S^T row n = row, p in [32*half, +32);  NST=128 -> n = tid, all p.
     constexpr int HP = NST == 64 ? 32 : 64;
     const int n_own = NST == 64 ? row : tid;
@@ -460,39 +593,36 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     };
     write_hs(hs_ptr(0));
     fence_proxy_async_smem();
-    named_bar_sync(1, 128);
+    named_bar_sync(BAR_STATE, 128);
     if (tid == 0) mbar_arrive(&hready[0]);
-    int c = 0;
-    for (; c < nchunks; ++c) {
-      const int s = c % ST, kb = c & 1;
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const int kb = c & 1, ds = c % DSL;
+      // S of chunk c, its decay data, and state tile (c+1)&1 no longer read (MMA3 of chunk c-1 done)
       bool bad = false;
       if (tid == 0) {
-        bad = !mbar_wait(&yfull[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
-        SSD_TRACE(c, 17);
+        bad = !mbar_wait(&sfull[kb], (c >> 1) & 1, abort_flag) || !mbar_wait(&dfull[ds], (c / DSL) & 1, abort_flag) ||
+              (c >= 1 && !mbar_wait(&y2full[(c - 1) & 1], ((c - 1) >> 1) & 1, abort_flag)) || *abort_flag;
         if (bad && !*abort_flag) fail(1008);
       }
-      if (named_bar_or(1, 128, bad)) break;
-      if (tid == 0) SSD_TRACE(c, 7);
-      mbar_wait(&full[s], (c / ST) & 1);
-      mbar_wait(&yfull[kb], (c >> 1) & 1);
+      if (named_bar_or(BAR_STATE, 128, bad)) {
+        ok = false;
+        break;
+      }
+      mbar_wait(&dfull[ds], (c / DSL) & 1);
+      if (tid == 0) SSD_TRACE(c, 14);
       tc_fence_after();
-      const float* sm = small_ptr(s);
-      const float e_last = sm[192];
-      // ---- carried state: H <- exp(s_last) H + S ; bf16 copy for MMA3 of chunk c+1.
-      // Y1 (ready together with S) is fetched in the same TMEM round trip.
-      float y1[32];
+      const float e_last = small_ptr(ds)[208];
+      // H <- exp(s_last) H + S ; bf16 copy for MMA3 of chunk c+1
       if (NST == 64) {
         float sv[32];
         tmem_ld16x2_32(tmem + lane_base + col_s(kb), sv);
-        tmem_ld16x2_32(tmem + lane_base + col_y1(kb), y1);
         tmem_wait_ld();
-        if (tid == 0) SSD_TRACE(c, 18);
 #pragma unroll
         for (int j = 0; j < 32; ++j) hreg[j] = e_last * hreg[j] + sv[j];
       } else {
         float sv[32];
         tmem_ld32(tmem + lane_base + col_s(kb), sv);
-        tmem_ld16x2_32(tmem + lane_base + col_y1(kb), y1);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 32; ++j) hreg[j] = e_last * hreg[j] + sv[j];
@@ -503,58 +633,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       }
       write_hs(hs_ptr((c + 1) & 1));
       fence_proxy_async_smem();
-      named_bar_sync(1, 128);
-      if (tid == 0) {
-        SSD_TRACE(c, 8);
-        mbar_arrive(&hready[(c + 1) & 1]);
-      }
-      // ---- output rows
-      if (tid == 0) {
-        bad = !mbar_wait(&y2full[kb], (c >> 1) & 1, abort_flag) || *abort_flag;
-        if (bad && !*abort_flag) fail(1009);
-      }
-      if (named_bar_or(1, 128, bad)) break;
-      if (tid == 0) SSD_TRACE(c, 9);
-      mbar_wait(&y2full[kb], (c >> 1) & 1);
-      tc_fence_after();
-      {
-        float y2[32];
-        tmem_ld16x2_32(tmem + lane_base + col_y2(kb), y2);
-        const float ei = exp2f(sm[row]);
-        const uint8_t* X = stage_ptr(s);
-        const int tok = c * Q + row;
-        uint4* dst = reinterpret_cast<uint4*>(y + ((int64_t)b * L + tok) * HPtot + h * P + half * 32);
-        tmem_wait_ld();
-        if (tid == 0) SSD_TRACE(c, 19);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int cc = half * 4 + q;
-          float xf[8];
-          unpack_bf16x8(*reinterpret_cast<const uint4*>(X + sw128_chunk(row, cc)), xf);
-          const float4 da = *reinterpret_cast<const float4*>(dsk + cc * 8);
-          const float4 db = *reinterpret_cast<const float4*>(dsk + cc * 8 + 4);
-          const float d8[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
-          uint32_t w4[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int jj = q * 8 + 2 * e;
-            const float o0 = y1[jj] + ei * y2[jj] + d8[2 * e] * xf[2 * e];
-            const float o1 = y1[jj + 1] + ei * y2[jj + 1] + d8[2 * e + 1] * xf[2 * e + 1];
-            w4[e] = pack_bf16x2(o0, o1);
-          }
-          if (tok < L) dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-        }
-      }
       tc_fence_before();
-      named_bar_sync(1, 128);
+      named_bar_sync(BAR_STATE, 128);
       if (tid == 0) {
-        SSD_TRACE(c, 10);
-        mbar_arrive(&tfree[kb]);
-        mbar_arrive(&empty[s]);
+        SSD_TRACE(c, 15);
+        mbar_arrive(&sfree[kb]);
+        mbar_arrive(&hready[(c + 1) & 1]);
+        mbar_arrive(&dempty[ds]);
       }
     }
-    if (tid == 0) *consumed = c;
-    if (h_last && !*abort_flag) {
+    if (ok && h_last && !*abort_flag) {
       float* dst = h_last + (((int64_t)b * H + h) * P) * NST + n_own;
 #pragma unroll
       for (int j = 0; j < HP; ++j) dst[(int64_t)(p0 + j) * NST] = hreg[j];
@@ -600,7 +688,7 @@ bool map3d_bf16(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint
 }
 
 template <int NST, bool ZOH>
-int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& mc, __nv_bfloat16* y,
+int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& my,
                const float* dt, const float* A_log, const float* Dskip, const float* h0, float* h_last,
                float* decay_log2, int64_t Bsz, int64_t L, int64_t H, cudaStream_t st) {
   constexpr int bytes = Layout<NST>::BYTES;
@@ -614,7 +702,7 @@ int launch_ssd(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& 
     return TSSM_ERR_CUDA;
   }
   dim3 grid((unsigned)H, (unsigned)Bsz);
-  kern<<<grid, NTHREADS, bytes, st>>>(mx, mb, mc, y, dt, A_log, Dskip, h0, h_last, decay_log2, status, (int)L,
+  kern<<<grid, NTHREADS, bytes, st>>>(mx, mb, mc, my, dt, A_log, Dskip, h0, h_last, decay_log2, status, (int)L,
                                       (int)H);
   return check_launch("ssd_chunk_scan");
 }
@@ -637,10 +725,11 @@ extern "C" int tssm_multihead_ssd(const void* x, const void* dt, const void* A_l
                "multihead_ssd: x, B, C, y must be 16-byte aligned");
   TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31) && H * N < (int64_t(1) << 31),
                "multihead_ssd: size out of range");
-  CUtensorMap mx, mb, mc;
+  CUtensorMap mx, mb, mc, mo;
   if (!map3d_bf16(&mx, x, (uint64_t)(H * P), (uint64_t)L, (uint64_t)Bsz) ||
       !map3d_bf16(&mb, B, (uint64_t)(H * N), (uint64_t)L, (uint64_t)Bsz) ||
-      !map3d_bf16(&mc, C, (uint64_t)(H * N), (uint64_t)L, (uint64_t)Bsz)) {
+      !map3d_bf16(&mc, C, (uint64_t)(H * N), (uint64_t)L, (uint64_t)Bsz) ||
+      !map3d_bf16(&mo, y, (uint64_t)(H * P), (uint64_t)L, (uint64_t)Bsz)) {
     set_error("multihead_ssd: cuTensorMapEncodeTiled failed");
     return TSSM_ERR_CUDA;
   }
@@ -651,17 +740,16 @@ extern "C" int tssm_multihead_ssd(const void* x, const void* dt, const void* A_l
   const float* hi = (const float*)h0;
   float* ho = (float*)h_last;
   float* dl = (float*)decay_log2;
-  __nv_bfloat16* my = (__nv_bfloat16*)y;
   if (N == 64)
-    return bdisc ? launch_ssd<64, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st)
-                 : launch_ssd<64, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st);
-  return bdisc ? launch_ssd<128, true>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st)
-               : launch_ssd<128, false>(mx, mb, mc, my, dtp, al, dk, hi, ho, dl, Bsz, L, H, st);
+    return bdisc ? launch_ssd<64, true>(mx, mb, mc, mo, dtp, al, dk, hi, ho, dl, Bsz, L, H, st)
+                 : launch_ssd<64, false>(mx, mb, mc, mo, dtp, al, dk, hi, ho, dl, Bsz, L, H, st);
+  return bdisc ? launch_ssd<128, true>(mx, mb, mc, mo, dtp, al, dk, hi, ho, dl, Bsz, L, H, st)
+               : launch_ssd<128, false>(mx, mb, mc, mo, dtp, al, dk, hi, ho, dl, Bsz, L, H, st);
 }
 
 #ifdef TSSM_SSD_TRACE
 extern "C" int tssm_debug_read_ssd_trace(unsigned long long* out, int n) {
-  return cudaMemcpyFromSymbol(out, tssm::g_ssd_trace, sizeof(unsigned long long) * (n < 1536 ? n : 1536)) ==
+  return cudaMemcpyFromSymbol(out, tssm::g_ssd_trace, sizeof(unsigned long long) * (n < 2048 ? n : 2048)) ==
                  cudaSuccess ? 0 : 3;
 }
 #endif

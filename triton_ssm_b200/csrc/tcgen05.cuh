@@ -26,14 +26,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// try_wait with a suspend-time hint: the waiting thread sleeps (instead of
+// re-polling shared memory) until the phase completes or ~hint_ns pass.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 1000000u) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
@@ -56,18 +58,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 // Bounded wait on an mbarrier phase: gives up after `timeout_ns` of wall time
 // (or as soon as *abort becomes non-zero) and returns false so the caller can
-// report a timeout instead of hanging the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort = nullptr,
-                                          uint64_t timeout_ns = 2000000000ull) {
-  if (mbar_try_wait(bar, parity)) return true;
+// report a timeout instead of hanging the GPU.  The polling loop is kept out of
+// line: kernels with many wait sites stay small enough for the instruction cache.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, const volatile int* abort,
+                                            uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
+  const uint32_t hint = timeout_ns < 1000000ull ? (uint32_t)timeout_ns : 1000000u;
   for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity, hint)) return true;
     if (abort && *abort) return false;
     if (globaltimer_ns() - t0 > timeout_ns) return false;
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort = nullptr,
+                                          uint64_t timeout_ns = 2000000000ull) {
+  if (mbar_test(bar, parity)) return true;   // cheap when the phase has already completed
+  return mbar_wait_slow(bar, parity, abort, timeout_ns);
 }
 
 // 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22,
