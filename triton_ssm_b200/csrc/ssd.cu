@@ -351,9 +351,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
-        if (!mbar_wait(&bready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1004); break; }
-        if (k >= 2 && !mbar_wait(&sfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1005); break; }
-        if (!mbar_wait(&full[s], (k / ST) & 1, abort_flag)) { if (!*abort_flag) fail(1014); break; }
+        if (!mbar_wait_n(abort_flag, &bready[kb], (k >> 1) & 1, k >= 2 ? &sfree[kb] : nullptr, ((k - 2) >> 1) & 1,
+                         &full[s], (k / ST) & 1)) {
+          if (!*abort_flag) fail(1004);
+          break;
+        }
         tc_fence_after();
         SSD_TRACE(k, 8);
         const uint32_t X = smem_u32(stage_ptr(s));
@@ -363,8 +365,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         umma_commit(&sfull[kb]);
         SSD_TRACE(k, 9);
         SSD_TRACE_DONE(&sfull[kb], (k >> 1) & 1, k, 21);
-        if (!mbar_wait(&mready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1015); break; }
-        if (k >= 2 && !mbar_wait(&yfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1016); break; }
+        if (!mbar_wait_n(abort_flag, &mready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1)) {
+          if (!*abort_flag) fail(1015);
+          break;
+        }
         tc_fence_after();
         SSD_TRACE(k, 10);
         const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
@@ -382,9 +386,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
-        if (!mbar_wait(&hready[kb], (k >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1006); break; }
-        if (k >= 2 && !mbar_wait(&yfree[kb], ((k - 2) >> 1) & 1, abort_flag)) { if (!*abort_flag) fail(1011); break; }
-        if (!mbar_wait(&full[s], (k / ST) & 1, abort_flag)) { if (!*abort_flag) fail(1012); break; }
+        if (!mbar_wait_n(abort_flag, &hready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1,
+                         &full[s], (k / ST) & 1)) {
+          if (!*abort_flag) fail(1006);
+          break;
+        }
         tc_fence_after();
         SSD_TRACE(k, 12);
         const uint64_t dC = make_desc_sw128(smem_u32(stage_ptr(s)) + TILE * (1 + NB), 16);
@@ -410,15 +416,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % ST, kb = c & 1, ds = c % DSL;
       // (1) B tile and decay data of chunk c landed; diag(w)B buffer free (MMA4 of chunk c-2 done)
-      bool bad = false;
-      if (t == 0) {
-        bad = !mbar_wait(&full[s], (c / ST) & 1, abort_flag) || !mbar_wait(&dfull[ds], (c / DSL) & 1, abort_flag) ||
-              (c >= 2 && !mbar_wait(&sfull[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
-        if (bad && !*abort_flag) fail(1007);
-      }
+      // every thread observes the phases itself (TMA data visibility); one uniform decision
+      bool bad = !mbar_wait_n(abort_flag, &full[s], (c / ST) & 1, &dfull[ds], (c / DSL) & 1,
+                              c >= 2 ? &sfull[kb] : nullptr, ((c - 2) >> 1) & 1);
+      if (bad && !*abort_flag) fail(1007);
       if (named_bar_or(BAR_MSK, 128, bad)) break;
-      mbar_wait(&full[s], (c / ST) & 1);
-      mbar_wait(&dfull[ds], (c / DSL) & 1);
       if (t == 0) SSD_TRACE(c, 4);
       const float* sm = small_ptr(ds);
       const uint8_t* Bt = stage_ptr(s) + TILE;
@@ -448,14 +450,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         mbar_arrive(&bready[kb]);
       }
       // (3) G of chunk c; mask buffer free (MMA2 of chunk c-2 done)
-      if (t == 0) {
-        SSD_TRACE(c, 24);
-        bad = !mbar_wait(&gfull[kb], (c >> 1) & 1, abort_flag);
-        SSD_TRACE(c, 25);
-        bad = bad || (c >= 2 && !mbar_wait(&y1full[kb], ((c - 2) >> 1) & 1, abort_flag)) || *abort_flag;
-        SSD_TRACE(c, 26);
-        if (bad && !*abort_flag) fail(1013);
-      }
+      bad = !mbar_wait_n(abort_flag, &gfull[kb], (c >> 1) & 1, c >= 2 ? &y1full[kb] : nullptr, ((c - 2) >> 1) & 1);
+      if (bad && !*abort_flag) fail(1013);
       if (named_bar_or(BAR_MSK, 128, bad)) break;
       if (t == 0) SSD_TRACE(c, 6);
       tc_fence_after();
@@ -478,10 +474,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
           const float v8[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
           float m[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
+          for (int e = 0; e < 8; e += 2) {
             const int jj = q * 8 + e;
-            const float val = (g[jj] * u[jj >> 2]) * v8[e];
-            m[e] = jj <= nvalid ? val : 0.f;
+            const float uu = u[jj >> 2];
+            const float2 val = fmul2(fmul2(make_float2(g[jj], g[jj + 1]), make_float2(uu, uu)), make_float2(v8[e], v8[e + 1]));
+            m[e] = jj <= nvalid ? val.x : 0.f;
+            m[e + 1] = jj + 1 <= nvalid ? val.y : 0.f;
           }
           *reinterpret_cast<uint4*>(Mt + sw128_chunk(row, half * 4 + q)) =
               make_uint4(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]), pack_bf16x2(m[4], m[5]),
@@ -507,17 +505,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     int c = 0;
     for (; c < nchunks; ++c) {
       const int s = c % ST, kb = c & 1, ds = c % DSL;
-      bool bad = false;
-      if (t == 0) {
-        if (c >= 2) bulk_wait_read<1>();   // the store of chunk c-2 has left y tile kb
-        bad = !mbar_wait(&y1full[kb], (c >> 1) & 1, abort_flag) || !mbar_wait(&y2full[kb], (c >> 1) & 1, abort_flag) ||
-              !mbar_wait(&full[s], (c / ST) & 1, abort_flag) || !mbar_wait(&dfull[ds], (c / DSL) & 1, abort_flag) ||
-              *abort_flag;
-        if (bad && !*abort_flag) fail(1009);
-      }
+      if (t == 0 && c >= 2) bulk_wait_read<1>();   // the store of chunk c-2 has left y tile kb
+      bool bad = !mbar_wait_n(abort_flag, &y1full[kb], (c >> 1) & 1, &y2full[kb], (c >> 1) & 1, &full[s],
+                              (c / ST) & 1, &dfull[ds], (c / DSL) & 1);
+      if (bad && !*abort_flag) fail(1009);
       if (named_bar_or(BAR_OUT, 128, bad)) break;
-      mbar_wait(&full[s], (c / ST) & 1);
-      mbar_wait(&dfull[ds], (c / DSL) & 1);
       if (t == 0) SSD_TRACE(c, 16);
       tc_fence_after();
       float y1[32], y2[32];
@@ -540,9 +532,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int jj = q * 8 + 2 * e;
-          const float o0 = y1[jj] + ei * y2[jj] + d8[2 * e] * xf[2 * e];
-          const float o1 = y1[jj + 1] + ei * y2[jj + 1] + d8[2 * e + 1] * xf[2 * e + 1];
-          w4[e] = pack_bf16x2(o0, o1);
+          // (y1 + ei*y2) + d*x, two tokens' columns per packed instruction
+          const float2 t2 = ffma2(make_float2(ei, ei), make_float2(y2[jj], y2[jj + 1]), make_float2(y1[jj], y1[jj + 1]));
+          const float2 o = ffma2(make_float2(d8[2 * e], d8[2 * e + 1]), make_float2(xf[2 * e], xf[2 * e + 1]), t2);
+          w4[e] = pack_bf16x2(o.x, o.y);
         }
         *reinterpret_cast<uint4*>(Ys + sw128_chunk(row, cc)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
@@ -599,17 +592,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     for (int c = 0; c < nchunks; ++c) {
       const int kb = c & 1, ds = c % DSL;
       // S of chunk c, its decay data, and state tile (c+1)&1 no longer read (MMA3 of chunk c-1 done)
-      bool bad = false;
-      if (tid == 0) {
-        bad = !mbar_wait(&sfull[kb], (c >> 1) & 1, abort_flag) || !mbar_wait(&dfull[ds], (c / DSL) & 1, abort_flag) ||
-              (c >= 1 && !mbar_wait(&y2full[(c - 1) & 1], ((c - 1) >> 1) & 1, abort_flag)) || *abort_flag;
-        if (bad && !*abort_flag) fail(1008);
-      }
+      const bool bad = !mbar_wait_n(abort_flag, &sfull[kb], (c >> 1) & 1, &dfull[ds], (c / DSL) & 1,
+                                    c >= 1 ? &y2full[(c - 1) & 1] : nullptr, ((c - 1) >> 1) & 1);
+      if (bad && !*abort_flag) fail(1008);
       if (named_bar_or(BAR_STATE, 128, bad)) {
         ok = false;
         break;
       }
-      mbar_wait(&dfull[ds], (c / DSL) & 1);
       if (tid == 0) SSD_TRACE(c, 14);
       tc_fence_after();
       const float e_last = small_ptr(ds)[208];
@@ -618,8 +607,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         float sv[32];
         tmem_ld16x2_32(tmem + lane_base + col_s(kb), sv);
         tmem_wait_ld();
+        const float2 e2 = make_float2(e_last, e_last);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) hreg[j] = e_last * hreg[j] + sv[j];
+        for (int j = 0; j < 32; j += 2) {
+          const float2 r = ffma2(e2, make_float2(hreg[j], hreg[j + 1]), make_float2(sv[j], sv[j + 1]));
+          hreg[j] = r.x;
+          hreg[j + 1] = r.y;
+        }
       } else {
         float sv[32];
         tmem_ld32(tmem + lane_base + col_s(kb), sv);

@@ -76,6 +76,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   return mbar_wait_slow(bar, parity, abort, timeout_ns);
 }
 
+// Waits for up to four barrier phases (null entries are skipped).  The
+// non-blocking tests are issued back to back, so when every phase has already
+// completed the cost is one round trip rather than one per barrier.
+__device__ __forceinline__ bool mbar_wait_n(const volatile int* abort, uint64_t* b0, uint32_t p0,
+                                            uint64_t* b1 = nullptr, uint32_t p1 = 0, uint64_t* b2 = nullptr,
+                                            uint32_t p2 = 0, uint64_t* b3 = nullptr, uint32_t p3 = 0,
+                                            uint64_t timeout_ns = 2000000000ull) {
+  const bool r = mbar_test(b0, p0) & (!b1 || mbar_test(b1, p1)) & (!b2 || mbar_test(b2, p2)) &
+                 (!b3 || mbar_test(b3, p3));
+  if (r) return true;
+  return mbar_wait_slow(b0, p0, abort, timeout_ns) && (!b1 || mbar_wait_slow(b1, p1, abort, timeout_ns)) &&
+         (!b2 || mbar_wait_slow(b2, p2, abort, timeout_ns)) && (!b3 || mbar_wait_slow(b3, p3, abort, timeout_ns));
+}
+
 // 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22,
 // flushes subnormal results to zero); used where results feed bf16 operands.
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -224,6 +238,26 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint6
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Whole-warp forms: every lane of a converged warp executes them and elect.sync
+// picks one lane (the same one each time) to issue, so descriptors computed by
+// the warp stay warp-uniform and the issue path is shorter than from a lane-0 branch.
+__device__ __forceinline__ void umma_bf16_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
       : "memory");
 }
 // Arrive once on `bar` when every previously issued tcgen05.mma of this thread completes.
