@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   uint64_t* sfull = gfull + 8;         // [2]   MMA4 done
   uint64_t* y1full = gfull + 10;       // [2]   MMA2 done (and the MMA4 before it)
   uint64_t* y2full = gfull + 12;       // [2]   MMA3 done
-  uint64_t* sfree = gfull + 14;        // [2]   S read by the state group
+  // gfull + 14, + 15: spare
   uint64_t* yfree = gfull + 16;        // [2]   Y1, Y2 read by the output group
   uint64_t* hready = gfull + 18;       // [2]   bf16 state tile for MMA3 written
   uint64_t* drain = gfull + 20;        // [3]   final commit of each MMA issuer
@@ -351,8 +351,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
-        if (!mbar_wait_n(abort_flag, &bready[kb], (k >> 1) & 1, k >= 2 ? &sfree[kb] : nullptr, ((k - 2) >> 1) & 1,
-                         &full[s], (k / ST) & 1)) {
+        // bready(k) also means S of chunk k-2 was consumed (the state group writes diag(w) B
+        // of chunk k after reading S of chunk k-2), so accumulator c&1 is free
+        if (!mbar_wait_n(abort_flag, &bready[kb], (k >> 1) & 1, &full[s], (k / ST) & 1)) {
           if (!*abort_flag) fail(1004);
           break;
         }
@@ -414,48 +415,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const int half = lane >> 4;             // which 32 columns
     const uint32_t lane_base = (uint32_t)(w * 32) << 16;
     for (int c = 0; c < nchunks; ++c) {
-      const int s = c % ST, kb = c & 1, ds = c % DSL;
-      // (1) B tile and decay data of chunk c landed; diag(w)B buffer free (MMA4 of chunk c-2 done)
-      // every thread observes the phases itself (TMA data visibility); one uniform decision
-      bool bad = !mbar_wait_n(abort_flag, &full[s], (c / ST) & 1, &dfull[ds], (c / DSL) & 1,
-                              c >= 2 ? &sfull[kb] : nullptr, ((c - 2) >> 1) & 1);
+      const int kb = c & 1, ds = c % DSL;
+      // G of chunk c, its decay data, and mask buffer c&1 free (MMA2 of chunk c-2 done)
+      const bool bad = !mbar_wait_n(abort_flag, &gfull[kb], (c >> 1) & 1, &dfull[ds], (c / DSL) & 1,
+                                    c >= 2 ? &y1full[kb] : nullptr, ((c - 2) >> 1) & 1);
       if (bad && !*abort_flag) fail(1007);
       if (named_bar_or(BAR_MSK, 128, bad)) break;
-      if (t == 0) SSD_TRACE(c, 4);
       const float* sm = small_ptr(ds);
-      const uint8_t* Bt = stage_ptr(s) + TILE;
-      // (2) diag(w) B into its own tile (bf16x2 arithmetic)
-      {
-        uint8_t* Bh = bh_ptr(kb);
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-#pragma unroll
-          for (int it = 0; it < 4; ++it) {
-            const int idx = t + it * 128;            // 16-byte chunk; row j = idx / 8
-            const __nv_bfloat162 w2 = __float2bfloat162_rn(sm[144 + (idx >> 3)]);
-            uint4 v = *reinterpret_cast<const uint4*>(Bt + nb * TILE + idx * 16);
-            __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v);
-            hv[0] = __hmul2(hv[0], w2);
-            hv[1] = __hmul2(hv[1], w2);
-            hv[2] = __hmul2(hv[2], w2);
-            hv[3] = __hmul2(hv[3], w2);
-            *reinterpret_cast<uint4*>(Bh + nb * TILE + idx * 16) = v;
-          }
-        }
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(BAR_MSK, 128);
-      if (t == 0) {
-        SSD_TRACE(c, 5);
-        mbar_arrive(&bready[kb]);
-      }
-      // (3) G of chunk c; mask buffer free (MMA2 of chunk c-2 done)
-      bad = !mbar_wait_n(abort_flag, &gfull[kb], (c >> 1) & 1, c >= 2 ? &y1full[kb] : nullptr, ((c - 2) >> 1) & 1);
-      if (bad && !*abort_flag) fail(1013);
-      if (named_bar_or(BAR_MSK, 128, bad)) break;
       if (t == 0) SSD_TRACE(c, 6);
       tc_fence_after();
-      // (4) M row `row`, columns [32*half, 32*half+32):
+      // M row `row`, columns [32*half, 32*half+32):
       //     M_ij = G_ij * exp2(s_i - s_ref(J)) * v_j for j <= i (J = 4-token sub-block of j)
       float g[32];
       tmem_ld16x2_32(tmem + lane_base + col_g(kb), g);
@@ -584,12 +553,47 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         *reinterpret_cast<uint4*>(Hs + sw128_chunk(n_own, p0 / 8 + q)) = o;
       }
     };
+    // diag(w) B of chunk j (MMA4's A operand) into buffer j&1; false if a wait gave up
+    auto write_bhat = [&](int j) -> bool {
+      const int sj = j % ST, dj = j % DSL;
+      const bool bad = !mbar_wait_n(abort_flag, &full[sj], (j / ST) & 1, &dfull[dj], (j / DSL) & 1);
+      if (bad && !*abort_flag) fail(1017);
+      if (named_bar_or(BAR_STATE, 128, bad)) return false;
+      const float* wv = small_ptr(dj) + 144;
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const uint8_t* Bt = stage_ptr(sj) + TILE * (1 + nb);
+        uint8_t* Bh = bh_ptr(j & 1) + TILE * nb;
+        uint4 v[4];
+#pragma unroll
+        for (int it = 0; it < 4; ++it) v[it] = *reinterpret_cast<const uint4*>(Bt + (tid + it * 128) * 16);
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int idx = tid + it * 128;          // 16-byte chunk; row (token) = idx / 8
+          const __nv_bfloat162 w2 = __float2bfloat162_rn(wv[idx >> 3]);
+          __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v[it]);
+          hv[0] = __hmul2(hv[0], w2);
+          hv[1] = __hmul2(hv[1], w2);
+          hv[2] = __hmul2(hv[2], w2);
+          hv[3] = __hmul2(hv[3], w2);
+          *reinterpret_cast<uint4*>(Bh + idx * 16) = v[it];
+        }
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(BAR_STATE, 128);
+      if (tid == 0) {
+        SSD_TRACE(j, 5);
+        mbar_arrive(&bready[j & 1]);
+      }
+      return true;
+    };
     write_hs(hs_ptr(0));
     fence_proxy_async_smem();
     named_bar_sync(BAR_STATE, 128);
     if (tid == 0) mbar_arrive(&hready[0]);
     bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
+    for (int j = 0; j < 2 && j < nchunks && ok; ++j) ok = write_bhat(j);
+    for (int c = 0; c < nchunks && ok; ++c) {
       const int kb = c & 1, ds = c % DSL;
       // S of chunk c, its decay data, and state tile (c+1)&1 no longer read (MMA3 of chunk c-1 done)
       const bool bad = !mbar_wait_n(abort_flag, &sfull[kb], (c >> 1) & 1, &dfull[ds], (c / DSL) & 1,
@@ -631,10 +635,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       named_bar_sync(BAR_STATE, 128);
       if (tid == 0) {
         SSD_TRACE(c, 15);
-        mbar_arrive(&sfree[kb]);
         mbar_arrive(&hready[(c + 1) & 1]);
         mbar_arrive(&dempty[ds]);
       }
+      // S of chunk c is consumed, so buffer c&1 may take diag(w) B of chunk c+2
+      if (c + 2 < nchunks && !write_bhat(c + 2)) ok = false;
     }
     if (ok && h_last && !*abort_flag) {
       float* dst = h_last + (((int64_t)b * H + h) * P) * NST + n_own;

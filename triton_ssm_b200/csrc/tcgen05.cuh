@@ -83,11 +83,12 @@ __device__ __forceinline__ bool mbar_wait_n(const volatile int* abort, uint64_t*
                                             uint64_t* b1 = nullptr, uint32_t p1 = 0, uint64_t* b2 = nullptr,
                                             uint32_t p2 = 0, uint64_t* b3 = nullptr, uint32_t p3 = 0,
                                             uint64_t timeout_ns = 2000000000ull) {
-  const bool r = mbar_test(b0, p0) & (!b1 || mbar_test(b1, p1)) & (!b2 || mbar_test(b2, p2)) &
-                 (!b3 || mbar_test(b3, p3));
-  if (r) return true;
-  return mbar_wait_slow(b0, p0, abort, timeout_ns) && (!b1 || mbar_wait_slow(b1, p1, abort, timeout_ns)) &&
-         (!b2 || mbar_wait_slow(b2, p2, abort, timeout_ns)) && (!b3 || mbar_wait_slow(b3, p3, abort, timeout_ns));
+  const bool r0 = mbar_test(b0, p0), r1 = !b1 || mbar_test(b1, p1), r2 = !b2 || mbar_test(b2, p2),
+             r3 = !b3 || mbar_test(b3, p3);
+  if (r0 & r1 & r2 & r3) return true;
+  // a completed phase stays completed until its consumer moves on: wait only on the others
+  return (r0 || mbar_wait_slow(b0, p0, abort, timeout_ns)) && (r1 || mbar_wait_slow(b1, p1, abort, timeout_ns)) &&
+         (r2 || mbar_wait_slow(b2, p2, abort, timeout_ns)) && (r3 || mbar_wait_slow(b3, p3, abort, timeout_ns));
 }
 
 // 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22,
