@@ -22,13 +22,13 @@
 //   warp 15     decay: streams dt (cp.async) and writes each chunk's decay prefix
 //               sums and input coefficients into a DSL-slot ring of its own, so it
 //               runs several chunks ahead of the consumers;
-//   warps 13,14 MMA issuers (one thread each: MMA4 then MMA2 | MMA3); issuing a
-//               tcgen05.mma costs the issuing thread tens of cycles, so the issue
-//               work is spread over three threads and each MMA goes out as soon as
-//               its own inputs are ready (MMA4 needs only diag(w) B, not M);
-//   warps 4-7   mask group: B -> diag(w) B, then G -> M (bf16), for chunk c;
+//   warps 13,14 MMA2 | MMA4 + MMA3 issuers (one thread each).  Issuing a tcgen05.mma
+//               costs the issuing thread tens of cycles, so the issue work is spread
+//               over three threads and each MMA goes out as soon as its inputs are ready;
+//   warps 4-7   mask group: G -> M (bf16) for chunk c;
 //   warps 0-3   state group: H <- exp(s_last) H + S in registers and the bf16 copy
-//               of H for the next MMA3 -- the only serial dependence between chunks;
+//               of H for the next MMA3 -- the only serial dependence between chunks --
+//               then diag(w) B for chunk c+2 (MMA4's A operand);
 //   warps 8-11  output group: y = Y1 + exp(s_i) Y2 + D x into a swizzled tile, one
 //               TMA store per chunk.
 // G, Y1, Y2 and S are double-buffered in TMEM (8 x 64 = 512 columns), M, diag(w) B,
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   float* dsk = reinterpret_cast<float*>(smem + LY::OFF_DSK);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
   uint64_t* full = bars;               // [ST]  TMA bytes of X, B, C landed
-  uint64_t* empty = full + ST;         // [ST]  stage released (output group)
+  uint64_t* empty = full + ST;         // [ST]  stage released (output group + state group)
   uint64_t* dfull = empty + ST;        // [DSL] decay data written
   uint64_t* dempty = dfull + DSL;      // [DSL] decay slot released (state + output groups)
   uint64_t* gfull = dempty + DSL;      // [2]   MMA1 done
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   uint64_t* bready = gfull + 4;        // [2]   diag(w) B written
   uint64_t* mready = gfull + 6;        // [2]   M written
   uint64_t* sfull = gfull + 8;         // [2]   MMA4 done
-  uint64_t* y1full = gfull + 10;       // [2]   MMA2 done (and the MMA4 before it)
+  uint64_t* y1full = gfull + 10;       // [2]   MMA2 done
   uint64_t* y2full = gfull + 12;       // [2]   MMA3 done
   // gfull + 14, + 15: spare
   uint64_t* yfree = gfull + 16;        // [2]   Y1, Y2 read by the output group
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   if (tid == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 2);
     }
     for (int d = 0; d < DSL; ++d) {
       mbar_init(&dfull[d], 1);
@@ -345,33 +345,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     asm volatile("cp.async.wait_all;" ::: "memory");   // no copy may outlive the loop
     if (decay_log2 && lane == 0 && !*abort_flag) decay_log2[(int64_t)b * H + h] = total_log2;
   } else if (warp == 13) {
-    // ================================================================ MMA4 + MMA2 issuer
+    // ================================================================ MMA2 issuer
     if (lane == 0) {
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
-      constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
-        // bready(k) also means S of chunk k-2 was consumed (the state group writes diag(w) B
-        // of chunk k after reading S of chunk k-2), so accumulator c&1 is free
-        if (!mbar_wait_n(abort_flag, &bready[kb], (k >> 1) & 1, &full[s], (k / ST) & 1)) {
-          if (!*abort_flag) fail(1004);
-          break;
-        }
-        tc_fence_after();
-        SSD_TRACE(k, 8);
-        const uint32_t X = smem_u32(stage_ptr(s));
-        const uint64_t dX = make_desc_sw128(X, TILE), dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_s(kb), dBh + 128 * kk, dX + 128 * kk, ID_MM, kk > 0);
-        umma_commit(&sfull[kb]);
-        SSD_TRACE(k, 9);
-        SSD_TRACE_DONE(&sfull[kb], (k >> 1) & 1, k, 21);
-        if (!mbar_wait_n(abort_flag, &mready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1)) {
+        if (!mbar_wait_n(abort_flag, &mready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1,
+                         &full[s], (k / ST) & 1)) {
           if (!*abort_flag) fail(1015);
           break;
         }
         tc_fence_after();
         SSD_TRACE(k, 10);
+        const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
         const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_y1(kb), dM + 2 * kk, dX + 128 * kk, ID_KM, kk > 0);
@@ -382,11 +368,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       drain_mmas(&drain[1]);
     }
   } else if (warp == 14) {
-    // ================================================================ MMA3 issuer
+    // ================================================================ MMA4 + MMA3 issuer
     if (lane == 0) {
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
+      constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
+        // MMA4 (S^T = diag(w)B^T X).  bready(k) also means S of chunk k-2 was consumed
+        // (the state group writes diag(w) B of chunk k after reading it).
+        if (!mbar_wait_n(abort_flag, &bready[kb], (k >> 1) & 1, &full[s], (k / ST) & 1)) {
+          if (!*abort_flag) fail(1004);
+          break;
+        }
+        tc_fence_after();
+        SSD_TRACE(k, 8);
+        {
+          const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
+          const uint64_t dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_s(kb), dBh + 128 * kk, dX + 128 * kk, ID_MM, kk > 0);
+        }
+        umma_commit(&sfull[kb]);
+        SSD_TRACE(k, 9);
+        SSD_TRACE_DONE(&sfull[kb], (k >> 1) & 1, k, 21);
+        // MMA3 (Y2 = C H^T) once the state tile of chunk k-1 is written
         if (!mbar_wait_n(abort_flag, &hready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1,
                          &full[s], (k / ST) & 1)) {
           if (!*abort_flag) fail(1006);
@@ -637,6 +642,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         SSD_TRACE(c, 15);
         mbar_arrive(&hready[(c + 1) & 1]);
         mbar_arrive(&dempty[ds]);
+        mbar_arrive(&empty[c % ST]);   // MMA4 of chunk c (which read X) is complete
       }
       // S of chunk c is consumed, so buffer c&1 may take diag(w) B of chunk c+2
       if (c + 2 < nchunks && !write_bhat(c + 2)) ok = false;
