@@ -558,12 +558,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         *reinterpret_cast<uint4*>(Hs + sw128_chunk(n_own, p0 / 8 + q)) = o;
       }
     };
-    // diag(w) B of chunk j (MMA4's A operand) into buffer j&1; false if a wait gave up
-    auto write_bhat = [&](int j) -> bool {
+    // diag(w) B of chunk j (MMA4's A operand) into buffer j&1 (its B tile and decay data have landed)
+    auto bhat_rows = [&](int j) {
       const int sj = j % ST, dj = j % DSL;
-      const bool bad = !mbar_wait_n(abort_flag, &full[sj], (j / ST) & 1, &dfull[dj], (j / DSL) & 1);
-      if (bad && !*abort_flag) fail(1017);
-      if (named_bar_or(BAR_STATE, 128, bad)) return false;
       const float* wv = small_ptr(dj) + 144;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
@@ -584,6 +581,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
           *reinterpret_cast<uint4*>(Bh + idx * 16) = v[it];
         }
       }
+    };
+    auto write_bhat = [&](int j) -> bool {   // standalone (first two chunks); false if a wait gave up
+      const bool bad = !mbar_wait_n(abort_flag, &full[j % ST], (j / ST) & 1, &dfull[j % DSL], (j / DSL) & 1);
+      if (bad && !*abort_flag) fail(1017);
+      if (named_bar_or(BAR_STATE, 128, bad)) return false;
+      bhat_rows(j);
       fence_proxy_async_smem();
       named_bar_sync(BAR_STATE, 128);
       if (tid == 0) {
@@ -600,9 +603,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     for (int j = 0; j < 2 && j < nchunks && ok; ++j) ok = write_bhat(j);
     for (int c = 0; c < nchunks && ok; ++c) {
       const int kb = c & 1, ds = c % DSL;
-      // S of chunk c, its decay data, and state tile (c+1)&1 no longer read (MMA3 of chunk c-1 done)
-      const bool bad = !mbar_wait_n(abort_flag, &sfull[kb], (c >> 1) & 1, &dfull[ds], (c / DSL) & 1,
-                                    c >= 1 ? &y2full[(c - 1) & 1] : nullptr, ((c - 1) >> 1) & 1);
+      const bool nxt = c + 2 < nchunks;   // diag(w) B of chunk c+2 is written in this iteration
+      const int jd = nxt ? c + 2 : c;
+      // S of chunk c (MMA4 is committed after MMA3 of chunk c-1 by the same thread, so state
+      // tile (c+1)&1 is no longer read either); decay data up to chunk jd (the decay warp
+      // publishes in order); the B tile of chunk c+2
+      const bool bad = !mbar_wait_n(abort_flag, &sfull[kb], (c >> 1) & 1, &dfull[jd % DSL], (jd / DSL) & 1,
+                                    nxt ? &full[(c + 2) % ST] : nullptr, ((c + 2) / ST) & 1);
       if (bad && !*abort_flag) fail(1008);
       if (named_bar_or(BAR_STATE, 128, bad)) {
         ok = false;
@@ -635,6 +642,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         for (int j = 0; j < 32; ++j) hreg[32 + j] = e_last * hreg[32 + j] + sv[j];
       }
       write_hs(hs_ptr((c + 1) & 1));
+      // S of chunk c is consumed, so buffer c&1 may take diag(w) B of chunk c+2
+      if (nxt) bhat_rows(c + 2);
       fence_proxy_async_smem();
       tc_fence_before();
       named_bar_sync(BAR_STATE, 128);
@@ -643,9 +652,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         mbar_arrive(&hready[(c + 1) & 1]);
         mbar_arrive(&dempty[ds]);
         mbar_arrive(&empty[c % ST]);   // MMA4 of chunk c (which read X) is complete
+        if (nxt) mbar_arrive(&bready[kb]);
       }
-      // S of chunk c is consumed, so buffer c&1 may take diag(w) B of chunk c+2
-      if (c + 2 < nchunks && !write_bhat(c + 2)) ok = false;
     }
     if (ok && h_last && !*abort_flag) {
       float* dst = h_last + (((int64_t)b * H + h) * P) * NST + n_own;
