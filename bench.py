@@ -363,6 +363,38 @@ def run_ours_c1(args, rank, world, local):
                  launches=launches)
 
 
+def run_ours_c1bwd(args, rank, world, local):
+    """Config 1 backward: the drop-in backward pair at the config-1 forward's
+    shapes (B4 L1024, H' = D*N = 1024, f32): ssm_backward (dY -> du, dA, dB, dC)
+    then zoh_discretize_bwd (dAbar = dA, dBbar = dB -> dA_log, dB, ddt)."""
+    import triton_ssm_b200 as ts
+    dev = torch.device("cuda", local)
+    Bt, L, Hp = 4, 1024, 1024
+    g = torch.Generator(device=dev)
+    g.manual_seed(13 + rank)
+    A_log = torch.log(torch.arange(1, 17, device=dev, dtype=torch.float32)).repeat(64)
+    Bc = torch.randn(Bt, L, Hp, device=dev, generator=g) / 4.0
+    dt = torch.empty(Bt, L, device=dev).exponential_(1.0, generator=g).clamp_(1e-3, 10.0)
+    u = torch.randn(Bt, L, Hp, device=dev, generator=g)
+    C = torch.randn(Bt, L, Hp, device=dev, generator=g) / 4.0
+    Ab, Bb = ts.zoh_discretize(A_log, Bc, dt)
+    _, h = ts.ssm_forward(u, Ab, Bb, C, torch.zeros(Hp, device=dev))
+    dY = torch.randn(Bt, L, Hp, device=dev, generator=g)
+
+    def step():
+        du, dA, dB, dC = ts.ssm_backward(u, Ab, Bb, C, h, dY)
+        ts.zoh_discretize_bwd(A_log, Bc, dt, Ab, dA, dB)
+    t_step, clocks = _timed(args, world, dev, step)
+    n = Bt * L * Hp
+    alg = n * 4 * 10 + n * 4 * 5 + Bt * L * 4 * 2 + Hp * 4 * 2   # ssm_backward 6R+4W, discretize_bwd 4R+1W
+    upd = Bt * L * Hp
+    cfg = {"workload": "config1 backward: ssm_backward + zoh_discretize_bwd, B4 L1024 H'=D*N=1024 f32",
+           "global_batch": Bt * world, "seq_len": L, "parallelism": "batch, %d rank(s)" % world}
+    return _line(args, world, METRIC, world * upd / t_step, t_step, "f32", cfg, alg,
+                 "ssm_backward_kernel + zoh_discretize_bwd_kernel", "ssm_backward_c1.md", clocks,
+                 launches=2 * args.steps)
+
+
 def run_ours_c4(args, rank, world, local):
     """Config 4: B4 H32 P64 N128 L=1,048,576 bf16, sequence sharded over the ranks
     (strong scaling): local scan from a zero state, one all-gather of
@@ -468,7 +500,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s pre-timing load")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c2",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c1bwd"], default="c2",
                     help="workload (default c2, the headline; the others are for measurement notes)")
     ap.add_argument("--c1-mode", choices=["pair", "fused"], default="pair")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays of the step")
@@ -491,7 +523,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         runner = {"c1": run_ours_c1, "c2": run_ours_c2, "c3": run_ours_c3, "c4": run_ours_c4,
-                  "c5": run_ours_c5}[args.config]
+                  "c5": run_ours_c5, "c1bwd": run_ours_c1bwd}[args.config]
         out = runner(args, rank, world, local)
         if rank == 0:
             print(json.dumps(out), flush=True)

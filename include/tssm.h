@@ -79,6 +79,34 @@ int tssm_ssm_forward(const void* u, const void* A, const void* B, const void* C,
                      int dtype, tssm_stream_t stream);
 
 /*
+ * Backward of the diagonal scan.  Replaces ssm_backward (ssm_scan.py:267-289),
+ * i.e. ssm_bwd_local_kernel / ssm_bwd_carry_scan_kernel / ssm_bwd_apply_kernel
+ * (ssm_scan.py:127-231), with one launch and no intermediate buffers.
+ *   u, A, B, C, h (forward states), dY [Bsz,L,H] contiguous (dtype);
+ *   du, dA, dB, dC [Bsz,L,H] (dtype), written.
+ *   dH_t = C_t*dY_t + A_{t+1}*dH_{t+1}; du = B*dH, dA = h_{t-1}*dH,
+ *   dB = u*dH, dC = dY*h.  As in the reference, D is a constant: no dD and
+ *   no D*dY term in du.  Math in f32.  dtype: TSSM_F32 or TSSM_BF16.
+ */
+int tssm_ssm_backward(const void* u, const void* A, const void* B, const void* C, const void* h,
+                      const void* dY, void* du, void* dA, void* dB, void* dC,
+                      int64_t Bsz, int64_t L, int64_t H, int dtype, tssm_stream_t stream);
+
+/*
+ * Backward of the ZOH discretisation.  Replaces zoh_discretize_bwd_kernel
+ * (discretize_kernel.py:97-162).
+ *   A_log [H]; B, Abar, dAbar, dBbar [Bsz,T,H]; dt [Bsz,T]; all f32, contiguous.
+ *   dA_log [H], dB [Bsz,T,H], ddt [Bsz,T] f32, written.
+ *   ddt is the full sum over H (the reference's per-block store/atomic mix at
+ *   :159-162 races); dA_log is overwritten with the sum over (b, t) -- the
+ *   reference accumulates into a buffer its caller must zero.  dA_log is
+ *   summed with float atomics, so its last bits may vary between runs.
+ */
+int tssm_zoh_discretize_bwd(const void* A_log, const void* B, const void* dt, const void* Abar,
+                            const void* dAbar, const void* dBbar, void* dA_log, void* dB, void* ddt,
+                            int64_t Bsz, int64_t T, int64_t H, tssm_stream_t stream);
+
+/*
  * Fused ZOH discretisation + diagonal scan + readout over an N-wide state per
  * channel: the composition zoh_discretize_diag_kernel (discretize_kernel.py:
  * 15-57) -> ssm_forward (ssm_scan.py:239-264) over H' = D*N channels with the

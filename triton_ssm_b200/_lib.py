@@ -30,6 +30,8 @@ SIGNATURES = {
     "tssm_zoh_discretize": ([P] * 5 + [I64] * 3 + [I64] * 8 + [I32, P], I32),
     "tssm_ssm_forward": ([P] * 7 + [I64] * 3 + [I32, P], I32),
     "tssm_selective_scan": ([P] * 8 + [I64] * 4 + [P], I32),
+    "tssm_ssm_backward": ([P] * 10 + [I64] * 3 + [I32, P], I32),
+    "tssm_zoh_discretize_bwd": ([P] * 9 + [I64] * 3 + [P], I32),
     "tssm_streaming_inplace": ([P] * 7 + [I64] * 2 + [I64] * 3 + [I32, P], I32),
     "tssm_streaming_step": ([P] * 8 + [I64] * 4 + [I32, P], I32),
     "tssm_multihead_ssd": ([P] * 10 + [I64] * 5 + [I32, P], I32),

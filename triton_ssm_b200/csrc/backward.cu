@@ -1,0 +1,257 @@
+// Backward passes of the diagonal scan and of the ZOH discretisation.
+//
+// ssm_backward (replaces ssm_scan.py:127-231 / :267-289): for the forward
+//     h_t = A_t h_{t-1} + B_t u_t ,  y_t = C_t h_t + D u_t
+// the reference propagates only the state path (D is a constant there):
+//     dH_t = C_t dY_t + A_{t+1} dH_{t+1}      (dH_{L-1} = C_{L-1} dY_{L-1})
+//     du = B dH,  dA = h_{t-1} dH,  dB = u dH,  dC = dY h.
+// One pass, same shape as the forward kernel but walking the sequence from the
+// end: a CTA owns 32 consecutive channels of one batch row (one lane each, so
+// every step is one coalesced 128-byte row segment per warp); warp w holds
+// steps [w*S, (w+1)*S) of a super-segment of NW*S steps, folds them into a
+// reverse (a, x) aggregate, takes the carry from the warps after it, and
+// replays its steps writing du, dA, dB, dC.  Every input is read from HBM once.
+//
+// zoh_discretize_bwd (replaces discretize_kernel.py:97-162): per (b, t, h)
+//     a = -exp(A_log), x = dt a, e = exp(x), em1 = guarded exp(x)-1 (bf16 form, :134)
+//     ddt   += dAbar a Abar + dBbar e B                       (summed over h)
+//     dA_log += (dAbar dt Abar + dBbar (e dt a - em1)/(a^2+1e-18) B) (-(-a))  (summed over b, t)
+//     dB     = dBbar em1 / (a + 1e-12)
+// A CTA owns a block of (b, t) rows and all of H, so each row's ddt is reduced
+// inside the CTA (no store/atomic race as in :159-162); dA_log gets one atomic
+// add per (CTA, h).
+#include "common.cuh"
+
+namespace tssm {
+namespace {
+
+template <typename T, int S, int NW>
+__global__ void __launch_bounds__(NW * 32, 1) ssm_backward_kernel(
+    const T* __restrict__ u, const T* __restrict__ A, const T* __restrict__ B, const T* __restrict__ C,
+    const T* __restrict__ h, const T* __restrict__ dY, T* __restrict__ du, T* __restrict__ dA,
+    T* __restrict__ dB, T* __restrict__ dC, int64_t L, int64_t H) {
+  __shared__ float s_a[NW][32];
+  __shared__ float s_x[NW][32];
+  __shared__ float s_carry[32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t ch = (int64_t)blockIdx.x * 32 + lane;
+  const bool valid = ch < H;
+  // One 64-bit base per CTA; offsets inside a batch row fit in 32 bits (host-checked).
+  const int64_t base = (int64_t)blockIdx.y * L * H + ch;
+  const T* __restrict__ ub = u + base;
+  const T* __restrict__ Ab = A + base;
+  const T* __restrict__ Bb = B + base;
+  const T* __restrict__ Cb = C + base;
+  const T* __restrict__ hb = h + base;
+  const T* __restrict__ dYb = dY + base;
+  T* __restrict__ dub = du + base;
+  T* __restrict__ dAb = dA + base;
+  T* __restrict__ dBb = dB + base;
+  T* __restrict__ dCb = dC + base;
+  const int Hi = (int)H;
+  const int Li = (int)L;
+  constexpr int SEG = NW * S;
+  float carry = 0.f;   // dH at the first step after the current super-segment (0 past the end)
+  for (int t0 = ((Li - 1) / SEG) * SEG; t0 >= 0; t0 -= SEG) {
+    const int ts = t0 + warp * S;
+    // coefficient A_{t+1} and input C_t dY_t of the reverse recurrence dH_t = A_{t+1} dH_{t+1} + C_t dY_t
+    float a[S], x[S], dy[S];
+#pragma unroll
+    for (int i = 0; i < S; ++i) {
+      const int t = ts + i;
+      if (valid && t < Li) {
+        const int off = t * Hi;
+        a[i] = t + 1 < Li ? ldf(Ab + off + Hi) : 0.f;
+        dy[i] = ldf(dYb + off);
+        x[i] = ldf(Cb + off) * dy[i];
+      } else {
+        a[i] = 1.f;
+        x[i] = 0.f;
+        dy[i] = 0.f;
+      }
+    }
+    float ag_a = 1.f, ag_x = 0.f;   // dH_ts = ag_a * dH_{ts+S} + ag_x
+#pragma unroll
+    for (int i = S - 1; i >= 0; --i) {
+      ag_x = a[i] * ag_x + x[i];
+      ag_a *= a[i];
+    }
+    s_a[warp][lane] = ag_a;
+    s_x[warp][lane] = ag_x;
+    __syncthreads();
+    float dh = carry;
+    for (int w = NW - 1; w > warp; --w) dh = s_a[w][lane] * dh + s_x[w][lane];
+    // replay from the end of this warp's steps; h_{t-1} of one step is h_t of the next
+    float hcur = (valid && ts + S - 1 < Li) ? ldf(hb + (ts + S - 1) * Hi) : 0.f;
+#pragma unroll
+    for (int i = S - 1; i >= 0; --i) {
+      const int t = ts + i;
+      dh = a[i] * dh + x[i];
+      const float hprev = (valid && t >= 1 && t - 1 < Li) ? ldf(hb + (t - 1) * Hi) : 0.f;
+      if (valid && t < Li) {
+        const int off = t * Hi;
+        stf(dub + off, ldf(Bb + off) * dh);
+        stf(dBb + off, ldf(ub + off) * dh);
+        stf(dCb + off, dy[i] * hcur);
+        stf(dAb + off, hprev * dh);
+      }
+      hcur = hprev;
+    }
+    if (warp == 0) s_carry[lane] = dh;   // dH at step t0
+    __syncthreads();
+    carry = s_carry[lane];
+  }
+}
+
+constexpr int DBWD_THREADS = 256;
+constexpr int DBWD_ROWS = 16;   // (b, t) rows per CTA
+
+// VEC: H % 4 == 0 and 16-byte aligned rows, four channels per thread per pass.
+template <bool VEC>
+__global__ void __launch_bounds__(DBWD_THREADS) zoh_discretize_bwd_kernel(
+    const float* __restrict__ A_log, const float* __restrict__ B, const float* __restrict__ dt,
+    const float* __restrict__ Abar, const float* __restrict__ dAbar, const float* __restrict__ dBbar,
+    float* __restrict__ dA_log, float* __restrict__ dB, float* __restrict__ ddt, int64_t R, int64_t H) {
+  constexpr int NWARP = DBWD_THREADS / 32;
+  constexpr int PER = VEC ? 4 : 1;
+  __shared__ float s_ddt[DBWD_ROWS][NWARP];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t r0 = (int64_t)blockIdx.x * DBWD_ROWS;
+  const int nrows = R - r0 < DBWD_ROWS ? (int)(R - r0) : DBWD_ROWS;
+  for (int i = tid; i < DBWD_ROWS * NWARP; i += DBWD_THREADS) (&s_ddt[0][0])[i] = 0.f;
+  __syncthreads();
+  // Chunks of DBWD_THREADS*PER channels; every thread runs every chunk (the ddt
+  // shuffle reduction needs whole warps), channels past H contribute nothing.
+  for (int64_t hc = 0; hc < H; hc += DBWD_THREADS * PER) {
+    const int64_t h0 = hc + (int64_t)tid * PER;
+    const bool act = h0 < H;   // VEC: H % 4 == 0, so all PER channels exist
+    float a[PER], na[PER], acc[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      na[k] = act ? expf(A_log[h0 + k]) : 1.f;
+      a[k] = -na[k];
+      acc[k] = 0.f;
+    }
+    for (int r = 0; r < nrows; ++r) {
+      const int64_t row = r0 + r;
+      const float dtv = dt[row];
+      float part = 0.f;
+      if (act) {
+        const int64_t off = row * H + h0;
+        float vb[PER], vab[PER], vda[PER], vdb[PER], out[PER];
+        if (VEC) {
+          const float4 q0 = *reinterpret_cast<const float4*>(B + off);
+          const float4 q1 = *reinterpret_cast<const float4*>(Abar + off);
+          const float4 q2 = *reinterpret_cast<const float4*>(dAbar + off);
+          const float4 q3 = *reinterpret_cast<const float4*>(dBbar + off);
+          const float t0[4] = {q0.x, q0.y, q0.z, q0.w}, t1[4] = {q1.x, q1.y, q1.z, q1.w};
+          const float t2[4] = {q2.x, q2.y, q2.z, q2.w}, t3[4] = {q3.x, q3.y, q3.z, q3.w};
+#pragma unroll
+          for (int k = 0; k < PER; ++k) {
+            vb[k] = t0[k];
+            vab[k] = t1[k];
+            vda[k] = t2[k];
+            vdb[k] = t3[k];
+          }
+        } else {
+          vb[0] = B[off];
+          vab[0] = Abar[off];
+          vda[0] = dAbar[off];
+          vdb[0] = dBbar[off];
+        }
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+          const float x = dtv * a[k];
+          const float e = expf(x);
+          const float em1 = expm1_guard_bf16(x, e);
+          part += vda[k] * a[k] * vab[k] + vdb[k] * e * vb[k];
+          const float num = (e * dtv * a[k] - em1) / (a[k] * a[k] + 1e-18f);
+          const float da = vda[k] * dtv * vab[k] + vdb[k] * num * vb[k];
+          acc[k] += da * (-na[k]);
+          out[k] = vdb[k] * em1 / (a[k] + 1e-12f);
+        }
+        if (VEC)
+          *reinterpret_cast<float4*>(dB + off) = make_float4(out[0], out[1], out[2], out[3]);
+        else
+          dB[off] = out[0];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0) s_ddt[r][warp] += part;
+    }
+    if (act) {
+#pragma unroll
+      for (int k = 0; k < PER; ++k) atomicAdd(dA_log + h0 + k, acc[k]);
+    }
+  }
+  __syncthreads();
+  if (tid < nrows) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) s += s_ddt[tid][w];
+    ddt[r0 + tid] = s;
+  }
+}
+
+}  // namespace
+}  // namespace tssm
+
+extern "C" int tssm_ssm_backward(const void* u, const void* A, const void* B, const void* C, const void* h,
+                                 const void* dY, void* du, void* dA, void* dB, void* dC, int64_t Bsz,
+                                 int64_t L, int64_t H, int dtype, tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(Bsz >= 0 && L >= 0 && H >= 0, "ssm_backward: negative size");
+  if (Bsz * L * H == 0) return TSSM_OK;
+  TSSM_REQUIRE(u && A && B && C && h && dY && du && dA && dB && dC, "ssm_backward: null pointer");
+  TSSM_REQUIRE(Bsz <= 65535, "ssm_backward: batch %lld exceeds 65535", (long long)Bsz);
+  TSSM_REQUIRE(L * H < (int64_t(1) << 31), "ssm_backward: L*H must be < 2^31 per batch row");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  constexpr int S = 16, NW = 16;
+  dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
+  if (dtype == TSSM_F32) {
+    ssm_backward_kernel<float, S, NW><<<grid, NW * 32, 0, st>>>(
+        (const float*)u, (const float*)A, (const float*)B, (const float*)C, (const float*)h, (const float*)dY,
+        (float*)du, (float*)dA, (float*)dB, (float*)dC, L, H);
+  } else if (dtype == TSSM_BF16) {
+    using bf = __nv_bfloat16;
+    ssm_backward_kernel<bf, S, NW><<<grid, NW * 32, 0, st>>>(
+        (const bf*)u, (const bf*)A, (const bf*)B, (const bf*)C, (const bf*)h, (const bf*)dY, (bf*)du, (bf*)dA,
+        (bf*)dB, (bf*)dC, L, H);
+  } else {
+    set_error("ssm_backward: dtype must be f32 or bf16 (got %d)", dtype);
+    return TSSM_ERR_INVALID;
+  }
+  return check_launch("ssm_backward");
+}
+
+extern "C" int tssm_zoh_discretize_bwd(const void* A_log, const void* B, const void* dt, const void* Abar,
+                                       const void* dAbar, const void* dBbar, void* dA_log, void* dB, void* ddt,
+                                       int64_t Bsz, int64_t T, int64_t H, tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(Bsz >= 0 && T >= 0 && H >= 0, "zoh_discretize_bwd: negative size");
+  TSSM_REQUIRE(!(H > 0 && !dA_log), "zoh_discretize_bwd: null dA_log");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // dA_log is a fresh gradient (the reference accumulates into a caller-zeroed buffer)
+  if (H > 0 && cudaMemsetAsync(dA_log, 0, (size_t)H * sizeof(float), st) != cudaSuccess)
+    return check_launch("zoh_discretize_bwd: clear dA_log");
+  const int64_t R = Bsz * T;
+  if (R == 0) return TSSM_OK;
+  TSSM_REQUIRE(A_log && B && dt && Abar && dAbar && dBbar && dB && ddt, "zoh_discretize_bwd: null pointer");
+  if (H == 0) return cudaMemsetAsync(ddt, 0, (size_t)R * sizeof(float), st) == cudaSuccess
+                         ? TSSM_OK
+                         : check_launch("zoh_discretize_bwd: clear ddt");
+  const bool vec = (H % 4 == 0) && aligned16(B) && aligned16(Abar) && aligned16(dAbar) && aligned16(dBbar) &&
+                   aligned16(dB);
+  const unsigned grid = (unsigned)cdiv(R, DBWD_ROWS);
+  TSSM_REQUIRE(cdiv(R, DBWD_ROWS) < (int64_t(1) << 31), "zoh_discretize_bwd: too many rows");
+  if (vec)
+    zoh_discretize_bwd_kernel<true><<<grid, DBWD_THREADS, 0, st>>>(
+        (const float*)A_log, (const float*)B, (const float*)dt, (const float*)Abar, (const float*)dAbar,
+        (const float*)dBbar, (float*)dA_log, (float*)dB, (float*)ddt, R, H);
+  else
+    zoh_discretize_bwd_kernel<false><<<grid, DBWD_THREADS, 0, st>>>(
+        (const float*)A_log, (const float*)B, (const float*)dt, (const float*)Abar, (const float*)dAbar,
+        (const float*)dBbar, (float*)dA_log, (float*)dB, (float*)ddt, R, H);
+  return check_launch("zoh_discretize_bwd");
+}

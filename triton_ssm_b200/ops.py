@@ -14,7 +14,7 @@ from ._lib import call, dtype_code, ptr, stream_of
 __all__ = ["zoh_discretize", "ssm_forward", "selective_scan", "streaming_ssm_inplace",
            "streaming_step", "multihead_ssm", "check_device_status", "fused_time_aware_interp",
            "fused_interp_ssm_step", "fused_interp_ssm", "linspace_queries", "interp_ssm_workspace_bytes",
-           "ssd_carry_fixup"]
+           "ssd_carry_fixup", "ssm_backward", "zoh_discretize_bwd"]
 
 
 def _cuda(*ts):
@@ -92,6 +92,58 @@ def ssm_forward(u, A, B, C, D, BLK=256, store_h=True):
     call("tssm_ssm_forward", ptr(u), ptr(A), ptr(B), ptr(C), ptr(D), ptr(y), ptr(h), Bt, L, H,
          dtype_code(u), stream_of(u))
     return y, h
+
+
+def ssm_backward(u, A, B, C, h, dY, BLK=256):
+    """Backward of the diagonal scan (``ssm_scan.py:267-289``).
+
+    u, A, B, C, h (the forward's states), dY [Bt,L,H]; f32 or bf16 (all the
+    same dtype).  Returns (du, dA, dB, dC) [Bt,L,H] with
+    dH_t = C_t dY_t + A_{t+1} dH_{t+1}, du = B dH, dA = h_{t-1} dH, dB = u dH,
+    dC = dY h.  As in the reference, D is a constant (no dD, no D*dY in du).
+    ``BLK`` is accepted for signature compatibility.
+    """
+    del BLK
+    _cuda(u, A, B, C, h, dY)
+    _need(u, (torch.float32, torch.bfloat16), "u")
+    for t in (A, B, C, h, dY):
+        if t.dtype != u.dtype:
+            raise ValueError("ssm_backward: u, A, B, C, h, dY must share a dtype")
+        if t.shape != u.shape:
+            raise ValueError("ssm_backward: expected u, A, B, C, h, dY of one shape [Bt,L,H]")
+    if u.dim() != 3:
+        raise ValueError("ssm_backward: expected [Bt,L,H] tensors")
+    u, A, B, C, h, dY = (t.contiguous() for t in (u, A, B, C, h, dY))
+    Bt, L, H = u.shape
+    du, dA, dB, dC = (torch.empty_like(u) for _ in range(4))
+    call("tssm_ssm_backward", ptr(u), ptr(A), ptr(B), ptr(C), ptr(h), ptr(dY), ptr(du), ptr(dA), ptr(dB),
+         ptr(dC), Bt, L, H, dtype_code(u), stream_of(u))
+    return du, dA, dB, dC
+
+
+def zoh_discretize_bwd(A_log, B, dt, Abar, dAbar, dBbar):
+    """Backward of the ZOH discretisation (``discretize_kernel.py:97-162``).
+
+    A_log [H]; B, Abar, dAbar, dBbar [Bt,T,H]; dt [Bt,T]; f32.
+    Returns (dA_log [H], dB [Bt,T,H], ddt [Bt,T]), f32.  ddt is the full sum
+    over H (the reference's ddt store/atomic mix races); dA_log is a fresh
+    gradient (the reference adds into a buffer its caller zeroes).
+    """
+    _cuda(A_log, B, dt, Abar, dAbar, dBbar)
+    for t, n in ((A_log, "A_log"), (B, "B"), (dt, "dt"), (Abar, "Abar"), (dAbar, "dAbar"), (dBbar, "dBbar")):
+        _need(t, (torch.float32,), n)
+    if B.dim() != 3 or dt.dim() != 2 or A_log.dim() != 1:
+        raise ValueError("zoh_discretize_bwd: expected A_log [H], B [Bt,T,H], dt [Bt,T]")
+    Bt, T, H = B.shape
+    if A_log.shape[0] != H or tuple(dt.shape) != (Bt, T) or any(t.shape != B.shape for t in (Abar, dAbar, dBbar)):
+        raise ValueError("zoh_discretize_bwd: shape mismatch")
+    A_log, B, dt, Abar, dAbar, dBbar = (t.contiguous() for t in (A_log, B, dt, Abar, dAbar, dBbar))
+    dA_log = torch.empty_like(A_log)
+    dB = torch.empty_like(B)
+    ddt = torch.empty_like(dt)
+    call("tssm_zoh_discretize_bwd", ptr(A_log), ptr(B), ptr(dt), ptr(Abar), ptr(dAbar), ptr(dBbar), ptr(dA_log),
+         ptr(dB), ptr(ddt), Bt, T, H, stream_of(B))
+    return dA_log, dB, ddt
 
 
 def selective_scan(x, dt, A_log, B, C, D, return_state=True):
