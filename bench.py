@@ -395,6 +395,44 @@ def run_ours_c1bwd(args, rank, world, local):
                  launches=2 * args.steps)
 
 
+def run_ours_ring(args, rank, world, local):
+    """Streaming ring-buffer ingest + forward fill + step (race-free
+    streaming_interp_then_ssm): S=4096 streams, H=1024 features, K=10 (the
+    reference's default ring), 128-feature tiles, f32; events cycle through
+    16 pre-generated sets, as config 5 does."""
+    import triton_ssm_b200 as ts
+    dev = torch.device("cuda", local)
+    S = args.batch or 4096
+    H, K = 1024, 10
+    g = torch.Generator(device=dev)
+    g.manual_seed(21 + rank)
+    ring = ts.StreamingRing(S, H, K, torch.rand(H, device=dev, generator=g) * 0.9,
+                            torch.randn(H, device=dev, generator=g), torch.randn(H, device=dev, generator=g),
+                            device=dev, block_h=128)
+    sets = [dict(v=torch.randn(S, H, device=dev, generator=g),
+                 m=(torch.rand(S, H, device=dev, generator=g) < 0.7).float(),
+                 tau=torch.rand(S, device=dev, generator=g),
+                 C=torch.randn(S, H, device=dev, generator=g)) for _ in range(16)]
+    y = torch.empty(S, H, device=dev)
+    it = [0]
+
+    def step():
+        e = sets[it[0] % 16]
+        it[0] += 1
+        ring.step(e["v"], e["m"], e["tau"], e["C"], y=y)
+    t_step, clocks = _timed(args, world, dev, step)
+    # per (stream, feature): event v, m in; ring slot V, M out; h in + out; C in; y out.
+    # A tile whose event is observed never reads the ring (with Bernoulli(0.7) masks
+    # over 128-feature tiles every tile is observed).
+    alg = S * H * 4 * 8 + S * 4 * 2 + H * 4 * 3 + S * 4 * 2
+    cfg = {"workload": "ring-buffer streaming step: S%d streams, H%d features, K=%d ring, 128-feature tiles, "
+                       "f32, mask Bernoulli(0.7)" % (S, H, K),
+           "global_batch": S * world, "seq_len": 1, "parallelism": "streams, %d rank(s)" % world,
+           "l2": "state + ring 420 MB per rank, larger than the 126 MB L2"}
+    return _line(args, world, METRIC, world * S * H / t_step, t_step, "f32", cfg, alg, "ring_ingest_step_kernel",
+                 "ring_ingest_step.md", clocks)
+
+
 def run_ours_c4(args, rank, world, local):
     """Config 4: B4 H32 P64 N128 L=1,048,576 bf16, sequence sharded over the ranks
     (strong scaling): local scan from a zero state, one all-gather of
@@ -500,7 +538,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s pre-timing load")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c1bwd"], default="c2",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c1bwd", "ring"], default="c2",
                     help="workload (default c2, the headline; the others are for measurement notes)")
     ap.add_argument("--c1-mode", choices=["pair", "fused"], default="pair")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays of the step")
@@ -523,7 +561,7 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         runner = {"c1": run_ours_c1, "c2": run_ours_c2, "c3": run_ours_c3, "c4": run_ours_c4,
-                  "c5": run_ours_c5, "c1bwd": run_ours_c1bwd}[args.config]
+                  "c5": run_ours_c5, "c1bwd": run_ours_c1bwd, "ring": run_ours_ring}[args.config]
         out = runner(args, rank, world, local)
         if rank == 0:
             print(json.dumps(out), flush=True)

@@ -148,6 +148,24 @@ int tssm_streaming_step(const void* x, const void* dt, void* h, const void* A_lo
                         int io_dtype, tssm_stream_t stream);
 
 /*
+ * Streaming ring-buffer ingest + forward fill + one step.  Replaces
+ * streaming_interp_then_ssm_kernel (streaming_inference_kernel.py:74-156),
+ * without its ring_head race (:115-117): one CTA owns each stream.
+ *   ring_V, ring_M [Bsz,K+1,H] f32, ring_tau [Bsz,K+1] f32, ring_head [Bsz]
+ *   int32 (all updated in place); v_new, m_new [Bsz,H] f32; tau_new [Bsz];
+ *   h [Bsz,H] f32 in place; Abar, Bbar, Dskip [H]; C [Bsz,H]; y [Bsz,H] out.
+ * The event goes to slot (head+1) % (K+1); per block_h-wide feature tile the
+ * nearest older slot whose mask sum exceeds 0.5 supplies vhat when the
+ * event's own tile mask sum is below 0.5; then h <- Abar h + Bbar vhat,
+ * y = C h + Dskip vhat.  All contiguous.  K+1 <= 64.
+ */
+int tssm_ring_ingest_step(void* ring_V, void* ring_M, void* ring_tau, void* ring_head,
+                          const void* v_new, const void* m_new, const void* tau_new, void* h,
+                          const void* Abar, const void* Bbar, const void* C, const void* Dskip,
+                          void* y, int64_t Bsz, int64_t H, int64_t K, int64_t block_h,
+                          tssm_stream_t stream);
+
+/*
  * Multi-head chunked scan with an outer-product state h[b,h,p,n] on tcgen05
  * tensor cores.  Replaces the multi-head chunked associative scan
  * multihead_ssm_fwd_local_kernel / multihead_ssm_carry_scan_kernel /

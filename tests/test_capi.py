@@ -71,3 +71,10 @@ def test_compat_namespaces_mirror_reference_names():
     # kernel objects are launched with [grid]
     fn = compat.discretize_kernel.zoh_discretize_diag_kernel[(1, 1, 1)]
     assert callable(fn)
+
+
+def test_streaming_ring_refuses_cpu():
+    import torch
+    import triton_ssm_b200 as ts
+    with pytest.raises(ValueError):
+        ts.StreamingRing(2, 8, 3, torch.ones(8), torch.ones(8), torch.ones(8), device="cpu")

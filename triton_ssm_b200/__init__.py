@@ -6,6 +6,7 @@ hand-written CUDA kernel through the C ABI in ``include/tssm.h``.
 from ._lib import load_library, LIB_PATH, TSSMError  # noqa: F401
 from .ops import *  # noqa: F401,F403
 from .ops import __all__ as _ops_all
+from .streaming import StreamingRing  # noqa: F401
 
-__all__ = ["load_library", "LIB_PATH", "TSSMError"] + list(_ops_all)
+__all__ = ["load_library", "LIB_PATH", "TSSMError", "StreamingRing"] + list(_ops_all)
 __version__ = "0.1.0"

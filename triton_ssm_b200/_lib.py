@@ -34,6 +34,7 @@ SIGNATURES = {
     "tssm_zoh_discretize_bwd": ([P] * 9 + [I64] * 3 + [P], I32),
     "tssm_streaming_inplace": ([P] * 7 + [I64] * 2 + [I64] * 3 + [I32, P], I32),
     "tssm_streaming_step": ([P] * 8 + [I64] * 4 + [I32, P], I32),
+    "tssm_ring_ingest_step": ([P] * 13 + [I64] * 4 + [P], I32),
     "tssm_multihead_ssd": ([P] * 10 + [I64] * 5 + [I32, P], I32),
     "tssm_multihead_diag": ([P] * 7 + [I64] * 4 + [I32, I32, P], I32),
     "tssm_ssd_carry_fixup": ([P, P, I64, I64, P, P, P, P] + [I64] * 5 + [P], I32),

@@ -14,7 +14,7 @@ from ._lib import call, dtype_code, ptr, stream_of
 __all__ = ["zoh_discretize", "ssm_forward", "selective_scan", "streaming_ssm_inplace",
            "streaming_step", "multihead_ssm", "check_device_status", "fused_time_aware_interp",
            "fused_interp_ssm_step", "fused_interp_ssm", "linspace_queries", "interp_ssm_workspace_bytes",
-           "ssd_carry_fixup", "ssm_backward", "zoh_discretize_bwd"]
+           "ssd_carry_fixup", "ssm_backward", "zoh_discretize_bwd", "streaming_interp_then_ssm"]
 
 
 def _cuda(*ts):
@@ -221,6 +221,46 @@ def streaming_step(x, dt, h, A_log, B, C, D, y=None):
 
 
 _BDISC = {"euler": 0, "zoh": 1}
+
+
+def streaming_interp_then_ssm(ring_V, ring_M, ring_tau, ring_head, v_new, m_new, tau_new, h, Abar, Bbar, C, D,
+                              y=None, BLOCK_H=128):
+    """Ring-buffer ingest + forward fill + one step
+    (``streaming_inference_kernel.py:74-156``), race-free.
+
+    ring_V, ring_M [Bt,K+1,H] f32, ring_tau [Bt,K+1] f32, ring_head [Bt] int32
+    and h [Bt,H] f32 are updated in place; v_new, m_new, C [Bt,H]; tau_new [Bt];
+    Abar, Bbar, D [H].  ``BLOCK_H`` is the feature-tile width over which mask
+    sums decide "observed" (the reference's H-block; it changes results).
+    Returns y [Bt,H].
+    """
+    _cuda(ring_V, ring_M, ring_tau, ring_head, v_new, m_new, tau_new, h, Abar, Bbar, C, D, y)
+    for t, n in ((ring_V, "ring_V"), (ring_M, "ring_M"), (ring_tau, "ring_tau"), (v_new, "v_new"),
+                 (m_new, "m_new"), (tau_new, "tau_new"), (h, "h"), (Abar, "Abar"), (Bbar, "Bbar"), (C, "C"),
+                 (D, "D")):
+        _need(t, (torch.float32,), n)
+    _need(ring_head, (torch.int32,), "ring_head")
+    if ring_V.dim() != 3:
+        raise ValueError("streaming_interp_then_ssm: ring_V must be [Bt,K+1,H]")
+    Bt, KR, H = ring_V.shape
+    shapes = ((ring_M, (Bt, KR, H)), (ring_tau, (Bt, KR)), (ring_head, (Bt,)), (v_new, (Bt, H)), (m_new, (Bt, H)),
+              (tau_new, (Bt,)), (h, (Bt, H)), (Abar, (H,)), (Bbar, (H,)), (C, (Bt, H)), (D, (H,)))
+    for t, shp in shapes:
+        if tuple(t.shape) != shp:
+            raise ValueError("streaming_interp_then_ssm: expected shape %s, got %s" % (shp, tuple(t.shape)))
+    for t in (ring_V, ring_M, ring_tau, ring_head, h):
+        if not t.is_contiguous():
+            raise ValueError("streaming_interp_then_ssm: ring tensors and h are updated in place and must be "
+                             "contiguous")
+    v_new, m_new, tau_new, Abar, Bbar, C, D = (t.contiguous() for t in (v_new, m_new, tau_new, Abar, Bbar, C, D))
+    if y is None:
+        y = torch.empty_like(v_new)
+    elif tuple(y.shape) != (Bt, H) or y.dtype != torch.float32 or not y.is_contiguous():
+        raise ValueError("streaming_interp_then_ssm: y must be a contiguous f32 [Bt,H] tensor")
+    call("tssm_ring_ingest_step", ptr(ring_V), ptr(ring_M), ptr(ring_tau), ptr(ring_head), ptr(v_new), ptr(m_new),
+         ptr(tau_new), ptr(h), ptr(Abar), ptr(Bbar), ptr(C), ptr(D), ptr(y), Bt, H, KR - 1, int(BLOCK_H),
+         stream_of(h))
+    return y
 
 
 def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h0=None,
