@@ -350,6 +350,17 @@ def run_ours_c1(args, rank, world, local):
         alg = 151019520
         kern = "zoh_discretize_kernel + ssm_forward_kernel"
         launches = 2 * args.steps
+    elif args.c1_mode == "pool":
+        # the pair with the mean-pooled logit head fused into the scan's epilogue
+        Wp = torch.randn(Hp, device=dev, generator=g) / math.sqrt(Hp)
+        bp = torch.zeros(1, device=dev)
+
+        def step():
+            Ab, Bb = ts.zoh_discretize(Al, B_exp, dt)
+            ts.ssm_forward(u_exp, Ab, Bb, C_exp, Dz, pool=(Wp, bp))
+        alg = 151019520 + Hp * 4 + 4 + Bt * 4
+        kern = "zoh_discretize_kernel + ssm_forward_kernel (fused mean-pool head)"
+        launches = 2 * args.steps
     else:
         step = lambda: ts.selective_scan(x, dt, A_log, Bs, Cs, D)
         alg = 2642176
@@ -431,6 +442,32 @@ def run_ours_ring(args, rank, world, local):
            "l2": "state + ring 420 MB per rank, larger than the 126 MB L2"}
     return _line(args, world, METRIC, world * S * H / t_step, t_step, "f32", cfg, alg, "ring_ingest_step_kernel",
                  "ring_ingest_step.md", clocks)
+
+
+def run_ours_dtproj(args, rank, world, local):
+    """Delta-t projection fused into the per-channel ZOH discretisation, H = D*N
+    = 1024 as in config 1, dt_rank 64, f32, batch 16 so a step moves more than
+    the L2 holds."""
+    import triton_ssm_b200 as ts
+    dev = torch.device("cuda", local)
+    Bt, T, H, R = args.batch or 16, 1024, 1024, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(31 + rank)
+    dt_raw = torch.randn(Bt, T, R, device=dev, generator=g)
+    W = torch.randn(R, H, device=dev, generator=g) / 8.0
+    bias = torch.randn(H, device=dev, generator=g) - 3.0
+    A_log = torch.log(torch.arange(1, 17, device=dev, dtype=torch.float32)).repeat(64)
+    B = torch.randn(Bt, T, H, device=dev, generator=g)
+    step = lambda: ts.zoh_discretize_dtproj(A_log, B, dt_raw, W, bias, 1e-3, 1e-1)
+    t_step, clocks = _timed(args, world, dev, step)
+    n = Bt * T * H
+    alg = n * 4 * 3 + Bt * T * R * 4 + R * H * 4 + H * 8
+    cfg = {"workload": "delta-t projection (dt_rank %d, softplus, clamp [1e-3, 0.1]) fused into the per-channel "
+                       "ZOH discretisation, B%d T%d H%d f32" % (R, Bt, T, H),
+           "global_batch": Bt * world, "seq_len": T, "parallelism": "batch, %d rank(s)" % world,
+           "l2": "B in + Abar, Bbar out: %d MB per step, larger than the 126 MB L2" % (n * 12 // 1000000)}
+    return _line(args, world, METRIC, world * n / t_step, t_step, "f32", cfg, alg, "dt_project_kernel<disc>",
+                 None, clocks)
 
 
 def run_ours_c4(args, rank, world, local):
@@ -538,9 +575,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s pre-timing load")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c1bwd", "ring"], default="c2",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c1bwd", "ring", "dtproj"], default="c2",
                     help="workload (default c2, the headline; the others are for measurement notes)")
-    ap.add_argument("--c1-mode", choices=["pair", "fused"], default="pair")
+    ap.add_argument("--c1-mode", choices=["pair", "fused", "pool"], default="pair")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays of the step")
     ap.add_argument("--seq-len", type=int, default=None, help="config 4: override L (multiple of 16384)")
     args = ap.parse_args()
@@ -561,7 +598,8 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         runner = {"c1": run_ours_c1, "c2": run_ours_c2, "c3": run_ours_c3, "c4": run_ours_c4,
-                  "c5": run_ours_c5, "c1bwd": run_ours_c1bwd, "ring": run_ours_ring}[args.config]
+                  "c5": run_ours_c5, "c1bwd": run_ours_c1bwd, "ring": run_ours_ring,
+                  "dtproj": run_ours_dtproj}[args.config]
         out = runner(args, rank, world, local)
         if rank == 0:
             print(json.dumps(out), flush=True)

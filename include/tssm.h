@@ -79,6 +79,29 @@ int tssm_ssm_forward(const void* u, const void* A, const void* B, const void* C,
                      int dtype, tssm_stream_t stream);
 
 /*
+ * The diagonal scan with the mean-pooled logit head fused into its epilogue:
+ * the composition ssm_forward (ssm_scan.py:239-264) -> mean_pool_logit_kernel
+ * (streaming_inference_kernel.py:159-194) applied to y, without re-reading y.
+ *   Arguments as tssm_ssm_forward, plus poolW [H] f32, pool_bias [1] f32 and
+ *   pool_out [Bsz] f32: pool_out[b] = sum_{t,h} poolW[h] y[b,t,h] / (L*H + 1e-9)
+ *   + pool_bias[0] (y as stored, in dtype).  pool_out is summed with float
+ *   atomics, so its last bits may vary between runs.
+ */
+int tssm_ssm_forward_pool(const void* u, const void* A, const void* B, const void* C, const void* D,
+                          void* y, void* h, const void* poolW, const void* pool_bias, void* pool_out,
+                          int64_t Bsz, int64_t L, int64_t H, int dtype, tssm_stream_t stream);
+
+/*
+ * Mean-pooled logit head.  Replaces mean_pool_logit_kernel
+ * (streaming_inference_kernel.py:159-194).
+ *   x [Bsz,T,H] (dtype TSSM_F32 or TSSM_BF16), W [H] f32, bias [1] f32 ->
+ *   out [Bsz] f32 = sum_{t,h} W[h] x[b,t,h] / (T*H + 1e-9) + bias[0].
+ *   Contiguous.  Summed with float atomics (last bits may vary between runs).
+ */
+int tssm_mean_pool_logit(const void* x, const void* W, const void* bias, void* out,
+                         int64_t Bsz, int64_t T, int64_t H, int dtype, tssm_stream_t stream);
+
+/*
  * Backward of the diagonal scan.  Replaces ssm_backward (ssm_scan.py:267-289),
  * i.e. ssm_bwd_local_kernel / ssm_bwd_carry_scan_kernel / ssm_bwd_apply_kernel
  * (ssm_scan.py:127-231), with one launch and no intermediate buffers.
@@ -105,6 +128,29 @@ int tssm_ssm_backward(const void* u, const void* A, const void* B, const void* C
 int tssm_zoh_discretize_bwd(const void* A_log, const void* B, const void* dt, const void* Abar,
                             const void* dAbar, const void* dBbar, void* dA_log, void* dB, void* ddt,
                             int64_t Bsz, int64_t T, int64_t H, tssm_stream_t stream);
+
+/*
+ * Delta-t projection.  Replaces dt_project_softplus_kernel
+ * (discretize_kernel.py:165-213), which does not compile in the reference.
+ *   dt_raw [Bsz,T,R] f32, W [R,H] f32, bias [H] f32 -> dt_out [Bsz,T,H] f32:
+ *   dt = clamp(log(1 + exp(dt_raw.W + bias)), dt_min, dt_max).  R <= 256.
+ */
+int tssm_dt_project_softplus(const void* dt_raw, const void* W, const void* bias, void* dt_out,
+                             int64_t Bsz, int64_t T, int64_t H, int64_t R, double dt_min, double dt_max,
+                             tssm_stream_t stream);
+
+/*
+ * The delta-t projection fused into the ZOH discretisation with one dt per
+ * (b, t, h): no reference counterpart as one kernel; it composes
+ * dt_project_softplus_kernel (discretize_kernel.py:165-213) with the
+ * arithmetic of zoh_discretize_diag_kernel (:38-54) at a per-channel dt.
+ *   A_log [H], B [Bsz,T,H], dt_raw [Bsz,T,R], W [R,H], bias [H]; all f32.
+ *   Abar, Bbar [Bsz,T,H] f32 out; dt_out [Bsz,T,H] f32 or NULL (not stored).
+ */
+int tssm_zoh_discretize_dtproj(const void* A_log, const void* B, const void* dt_raw, const void* W,
+                               const void* bias, void* Abar, void* Bbar, void* dt_out,
+                               int64_t Bsz, int64_t T, int64_t H, int64_t R, double dt_min, double dt_max,
+                               tssm_stream_t stream);
 
 /*
  * Fused ZOH discretisation + diagonal scan + readout over an N-wide state per

@@ -49,3 +49,28 @@ def zoh_discretize_bwd(A_log, B, dt, Abar, dAbar, dBbar):
     dA_log = (da * (-neg_a)).reshape(-1, A_log.shape[0]).sum(0)       # :151,156
     dB = dBbar * em1 / (a + 1e-12)                     # :154
     return dA_log, dB, ddt
+
+
+def dt_project_softplus(dt_raw, W, bias, dt_min, dt_max):
+    """``dt_project_softplus_kernel`` (``discretize_kernel.py:165-213``).
+
+    dt_raw [Bt,T,R], W [R,H], bias [H] -> dt [Bt,T,H] f32:
+        acc = sum_r dt_raw[..., r] * W[r, :] + bias       (:193-204)
+        dt  = clamp(log(1 + exp(acc)), dt_min, dt_max)   (:207-210)
+    The softplus is written as there, so a large acc overflows exp to inf and
+    clamps to dt_max.  The reference kernel does not compile (it indexes a
+    block tensor with a Python int at :201), so this restates its evident
+    intent; parity for this function is pinned only by this restatement.
+    """
+    acc = torch.einsum("btr,rh->bth", dt_raw.float(), W.float()) + bias.float()
+    dt = torch.log(1.0 + torch.exp(acc))
+    return torch.clamp(dt, min=dt_min, max=dt_max)
+
+
+def zoh_discretize_dt(A_log, B, dt, variant="fp32"):
+    """ZOH discretisation with one dt per (b, t, h) -- the per-channel dt that
+    ``dt_project_softplus`` produces -- using the arithmetic of
+    ``discretize_kernel.py:38-54``.  Returns (Abar, Bbar) f32 [Bt,T,H]."""
+    a = -torch.exp(A_log.float())
+    x = dt.float() * a
+    return torch.exp(x), expm1_ref(x, variant) / (a + 1e-12) * B.float()

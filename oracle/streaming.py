@@ -75,3 +75,16 @@ def ring_interp_then_ssm(ring_V, ring_M, ring_tau, ring_head, v_new, m_new, tau_
             h[b, sl] = hn
             y[b, sl] = C[b, sl].float() * hn + D[sl].float() * vh
     return y
+
+
+def mean_pool_logit(h, W, bias):
+    """``mean_pool_logit_kernel`` (``streaming_inference_kernel.py:159-194``):
+    out[b] = sum_{t,h} W[h] * h[b,t,h] / (T*H + 1e-9) + bias[0].
+
+    The reference kernel does not run under the interpreter (it indexes a block
+    tensor with a Python int at :190), so this restates its evident intent;
+    parity for this function is pinned only by this restatement.
+    """
+    Bt, T, H = h.shape
+    acc = (h.double() * W.double()).sum(dim=(1, 2))
+    return (acc / (T * H + 1e-9) + bias.double().reshape(-1)[0]).float()

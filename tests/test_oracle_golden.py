@@ -156,3 +156,25 @@ def test_discretize_bwd():
     assert rel_err(dA, g["dA_log"]) < TOL_FP32
     assert rel_err(dB, g["dB"]) < TOL_FP32
     assert rel_err(ddt, g["ddt"]) < TOL_FP32
+
+
+def test_dt_project_softplus_restatement():
+    """The restated projection (the reference kernel does not compile): the
+    softplus is log(1 + exp(x)) as written there, a large pre-activation
+    overflows to inf and clamps to DT_MAX, and per-channel discretisation with
+    a dt that is constant over H equals the reference's shared-dt discretisation."""
+    g = torch.Generator().manual_seed(0)
+    dt_raw = torch.randn(2, 5, 3, generator=g)
+    W = torch.randn(3, 7, generator=g)
+    bias = torch.randn(7, generator=g)
+    dt = oracle.dt_project_softplus(dt_raw, W, bias, 1e-3, 0.5)
+    acc = dt_raw @ W + bias
+    assert torch.allclose(dt, torch.clamp(torch.nn.functional.softplus(acc), 1e-3, 0.5), rtol=1e-6, atol=1e-7)
+    big = oracle.dt_project_softplus(dt_raw * 1e4, W, bias, 1e-3, 0.5)
+    assert torch.isfinite(big).all() and float(big.max()) == 0.5
+    A_log = torch.log(torch.empty(7).uniform_(0.5, 16, generator=g))
+    B = torch.randn(2, 5, 7, generator=g)
+    dts = torch.rand(2, 5, generator=g)
+    a1, b1 = oracle.zoh_discretize_dt(A_log, B, dts[..., None].expand(2, 5, 7))
+    a2, b2 = oracle.zoh_discretize(A_log, B, dts)
+    assert torch.equal(a1, a2) and torch.equal(b1, b2)

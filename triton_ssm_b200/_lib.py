@@ -21,6 +21,7 @@ _DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16, tor
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
 I32 = ctypes.c_int
+F64 = ctypes.c_double
 
 # name -> argument types (the trailing stream is a c_void_p).  Must match include/tssm.h.
 SIGNATURES = {
@@ -31,7 +32,11 @@ SIGNATURES = {
     "tssm_ssm_forward": ([P] * 7 + [I64] * 3 + [I32, P], I32),
     "tssm_selective_scan": ([P] * 8 + [I64] * 4 + [P], I32),
     "tssm_ssm_backward": ([P] * 10 + [I64] * 3 + [I32, P], I32),
+    "tssm_ssm_forward_pool": ([P] * 10 + [I64] * 3 + [I32, P], I32),
+    "tssm_mean_pool_logit": ([P] * 4 + [I64] * 3 + [I32, P], I32),
     "tssm_zoh_discretize_bwd": ([P] * 9 + [I64] * 3 + [P], I32),
+    "tssm_dt_project_softplus": ([P] * 4 + [I64] * 4 + [F64, F64, P], I32),
+    "tssm_zoh_discretize_dtproj": ([P] * 8 + [I64] * 4 + [F64, F64, P], I32),
     "tssm_streaming_inplace": ([P] * 7 + [I64] * 2 + [I64] * 3 + [I32, P], I32),
     "tssm_streaming_step": ([P] * 8 + [I64] * 4 + [I32, P], I32),
     "tssm_ring_ingest_step": ([P] * 13 + [I64] * 4 + [P], I32),

@@ -49,6 +49,12 @@ template <> struct io<__half> {
 
 template <typename T>
 __device__ __forceinline__ float ldf(const T* p) { return io<T>::ld(p); }
+// v rounded to T and back (what a T tensor holds after storing v).
+template <typename T>
+__device__ __forceinline__ float io_round(float v) {
+  if constexpr (std::is_same<T, float>::value) return v;
+  else { T t; io<T>::st(&t, v); return io<T>::ld(&t); }
+}
 template <typename T>
 __device__ __forceinline__ void stf(T* p, float v) { io<T>::st(p, v); }
 

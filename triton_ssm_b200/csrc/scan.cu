@@ -14,14 +14,20 @@
 namespace tssm {
 namespace {
 
-template <typename T, int S, int NW>
+// Optional fused mean-pool head (POOL): every CTA adds
+// sum_{t, its channels} poolW[ch] * y[b,t,ch] * pool_inv to pool_out[b] (plus the
+// bias once per batch row), the composition ssm_forward -> mean_pool_logit_kernel
+// (streaming_inference_kernel.py:159-194) over y without re-reading it.
+template <typename T, int S, int NW, bool POOL>
 __global__ void __launch_bounds__(NW * 32, 1) ssm_forward_kernel(
     const T* __restrict__ u, const T* __restrict__ A, const T* __restrict__ B,
     const T* __restrict__ C, const T* __restrict__ D, T* __restrict__ y, T* __restrict__ h,
-    int64_t L, int64_t H) {
+    int64_t L, int64_t H, const float* __restrict__ poolW, const float* __restrict__ pool_bias,
+    float* __restrict__ pool_out, float pool_inv) {
   __shared__ float s_a[NW][32];
   __shared__ float s_x[NW][32];
   __shared__ float s_carry[32];
+  __shared__ float s_pool[NW];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t ch = (int64_t)blockIdx.x * 32 + lane;
@@ -37,6 +43,8 @@ __global__ void __launch_bounds__(NW * 32, 1) ssm_forward_kernel(
   const int Hi = (int)H;
   const int Li = (int)L;
   const float dv = valid ? ldf(D + ch) : 0.f;
+  const float pw = (POOL && valid) ? poolW[ch] : 0.f;
+  float pacc = 0.f;
   float carry = 0.f;
   for (int t0 = 0; t0 < Li; t0 += NW * S) {
     const int ts = t0 + warp * S;
@@ -73,12 +81,25 @@ __global__ void __launch_bounds__(NW * 32, 1) ssm_forward_kernel(
       if (valid && t < Li) {
         const int off = t * Hi;
         if (hb) stf(hb + off, hs);
-        stf(yb + off, ldf(Cb + off) * hs + dv * uu[i]);
+        const float yv = ldf(Cb + off) * hs + dv * uu[i];
+        stf(yb + off, yv);
+        if (POOL) pacc += pw * io_round<T>(yv);
       }
     }
     if (warp == NW - 1) s_carry[lane] = hs;
     __syncthreads();
     carry = s_carry[lane];
+  }
+  if (POOL) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) pacc += __shfl_xor_sync(0xffffffffu, pacc, o);
+    if (lane == 0) s_pool[warp] = pacc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s2 = 0.f;
+      for (int w = 0; w < NW; ++w) s2 += s_pool[w];
+      atomicAdd(pool_out + blockIdx.y, s2 * pool_inv + (blockIdx.x == 0 ? pool_bias[0] : 0.f));
+    }
   }
 }
 
@@ -268,10 +289,10 @@ int dispatch_diag(const void* u, const void* A_log, const void* B, const void* C
 }  // namespace
 }  // namespace tssm
 
-extern "C" int tssm_ssm_forward(const void* u, const void* A, const void* B, const void* C,
-                                const void* D, void* y, void* h, int64_t Bsz, int64_t L,
-                                int64_t H, int dtype, tssm_stream_t stream) {
-  using namespace tssm;
+namespace tssm {
+int ssm_forward_impl(const void* u, const void* A, const void* B, const void* C, const void* D, void* y, void* h,
+                     const void* poolW, const void* pool_bias, void* pool_out, int64_t Bsz, int64_t L, int64_t H,
+                     int dtype, tssm_stream_t stream) {
   TSSM_REQUIRE(Bsz >= 0 && L >= 0 && H >= 0, "ssm_forward: negative size");
   if (Bsz * L * H == 0) return TSSM_OK;
   TSSM_REQUIRE(u && A && B && C && D && y, "ssm_forward: null pointer");
@@ -280,19 +301,49 @@ extern "C" int tssm_ssm_forward(const void* u, const void* A, const void* B, con
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   constexpr int S = 16, NW = 16;
   dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
+  const float pool_inv = (float)(1.0 / ((double)L * (double)H + 1e-9));
+  // With the pooled head the kernel walks shorter per-warp runs (S=8) with twice
+  // the warps: at S=16 the extra accumulator leaves too few registers for the
+  // loads in flight (measured: +18 us against +6 us at config-1 size).
+  const bool pool = pool_out != nullptr;
+  const int nthr = pool ? 32 * 32 : NW * 32;
   if (dtype == TSSM_F32) {
-    ssm_forward_kernel<float, S, NW><<<grid, NW * 32, 0, st>>>(
-        (const float*)u, (const float*)A, (const float*)B, (const float*)C, (const float*)D,
-        (float*)y, (float*)h, L, H);
+    auto kern = pool ? ssm_forward_kernel<float, 8, 32, true> : ssm_forward_kernel<float, S, NW, false>;
+    kern<<<grid, nthr, 0, st>>>((const float*)u, (const float*)A, (const float*)B, (const float*)C,
+                                (const float*)D, (float*)y, (float*)h, L, H, (const float*)poolW,
+                                (const float*)pool_bias, (float*)pool_out, pool_inv);
   } else if (dtype == TSSM_BF16) {
     using bf = __nv_bfloat16;
-    ssm_forward_kernel<bf, S, NW><<<grid, NW * 32, 0, st>>>(
-        (const bf*)u, (const bf*)A, (const bf*)B, (const bf*)C, (const bf*)D, (bf*)y, (bf*)h, L, H);
+    auto kern = pool ? ssm_forward_kernel<bf, 8, 32, true> : ssm_forward_kernel<bf, S, NW, false>;
+    kern<<<grid, nthr, 0, st>>>((const bf*)u, (const bf*)A, (const bf*)B, (const bf*)C, (const bf*)D, (bf*)y,
+                                (bf*)h, L, H, (const float*)poolW, (const float*)pool_bias, (float*)pool_out,
+                                pool_inv);
   } else {
     set_error("ssm_forward: dtype must be f32 or bf16 (got %d)", dtype);
     return TSSM_ERR_INVALID;
   }
   return check_launch("ssm_forward");
+}
+}  // namespace tssm
+
+extern "C" int tssm_ssm_forward(const void* u, const void* A, const void* B, const void* C,
+                                const void* D, void* y, void* h, int64_t Bsz, int64_t L,
+                                int64_t H, int dtype, tssm_stream_t stream) {
+  return tssm::ssm_forward_impl(u, A, B, C, D, y, h, nullptr, nullptr, nullptr, Bsz, L, H, dtype, stream);
+}
+
+extern "C" int tssm_ssm_forward_pool(const void* u, const void* A, const void* B, const void* C, const void* D,
+                                     void* y, void* h, const void* poolW, const void* pool_bias, void* pool_out,
+                                     int64_t Bsz, int64_t L, int64_t H, int dtype, tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(Bsz >= 0 && L >= 0 && H >= 0, "ssm_forward_pool: negative size");
+  TSSM_REQUIRE(poolW && pool_bias && pool_out, "ssm_forward_pool: null pool pointer");
+  if (Bsz == 0) return TSSM_OK;
+  if (L * H == 0)   // nothing to pool: the logit is the bias
+    return tssm_mean_pool_logit(nullptr, poolW, pool_bias, pool_out, Bsz, L, H, TSSM_F32, stream);
+  if (cudaMemsetAsync(pool_out, 0, (size_t)Bsz * sizeof(float), reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return check_launch("ssm_forward_pool: clear pool_out");
+  return ssm_forward_impl(u, A, B, C, D, y, h, poolW, pool_bias, pool_out, Bsz, L, H, dtype, stream);
 }
 
 extern "C" int tssm_selective_scan(const void* x, const void* dt, const void* A_log, const void* B,

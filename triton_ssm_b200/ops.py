@@ -14,7 +14,8 @@ from ._lib import call, dtype_code, ptr, stream_of
 __all__ = ["zoh_discretize", "ssm_forward", "selective_scan", "streaming_ssm_inplace",
            "streaming_step", "multihead_ssm", "check_device_status", "fused_time_aware_interp",
            "fused_interp_ssm_step", "fused_interp_ssm", "linspace_queries", "interp_ssm_workspace_bytes",
-           "ssd_carry_fixup", "ssm_backward", "zoh_discretize_bwd", "streaming_interp_then_ssm"]
+           "ssd_carry_fixup", "ssm_backward", "zoh_discretize_bwd", "streaming_interp_then_ssm",
+           "dt_project_softplus", "zoh_discretize_dtproj", "mean_pool_logit"]
 
 
 def _cuda(*ts):
@@ -68,16 +69,72 @@ def zoh_discretize(A_log, B, dt, out=None):
     return Abar, Bbar
 
 
-def ssm_forward(u, A, B, C, D, BLK=256, store_h=True):
+def _dtproj_args(dt_raw, W, bias, name):
+    for t, n in ((dt_raw, "dt_raw"), (W, "W"), (bias, "bias")):
+        _need(t, (torch.float32,), n)
+    if dt_raw.dim() != 3 or W.dim() != 2 or bias.dim() != 1:
+        raise ValueError("%s: expected dt_raw [Bt,T,R], W [R,H], bias [H]" % name)
+    Bt, T, R = dt_raw.shape
+    if W.shape[0] != R or bias.shape[0] != W.shape[1]:
+        raise ValueError("%s: shape mismatch (dt_raw %s, W %s, bias %s)" % (name, tuple(dt_raw.shape),
+                                                                           tuple(W.shape), tuple(bias.shape)))
+    return Bt, T, W.shape[1], R
+
+
+def dt_project_softplus(dt_raw, W, bias, DT_MIN=1e-3, DT_MAX=1e-1, out=None):
+    """Delta-t projection (``discretize_kernel.py:165-213``):
+    dt = clamp(log(1 + exp(dt_raw @ W + bias)), DT_MIN, DT_MAX).
+
+    dt_raw [Bt,T,R], W [R,H], bias [H], f32; R <= 256.  Returns dt [Bt,T,H].
+    """
+    _cuda(dt_raw, W, bias, out)
+    Bt, T, H, R = _dtproj_args(dt_raw, W, bias, "dt_project_softplus")
+    dt_raw, W, bias = (t.contiguous() for t in (dt_raw, W, bias))
+    if out is None:
+        out = torch.empty(Bt, T, H, device=dt_raw.device, dtype=torch.float32)
+    elif tuple(out.shape) != (Bt, T, H) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("dt_project_softplus: out must be a contiguous f32 [Bt,T,H] tensor")
+    call("tssm_dt_project_softplus", ptr(dt_raw), ptr(W), ptr(bias), ptr(out), Bt, T, H, R, float(DT_MIN),
+         float(DT_MAX), stream_of(dt_raw))
+    return out
+
+
+def zoh_discretize_dtproj(A_log, B, dt_raw, W, bias, DT_MIN=1e-3, DT_MAX=1e-1, return_dt=False):
+    """The delta-t projection fused into the ZOH discretisation, one dt per
+    (b, t, h): ``dt_project_softplus`` then ``discretize_kernel.py:38-54`` with
+    that dt, in one launch (dt is not written unless ``return_dt``).
+
+    A_log [H]; B [Bt,T,H]; dt_raw [Bt,T,R]; W [R,H]; bias [H]; all f32.
+    Returns (Abar, Bbar) [Bt,T,H] (and dt when ``return_dt``).
+    """
+    _cuda(A_log, B, dt_raw, W, bias)
+    Bt, T, H, R = _dtproj_args(dt_raw, W, bias, "zoh_discretize_dtproj")
+    _need(A_log, (torch.float32,), "A_log")
+    _need(B, (torch.float32,), "B")
+    if tuple(B.shape) != (Bt, T, H) or tuple(A_log.shape) != (H,):
+        raise ValueError("zoh_discretize_dtproj: expected A_log [H] and B [Bt,T,H]")
+    A_log, B, dt_raw, W, bias = (t.contiguous() for t in (A_log, B, dt_raw, W, bias))
+    Abar, Bbar = torch.empty_like(B), torch.empty_like(B)
+    dt = torch.empty_like(B) if return_dt else None
+    call("tssm_zoh_discretize_dtproj", ptr(A_log), ptr(B), ptr(dt_raw), ptr(W), ptr(bias), ptr(Abar), ptr(Bbar),
+         ptr(dt), Bt, T, H, R, float(DT_MIN), float(DT_MAX), stream_of(B))
+    return (Abar, Bbar, dt) if return_dt else (Abar, Bbar)
+
+
+def ssm_forward(u, A, B, C, D, BLK=256, store_h=True, pool=None):
     """Diagonal selective scan (``ssm_scan.py:239-264``).
 
     u, A, B, C [Bt,L,H]; D [H]; f32 or bf16 (all the same dtype).
     Returns (y, h) [Bt,L,H] (h is None when ``store_h`` is False).  ``BLK``
     is accepted for signature compatibility; the single-pass kernel has no
     block-size dependence.
+
+    ``pool=(W, bias)`` (W [H] f32, bias [1] f32) fuses the mean-pooled logit
+    head (``streaming_inference_kernel.py:159-194``) over y into the scan and
+    returns (y, h, logits [Bt]).
     """
     del BLK
-    _cuda(u, A, B, C, D)
+    _cuda(u, A, B, C, D, *(pool or ()))
     _need(u, (torch.float32, torch.bfloat16), "u")
     for t in (A, B, C, D):
         if t.dtype != u.dtype:
@@ -89,9 +146,41 @@ def ssm_forward(u, A, B, C, D, BLK=256, store_h=True):
     Bt, L, H = u.shape
     y = torch.empty_like(u)
     h = torch.empty_like(u) if store_h else None
-    call("tssm_ssm_forward", ptr(u), ptr(A), ptr(B), ptr(C), ptr(D), ptr(y), ptr(h), Bt, L, H,
-         dtype_code(u), stream_of(u))
-    return y, h
+    if pool is None:
+        call("tssm_ssm_forward", ptr(u), ptr(A), ptr(B), ptr(C), ptr(D), ptr(y), ptr(h), Bt, L, H,
+             dtype_code(u), stream_of(u))
+        return y, h
+    W, bias = _pool_args(pool[0], pool[1], H, "ssm_forward")
+    logits = torch.empty(Bt, device=u.device, dtype=torch.float32)
+    call("tssm_ssm_forward_pool", ptr(u), ptr(A), ptr(B), ptr(C), ptr(D), ptr(y), ptr(h), ptr(W), ptr(bias),
+         ptr(logits), Bt, L, H, dtype_code(u), stream_of(u))
+    return y, h, logits
+
+
+def _pool_args(W, bias, H, name):
+    _need(W, (torch.float32,), "W")
+    _need(bias, (torch.float32,), "bias")
+    if tuple(W.shape) != (H,) or bias.numel() != 1:
+        raise ValueError("%s: pool weight must be [H] and bias one element" % name)
+    return W.contiguous(), bias.reshape(1).contiguous()
+
+
+def mean_pool_logit(h, W, bias):
+    """Mean-pooled logit head (``streaming_inference_kernel.py:159-194``):
+    out[b] = sum_{t,h} W[h] h[b,t,h] / (T*H + 1e-9) + bias.
+
+    h [Bt,T,H] f32 or bf16; W [H] f32; bias one element, f32.  Returns [Bt] f32.
+    """
+    _cuda(h, W, bias)
+    _need(h, (torch.float32, torch.bfloat16), "h")
+    if h.dim() != 3:
+        raise ValueError("mean_pool_logit: expected h [Bt,T,H]")
+    Bt, T, H = h.shape
+    W, bias = _pool_args(W, bias, H, "mean_pool_logit")
+    h = h.contiguous()
+    out = torch.empty(Bt, device=h.device, dtype=torch.float32)
+    call("tssm_mean_pool_logit", ptr(h), ptr(W), ptr(bias), ptr(out), Bt, T, H, dtype_code(h), stream_of(h))
+    return out
 
 
 def ssm_backward(u, A, B, C, h, dY, BLK=256):
