@@ -467,7 +467,7 @@ def run_ours_dtproj(args, rank, world, local):
            "global_batch": Bt * world, "seq_len": T, "parallelism": "batch, %d rank(s)" % world,
            "l2": "B in + Abar, Bbar out: %d MB per step, larger than the 126 MB L2" % (n * 12 // 1000000)}
     return _line(args, world, METRIC, world * n / t_step, t_step, "f32", cfg, alg, "dt_project_kernel<disc>",
-                 None, clocks)
+                 "dt_project_discretize.md", clocks)
 
 
 def run_ours_c4(args, rank, world, local):
