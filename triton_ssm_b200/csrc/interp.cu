@@ -16,6 +16,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace tssm {
 #ifdef TSSM_INTERP_TRACE
@@ -23,7 +24,7 @@ namespace tssm {
 __device__ unsigned long long g_interp_trace[128 * 8];
 #define IT_TRACE(blk, ev)                                                                          \
   do {                                                                                             \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && (blk) < 128)                    \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && (blk) < 128)                                         \
       g_interp_trace[(blk) * 8 + (ev)] = clock64();                                                \
   } while (0)
 #else
@@ -32,6 +33,8 @@ __device__ unsigned long long g_interp_trace[128 * 8];
   } while (0)
 #endif
 namespace {
+using sm100::named_bar_arrive;
+using sm100::named_bar_sync;
 
 template <typename M>
 __device__ __forceinline__ float mval(const M* p) { return ldf(p); }
@@ -346,8 +349,23 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Two warp groups per CTA, handing blocks of QB queries over through named
+// barriers (hardware barriers, no polling):
+//   warps 4-7  interpolation group: the cp.async pipeline of neighbour tables
+//              and staged observation rows, and (A) the interpolated inputs of
+//              block k into vh[k & 1];
+//   warps 0-3  state group (NPT states of the 32 features per warp): (B) the
+//              recurrence over vh[k & 1] and (C) the readout of block k, while
+//              the other group already builds block k+1.
+// Barrier ids: FULL(k&1) = 1 + (k&1) (interpolation arrives, state waits),
+// FREE(k&1) = 3 + (k&1) (state arrives, interpolation waits before reusing the
+// buffer two blocks later), 5 and 6 inside the interpolation / state group.
+constexpr int SCAN_SW = 4;                         // state warps
+constexpr int SCAN_THREADS = SCAN_SW * 32 + 128;   // + four interpolation warps
+static_assert(SCAN_SW == 4, "the readout sums four per-warp partials");
+
 template <int NPT>
-__global__ void __launch_bounds__(128) interp_ssm_scan_kernel(
+__global__ void __launch_bounds__(SCAN_THREADS) interp_ssm_scan_kernel(
     const float* __restrict__ Vp, const Nbr* __restrict__ tab, const float* __restrict__ A_log,
     const float* __restrict__ Bp, const float* __restrict__ Cp, const float* __restrict__ Dskip,
     const float* __restrict__ dt, float* __restrict__ y, float* __restrict__ h_last, float* __restrict__ vhat_out,
@@ -355,60 +373,38 @@ __global__ void __launch_bounds__(128) interp_ssm_scan_kernel(
   extern __shared__ __align__(16) uint8_t dsm[];
   float (*vt)[RMAX][32] = reinterpret_cast<float (*)[RMAX][32]>(dsm);                 // [2][RMAX][32]
   Nbr (*nb)[QB] = reinterpret_cast<Nbr (*)[QB]>(dsm + 2 * RMAX * 32 * 4);              // [3][QB]
-  float (*vh)[33] = reinterpret_cast<float (*)[33]>(dsm + 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr));
-  float (*yp)[QB][33] = reinterpret_cast<float (*)[QB][33]>(reinterpret_cast<uint8_t*>(vh) + QB * 33 * 4);
+  float (*vhb)[QB][33] = reinterpret_cast<float (*)[QB][33]>(dsm + 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr));
+  float (*yp)[QB][33] = reinterpret_cast<float (*)[QB][33]>(reinterpret_cast<uint8_t*>(vhb) + 2 * QB * 33 * 4);
   __shared__ int s_rlo[2], s_direct[2];   // per staged block: first row, row count (-1: gather directly)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
   const int d0 = blockIdx.x * 32, b = blockIdx.y;
   const int d = d0 + lane;
   const bool dvalid = d < Dm;
-  // one tile per CTA when the 32 features lie in one tile (the staged path); otherwise direct gathers
-  const int tile0 = d0 / FTILE;
-  const bool one_tile = (min(Dm, d0 + 32) - 1) / FTILE == tile0;
-  const bool vec_rows = one_tile && (Dm % 4 == 0) && (d0 + 32 <= Dm);
-  const Nbr* tb = tab + ((int64_t)b * ntiles + (dvalid ? d : d0) / FTILE) * Lq;
-  const Nbr* tb0 = tab + ((int64_t)b * ntiles + tile0) * Lq;
-  const float* Vb = Vp + (int64_t)b * T * Dm;
-  const float dtb = dt[b];
-  static_assert(NPT % 2 == 0, "states per thread come in pairs");
-  constexpr int NP2 = NPT / 2;
-  float2 a2[NP2], c2[NP2], g2[NP2], b2[NP2];
-#pragma unroll
-  for (int k = 0; k < NPT; ++k) {
-    const int n = warp * NPT + k;
-    float ab = 0.f, bb = 0.f, cb = 0.f;
-    if (dvalid && n < N) {
-      const float a = -expf(A_log[(int64_t)d * N + n]);
-      const float x = dtb * a;
-      const float e = expf(x);
-      ab = e;
-      bb = zoh_coeff(x, e, a) * Bp[(int64_t)d * N + n];
-      cb = Cp[(int64_t)d * N + n] * bb;
-    }
-    if (k & 1) { a2[k / 2].y = ab; b2[k / 2].y = bb; c2[k / 2].y = cb; }
-    else { a2[k / 2].x = ab; b2[k / 2].x = bb; c2[k / 2].x = cb; }
-  }
-#pragma unroll
-  for (int k = 0; k < NP2; ++k) g2[k] = make_float2(0.f, 0.f);
-  const float dsk = (Dskip && dvalid) ? Dskip[d] : 0.f;
   const int nblk = (Lq + QB - 1) / QB;
 
-  // table entries of block `blk` -> nb[blk % 3] (one 16-byte copy per query)
-  auto issue_table = [&](int blk) {
-    if (blk < nblk) {
-      const int qs = blk * QB, nq = min(QB, Lq - qs);
-      if (tid < nq) cp_async16(&nb[blk % 3][tid], tb0 + qs + tid);
-    }
-    cp_async_commit();
-  };
-  // row range of block `blk` (its table must be resident) and, when it fits,
-  // the copies of those rows into vt[blk & 1]; one committed group either way
-  auto issue_rows = [&](int blk) {
-    if (blk < nblk && vec_rows) {
-      const int qs = blk * QB, nq = min(QB, Lq - qs);
-      const Nbr* e = nb[blk % 3];
-      // warp 0 reduces the range; broadcast through shared memory
-      if (warp == 0) {
+  if (warp >= SCAN_SW) {
+    // ================================================================ interpolation group
+    const int iw = warp - SCAN_SW, itid = tid - SCAN_SW * 32;
+    // one tile per CTA when the 32 features lie in one tile (the staged path); otherwise direct gathers
+    const int tile0 = d0 / FTILE;
+    const bool one_tile = (min(Dm, d0 + 32) - 1) / FTILE == tile0;
+    const bool vec_rows = one_tile && (Dm % 4 == 0) && (d0 + 32 <= Dm);
+    const Nbr* tb = tab + ((int64_t)b * ntiles + (dvalid ? d : d0) / FTILE) * Lq;
+    const Nbr* tb0 = tab + ((int64_t)b * ntiles + tile0) * Lq;
+    const float* Vb = Vp + (int64_t)b * T * Dm;
+    // table entries of block `blk` -> nb[blk % 3] (one 16-byte copy per query)
+    auto issue_table = [&](int blk) {
+      if (blk < nblk) {
+        const int qs = blk * QB, nq = min(QB, Lq - qs);
+        if (itid < nq) cp_async16(&nb[blk % 3][itid], tb0 + qs + itid);
+      }
+      cp_async_commit();
+    };
+    // row range of block `blk` (its table must be resident), computed by the group's first warp
+    auto issue_rows = [&](int blk) {
+      if (blk < nblk && vec_rows && iw == 0) {
+        const int qs = blk * QB, nq = min(QB, Lq - qs);
+        const Nbr* e = nb[blk % 3];
         int lo = 1 << 30, hi = -1;
         for (int i = lane; i < nq; i += 32) {
           const Nbr x = e[i];
@@ -427,117 +423,188 @@ __global__ void __launch_bounds__(128) interp_ssm_scan_kernel(
           s_direct[blk & 1] = hi >= lo ? (hi - lo + 1 > RMAX ? -1 : hi - lo + 1) : 0;
         }
       }
-      __syncwarp();
-    }
-  };
-  auto copy_rows = [&](int blk) {
-    if (blk < nblk && vec_rows) {
-      const int nrows = s_direct[blk & 1];
-      const int lo = s_rlo[blk & 1];
-      for (int c = tid; c < nrows * 8; c += 128) {
-        const int r = c >> 3, part = c & 7;
-        cp_async16(&vt[blk & 1][r][part * 4], Vb + (int64_t)(lo + r) * Dm + d0 + part * 4);
+    };
+    // copies of block `blk`'s rows into vt[blk & 1]; one committed group either way
+    auto copy_rows = [&](int blk) {
+      if (blk < nblk && vec_rows) {
+        const int nrows = s_direct[blk & 1];
+        const int lo = s_rlo[blk & 1];
+        for (int c = itid; c < nrows * 8; c += 128) {
+          const int r = c >> 3, part = c & 7;
+          cp_async16(&vt[blk & 1][r][part * 4], Vb + (int64_t)(lo + r) * Dm + d0 + part * 4);
+        }
       }
-    }
-    cp_async_commit();
-  };
-
-  issue_table(0);
-  issue_table(1);
-  cp_async_wait<1>();          // table of block 0 landed
-  __syncthreads();
-  issue_rows(0);
-  __syncthreads();
-  copy_rows(0);
-  for (int blk = 0; blk < nblk; ++blk) {
-    const int q0 = blk * QB, nq = min(QB, Lq - q0);
-    // groups in flight: table(blk+1), rows(blk) -> wait for both
-    cp_async_wait<0>();
-    __syncthreads();
-    // next block's range (its table is resident now), then the next table + rows go out
-    issue_rows(blk + 1);
-    IT_TRACE(blk, 0);
-    // (A) interpolated inputs of this block
-    {
-      const Nbr* e = nb[blk % 3];
-      const int nrows = vec_rows ? s_direct[blk & 1] : -1;
-      const int lo = vec_rows ? s_rlo[blk & 1] : 0;
-      for (int i = warp; i < nq; i += 4) {
-        const Nbr x = e[i];
-        float v = 0.f;
-        if (dvalid) {
-          if (nrows >= 0) {
-            const float* row = &vt[blk & 1][0][lane];
-            if (x.prev >= 0 && x.next >= 0) v = lerp_ref(x.w, row[(x.prev - lo) * 32], row[(x.next - lo) * 32]);
-            else if (x.prev >= 0) v = row[(x.prev - lo) * 32];
-            else if (x.next >= 0) v = row[(x.next - lo) * 32];
-            else if (x.cur >= 0) v = row[(x.cur - lo) * 32];
-          } else {
-            const Nbr xx = tb[q0 + i];   // this lane's own tile
-            if (xx.prev >= 0 && xx.next >= 0)
-              v = lerp_ref(xx.w, Vb[(int64_t)xx.prev * Dm + d], Vb[(int64_t)xx.next * Dm + d]);
-            else if (xx.prev >= 0) v = Vb[(int64_t)xx.prev * Dm + d];
-            else if (xx.next >= 0) v = Vb[(int64_t)xx.next * Dm + d];
-            else if (xx.cur >= 0) v = Vb[(int64_t)xx.cur * Dm + d];
+      cp_async_commit();
+    };
+    issue_table(0);
+    issue_table(1);
+    cp_async_wait<1>();   // table of block 0 landed
+    named_bar_sync(5, 128);
+    issue_rows(0);
+    named_bar_sync(5, 128);
+    copy_rows(0);
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int q0 = blk * QB, nq = min(QB, Lq - q0);
+      // groups in flight: table(blk+1), rows(blk) -> wait for both
+      cp_async_wait<0>();
+      named_bar_sync(5, 128);
+      // next block's row range (its table is resident now); its rows and the table
+      // after it go out at once (vt[(blk+1)&1] and nb[(blk+2)%3] were last read by
+      // block blk-1, before the barrier above)
+      issue_rows(blk + 1);
+      named_bar_sync(5, 128);
+      copy_rows(blk + 1);
+      issue_table(blk + 2);
+      if (itid == 0) IT_TRACE(blk, 1);
+      if (blk >= 2) named_bar_sync(3 + (blk & 1), SCAN_THREADS);   // the state group is done with vh[blk & 1]
+      float (*vh)[33] = vhb[blk & 1];
+      // (A) interpolated inputs of this block
+      {
+        const Nbr* e = nb[blk % 3];
+        const int nrows = vec_rows ? s_direct[blk & 1] : -1;
+        const int lo = vec_rows ? s_rlo[blk & 1] : 0;
+        if (nrows >= 0) {
+          // staged rows: four queries per step (i0, i0+4, i0+8, i0+12), table
+          // entries first, then the row values, so the loads overlap
+          const float* row = &vt[blk & 1][0][lane];
+          for (int i0 = iw; i0 < nq; i0 += 16) {
+            int xp[4], xn[4], xc[4];
+            float xw[4];
+  #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = i0 + 4 * u;
+              const int4 raw = i < nq ? *reinterpret_cast<const int4*>(&e[i]) : make_int4(-1, -1, -1, 0);
+              xp[u] = raw.x;
+              xn[u] = raw.y;
+              xc[u] = raw.z;
+              xw[u] = __int_as_float(raw.w);
+            }
+            float vp[4], vn[4];
+  #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              // the value used when there is no pair to interpolate: prev, else next, else cur
+              const int ip = xp[u] >= 0 ? xp[u] : (xn[u] >= 0 ? xn[u] : xc[u]);
+              const int in = xn[u] >= 0 ? xn[u] : ip;
+              vp[u] = (dvalid && ip >= 0) ? row[(ip - lo) * 32] : 0.f;
+              vn[u] = (dvalid && in >= 0) ? row[(in - lo) * 32] : 0.f;
+            }
+  #pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = i0 + 4 * u;
+              if (i < nq) vh[i][lane] = (xp[u] >= 0 && xn[u] >= 0) ? lerp_ref(xw[u], vp[u], vn[u]) : vp[u];
+            }
+          }
+        } else {
+          for (int i = iw; i < nq; i += 4) {
+            float v = 0.f;
+            if (dvalid) {
+              const Nbr xx = tb[q0 + i];   // this lane's own tile
+              if (xx.prev >= 0 && xx.next >= 0)
+                v = lerp_ref(xx.w, Vb[(int64_t)xx.prev * Dm + d], Vb[(int64_t)xx.next * Dm + d]);
+              else if (xx.prev >= 0) v = Vb[(int64_t)xx.prev * Dm + d];
+              else if (xx.next >= 0) v = Vb[(int64_t)xx.next * Dm + d];
+              else if (xx.cur >= 0) v = Vb[(int64_t)xx.cur * Dm + d];
+            }
+            vh[i][lane] = v;
           }
         }
-        vh[i][lane] = v;
       }
+      if (itid == 0) IT_TRACE(blk, 2);
+      named_bar_arrive(1 + (blk & 1), SCAN_THREADS);   // vh[blk & 1] ready
     }
-    __syncthreads();   // vh ready; vt[blk & 1] and nb[blk % 3] free after this point
-    issue_table(blk + 2);
-    copy_rows(blk + 1);
-    IT_TRACE(blk, 1);
-    IT_TRACE(blk, 2);
-    // (B) recurrence, packed two states per instruction, 8 queries per step
-    {
-      auto one = [&](float v, int i) {
-        const float2 v2 = make_float2(v, v);
-        float2 acc;
-#pragma unroll
-        for (int k = 0; k < NP2; ++k) {
-          g2[k] = ffma2(a2[k], g2[k], v2);
-          acc = k == 0 ? fmul2(c2[k], g2[k]) : ffma2(c2[k], g2[k], acc);
-        }
-        yp[warp][i][lane] = acc.x + acc.y;
-      };
-      int i0 = 0;
-      for (; i0 + 8 <= nq; i0 += 8) {
-        float vv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) vv[u] = vh[i0 + u][lane];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) one(vv[u], i0 + u);
-      }
-      for (; i0 < nq; ++i0) one(vh[i0][lane], i0);
-    }
-    IT_TRACE(blk, 3);
-    __syncthreads();
-    IT_TRACE(blk, 4);
-    // (C) readout
-    if (dvalid) {
-      float* yrow = y + ((int64_t)b * Lq + q0) * Dm + d;
-      float* vrow = vhat_out ? vhat_out + ((int64_t)b * Lq + q0) * Dm + d : nullptr;
-      for (int i = warp; i < nq; i += 4) {
-        const float v = vh[i][lane];
-        yrow[(int64_t)i * Dm] = (yp[0][i][lane] + yp[1][i][lane]) + (yp[2][i][lane] + yp[3][i][lane]) + dsk * v;
-        if (vrow) vrow[(int64_t)i * Dm] = v;
-      }
-    }
-  }
-  cp_async_wait<0>();
-  if (h_last && dvalid) {
+    cp_async_wait<0>();
+  } else {
+    // ================================================================ state group
+    const float dtb = dt[b];
+    static_assert(NPT % 2 == 0, "states per thread come in pairs");
+    constexpr int NP2 = NPT / 2;
+    float2 a2[NP2], c2[NP2], g2[NP2], b2[NP2];
 #pragma unroll
     for (int k = 0; k < NPT; ++k) {
       const int n = warp * NPT + k;
-      const float gk = (k & 1) ? g2[k / 2].y : g2[k / 2].x;
-      const float bk = (k & 1) ? b2[k / 2].y : b2[k / 2].x;
-      if (n < N) h_last[((int64_t)b * Dm + d) * N + n] = bk * gk;
+      float ab = 0.f, bb = 0.f, cb = 0.f;
+      if (dvalid && n < N) {
+        const float a = -expf(A_log[(int64_t)d * N + n]);
+        const float x = dtb * a;
+        const float e = expf(x);
+        ab = e;
+        bb = zoh_coeff(x, e, a) * Bp[(int64_t)d * N + n];
+        cb = Cp[(int64_t)d * N + n] * bb;
+      }
+      if (k & 1) { a2[k / 2].y = ab; b2[k / 2].y = bb; c2[k / 2].y = cb; }
+      else { a2[k / 2].x = ab; b2[k / 2].x = bb; c2[k / 2].x = cb; }
+    }
+#pragma unroll
+    for (int k = 0; k < NP2; ++k) g2[k] = make_float2(0.f, 0.f);
+    const float dsk = (Dskip && dvalid) ? Dskip[d] : 0.f;
+    for (int blk = 0; blk < nblk; ++blk) {
+      const int q0 = blk * QB, nq = min(QB, Lq - q0);
+      named_bar_sync(1 + (blk & 1), SCAN_THREADS);   // vh[blk & 1] written
+      if (tid == 0) IT_TRACE(blk, 0);
+      float (*vh)[33] = vhb[blk & 1];
+      // (B) recurrence, packed two states per instruction, 8 queries per step
+      {
+        auto one = [&](float v, int i) {
+          const float2 v2 = make_float2(v, v);
+          float2 acc;
+#pragma unroll
+          for (int k = 0; k < NP2; ++k) {
+            g2[k] = ffma2(a2[k], g2[k], v2);
+            acc = k == 0 ? fmul2(c2[k], g2[k]) : ffma2(c2[k], g2[k], acc);
+          }
+          yp[warp][i][lane] = acc.x + acc.y;
+        };
+        int i0 = 0;
+        for (; i0 + 8 <= nq; i0 += 8) {
+          float vv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) vv[u] = vh[i0 + u][lane];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) one(vv[u], i0 + u);
+        }
+        for (; i0 < nq; ++i0) one(vh[i0][lane], i0);
+      }
+      if (tid == 0) IT_TRACE(blk, 3);
+      named_bar_sync(6, SCAN_SW * 32);   // all partials of the block written
+      // (C) readout
+      if (dvalid) {
+        float* yrow = y + ((int64_t)b * Lq + q0) * Dm + d;
+        float* vrow = vhat_out ? vhat_out + ((int64_t)b * Lq + q0) * Dm + d : nullptr;
+        for (int i0 = warp; i0 < nq; i0 += 4 * SCAN_SW) {   // four queries per step, loads first
+          float v[4], o[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = min(i0 + SCAN_SW * u, nq - 1);   // rows past nq are computed but not stored
+            v[u] = vh[i][lane];
+            o[u] = (yp[0][i][lane] + yp[1][i][lane]) + (yp[2][i][lane] + yp[3][i][lane]) + dsk * v[u];
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = i0 + SCAN_SW * u;
+            if (i < nq) {
+              yrow[(int64_t)i * Dm] = o[u];
+              if (vrow) vrow[(int64_t)i * Dm] = v[u];
+            }
+          }
+        }
+      }
+      named_bar_sync(6, SCAN_SW * 32);   // partials and vh[blk & 1] read by every state warp
+      if (tid == 0) IT_TRACE(blk, 4);
+      if (blk + 2 < nblk) named_bar_arrive(3 + (blk & 1), SCAN_THREADS);   // the interpolation group may refill it
+    }
+    if (h_last && dvalid) {
+#pragma unroll
+      for (int k = 0; k < NPT; ++k) {
+        const int n = warp * NPT + k;
+        const float gk = (k & 1) ? g2[k / 2].y : g2[k / 2].x;
+        const float bk = (k & 1) ? b2[k / 2].y : b2[k / 2].x;
+        if (n < N) h_last[((int64_t)b * Dm + d) * N + n] = bk * gk;
+      }
     }
   }
 }
 
-constexpr size_t kScanSmem = 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr) + QB * 33 * 4 + 4 * QB * 33 * 4;
+constexpr size_t kScanSmem = 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr) + 2 * QB * 33 * 4 + SCAN_SW * QB * 33 * 4;
 
 size_t ws_flags_bytes(int64_t Bsz, int64_t T, int64_t ntiles) { return (size_t)((Bsz * ntiles * T + 255) / 256 * 256); }
 size_t ws_table_bytes(int64_t Bsz, int64_t Lq, int64_t ntiles) { return (size_t)(Bsz * ntiles * Lq * sizeof(Nbr)); }
@@ -668,7 +735,7 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
         flags, (const float*)tau, (const float*)q, tab, (int)T, (int)Lq, (int)K, ntiles);
   }
   dim3 grid((unsigned)cdiv(Dm, 32), (unsigned)Bsz);
-  const int npt = (int)cdiv(N, 4);
+  const int npt = (int)cdiv(N, SCAN_SW);
   const float* Vf = (const float*)V;
   const float* al = (const float*)A_log;
   const float* bp = (const float*)B;
@@ -680,14 +747,14 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
     if (cudaFuncSetAttribute(interp_ssm_scan_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
                              (int)kScanSmem) != cudaSuccess)                                               \
       return check_launch("interp_ssm: scan smem");                                                        \
-    interp_ssm_scan_kernel<NP><<<grid, 128, kScanSmem, st>>>(Vf, tab, al, bp, cp, dk, dtp, (float*)y,      \
+    interp_ssm_scan_kernel<NP><<<grid, SCAN_THREADS, kScanSmem, st>>>(Vf, tab, al, bp, cp, dk, dtp, (float*)y,      \
                                                              (float*)h_last, (float*)vhat, (int)T, (int)Dm, \
                                                              (int)N, (int)Lq, (int)FTILE, ntiles);          \
   } while (0)
   if (npt <= 2) SCAN_LAUNCH(2);
   else if (npt <= 4) SCAN_LAUNCH(4);
   else if (npt <= 8) SCAN_LAUNCH(8);
-  else SCAN_LAUNCH(16);
+  else SCAN_LAUNCH(16);   // N <= 64
 #undef SCAN_LAUNCH
   return check_launch("interp_ssm");
 }

@@ -112,6 +112,10 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Arrive on a named barrier without waiting (producer side of a hand-over).
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 // Named barrier that also ORs a predicate over its participants: every thread
 // gets the same answer, so a decision taken after it is uniform.
 __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t nthreads, bool pred) {
