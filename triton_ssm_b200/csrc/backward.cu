@@ -10,7 +10,9 @@
 // every step is one coalesced 128-byte row segment per warp); warp w holds
 // steps [w*S, (w+1)*S) of a super-segment of NW*S steps, folds them into a
 // reverse (a, x) aggregate, takes the carry from the warps after it, and
-// replays its steps writing du, dA, dB, dC.  Every input is read from HBM once.
+// replays its steps writing du, dA, dB, dC.  Every input is read from HBM once
+// (A_{t+1} and h_{t-1} at a run's edge come from the neighbouring run's rows,
+// which the cache holds).
 //
 // zoh_discretize_bwd (replaces discretize_kernel.py:97-162): per (b, t, h)
 //     a = -exp(A_log), x = dt a, e = exp(x), em1 = guarded exp(x)-1 (bf16 form, :134)
@@ -55,8 +57,9 @@ __global__ void __launch_bounds__(NW * 32, 1) ssm_backward_kernel(
   float carry = 0.f;   // dH at the first step after the current super-segment (0 past the end)
   for (int t0 = ((Li - 1) / SEG) * SEG; t0 >= 0; t0 -= SEG) {
     const int ts = t0 + warp * S;
-    // coefficient A_{t+1} and input C_t dY_t of the reverse recurrence dH_t = A_{t+1} dH_{t+1} + C_t dY_t
-    float a[S], x[S], dy[S];
+    // coefficient A_{t+1} and input C_t dY_t of the reverse recurrence dH_t = A_{t+1} dH_{t+1} + C_t dY_t;
+    // the replay's B, u, h are loaded here too, so all of a run's loads are in flight together
+    float a[S], x[S], dy[S], bb[S], uu[S], hh[S];
 #pragma unroll
     for (int i = 0; i < S; ++i) {
       const int t = ts + i;
@@ -65,12 +68,18 @@ __global__ void __launch_bounds__(NW * 32, 1) ssm_backward_kernel(
         a[i] = t + 1 < Li ? ldf(Ab + off + Hi) : 0.f;
         dy[i] = ldf(dYb + off);
         x[i] = ldf(Cb + off) * dy[i];
+        bb[i] = ldf(Bb + off);
+        uu[i] = ldf(ub + off);
+        hh[i] = ldf(hb + off);
       } else {
         a[i] = 1.f;
         x[i] = 0.f;
         dy[i] = 0.f;
+        bb[i] = uu[i] = hh[i] = 0.f;
       }
     }
+    // h_{ts-1}, the state before this run (for dA of its first step)
+    const float hbefore = (valid && ts >= 1 && ts - 1 < Li) ? ldf(hb + (ts - 1) * Hi) : 0.f;
     float ag_a = 1.f, ag_x = 0.f;   // dH_ts = ag_a * dH_{ts+S} + ag_x
 #pragma unroll
     for (int i = S - 1; i >= 0; --i) {
@@ -82,21 +91,19 @@ __global__ void __launch_bounds__(NW * 32, 1) ssm_backward_kernel(
     __syncthreads();
     float dh = carry;
     for (int w = NW - 1; w > warp; --w) dh = s_a[w][lane] * dh + s_x[w][lane];
-    // replay from the end of this warp's steps; h_{t-1} of one step is h_t of the next
-    float hcur = (valid && ts + S - 1 < Li) ? ldf(hb + (ts + S - 1) * Hi) : 0.f;
+    // replay from the end of this warp's steps
 #pragma unroll
     for (int i = S - 1; i >= 0; --i) {
       const int t = ts + i;
       dh = a[i] * dh + x[i];
-      const float hprev = (valid && t >= 1 && t - 1 < Li) ? ldf(hb + (t - 1) * Hi) : 0.f;
+      const float hprev = i > 0 ? hh[i - 1] : hbefore;
       if (valid && t < Li) {
         const int off = t * Hi;
-        stf(dub + off, ldf(Bb + off) * dh);
-        stf(dBb + off, ldf(ub + off) * dh);
-        stf(dCb + off, dy[i] * hcur);
+        stf(dub + off, bb[i] * dh);
+        stf(dBb + off, uu[i] * dh);
+        stf(dCb + off, dy[i] * hh[i]);
         stf(dAb + off, hprev * dh);
       }
-      hcur = hprev;
     }
     if (warp == 0) s_carry[lane] = dh;   // dH at step t0
     __syncthreads();
@@ -133,52 +140,77 @@ __global__ void __launch_bounds__(DBWD_THREADS) zoh_discretize_bwd_kernel(
       a[k] = -na[k];
       acc[k] = 0.f;
     }
-    for (int r = 0; r < nrows; ++r) {
-      const int64_t row = r0 + r;
-      const float dtv = dt[row];
-      float part = 0.f;
-      if (act) {
-        const int64_t off = row * H + h0;
-        float vb[PER], vab[PER], vda[PER], vdb[PER], out[PER];
-        if (VEC) {
-          const float4 q0 = *reinterpret_cast<const float4*>(B + off);
-          const float4 q1 = *reinterpret_cast<const float4*>(Abar + off);
-          const float4 q2 = *reinterpret_cast<const float4*>(dAbar + off);
-          const float4 q3 = *reinterpret_cast<const float4*>(dBbar + off);
-          const float t0[4] = {q0.x, q0.y, q0.z, q0.w}, t1[4] = {q1.x, q1.y, q1.z, q1.w};
-          const float t2[4] = {q2.x, q2.y, q2.z, q2.w}, t3[4] = {q3.x, q3.y, q3.z, q3.w};
+    // four rows per step: their loads go out together, then four independent reductions
+    for (int r4 = 0; r4 < nrows; r4 += 4) {
+      float vb[4][PER], vab[4][PER], vda[4][PER], vdb[4][PER], dtv[4];
 #pragma unroll
-          for (int k = 0; k < PER; ++k) {
-            vb[k] = t0[k];
-            vab[k] = t1[k];
-            vda[k] = t2[k];
-            vdb[k] = t3[k];
+      for (int j = 0; j < 4; ++j) {
+        const int r = r4 + j < nrows ? r4 + j : nrows - 1;   // duplicate rows are computed, not used
+        const int64_t row = r0 + r;
+        dtv[j] = dt[row];
+        if (act) {
+          const int64_t off = row * H + h0;
+          if (VEC) {
+            const float4 q0 = *reinterpret_cast<const float4*>(B + off);
+            const float4 q1 = *reinterpret_cast<const float4*>(Abar + off);
+            const float4 q2 = *reinterpret_cast<const float4*>(dAbar + off);
+            const float4 q3 = *reinterpret_cast<const float4*>(dBbar + off);
+            const float t0[4] = {q0.x, q0.y, q0.z, q0.w}, t1[4] = {q1.x, q1.y, q1.z, q1.w};
+            const float t2[4] = {q2.x, q2.y, q2.z, q2.w}, t3[4] = {q3.x, q3.y, q3.z, q3.w};
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+              vb[j][k] = t0[k];
+              vab[j][k] = t1[k];
+              vda[j][k] = t2[k];
+              vdb[j][k] = t3[k];
+            }
+          } else {
+            vb[j][0] = B[off];
+            vab[j][0] = Abar[off];
+            vda[j][0] = dAbar[off];
+            vdb[j][0] = dBbar[off];
           }
         } else {
-          vb[0] = B[off];
-          vab[0] = Abar[off];
-          vda[0] = dAbar[off];
-          vdb[0] = dBbar[off];
+#pragma unroll
+          for (int k = 0; k < PER; ++k) vb[j][k] = vab[j][k] = vda[j][k] = vdb[j][k] = 0.f;
         }
+      }
+      float part[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        part[j] = 0.f;
+        const bool use = act && r4 + j < nrows;
+        float out[PER];
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
-          const float x = dtv * a[k];
+          const float x = dtv[j] * a[k];
           const float e = expf(x);
           const float em1 = expm1_guard_bf16(x, e);
-          part += vda[k] * a[k] * vab[k] + vdb[k] * e * vb[k];
-          const float num = (e * dtv * a[k] - em1) / (a[k] * a[k] + 1e-18f);
-          const float da = vda[k] * dtv * vab[k] + vdb[k] * num * vb[k];
-          acc[k] += da * (-na[k]);
-          out[k] = vdb[k] * em1 / (a[k] + 1e-12f);
+          part[j] += vda[j][k] * a[k] * vab[j][k] + vdb[j][k] * e * vb[j][k];
+          const float num = (e * dtv[j] * a[k] - em1) / (a[k] * a[k] + 1e-18f);
+          const float da = vda[j][k] * dtv[j] * vab[j][k] + vdb[j][k] * num * vb[j][k];
+          if (use) acc[k] += da * (-na[k]);
+          out[k] = vdb[j][k] * em1 / (a[k] + 1e-12f);
         }
-        if (VEC)
-          *reinterpret_cast<float4*>(dB + off) = make_float4(out[0], out[1], out[2], out[3]);
-        else
-          dB[off] = out[0];
+        if (!use) part[j] = 0.f;
+        if (use) {
+          const int64_t off = (r0 + r4 + j) * H + h0;
+          if (VEC)
+            *reinterpret_cast<float4*>(dB + off) = make_float4(out[0], out[1], out[2], out[3]);
+          else
+            dB[off] = out[0];
+        }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-      if (lane == 0) s_ddt[r][warp] += part;
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) part[j] += __shfl_xor_sync(0xffffffffu, part[j], o);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (r4 + j < nrows) s_ddt[r4 + j][warp] += part[j];
+      }
     }
     if (act) {
 #pragma unroll
@@ -207,7 +239,8 @@ extern "C" int tssm_ssm_backward(const void* u, const void* A, const void* B, co
   TSSM_REQUIRE(Bsz <= 65535, "ssm_backward: batch %lld exceeds 65535", (long long)Bsz);
   TSSM_REQUIRE(L * H < (int64_t(1) << 31), "ssm_backward: L*H must be < 2^31 per batch row");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  constexpr int S = 16, NW = 16;
+  // runs of 4 steps, 32 warps: the six inputs of a run are loaded before its replay
+  constexpr int S = 4, NW = 32;
   dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
   if (dtype == TSSM_F32) {
     ssm_backward_kernel<float, S, NW><<<grid, NW * 32, 0, st>>>(
