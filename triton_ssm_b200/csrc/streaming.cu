@@ -54,44 +54,53 @@ __global__ void __launch_bounds__(256) streaming_step_kernel(
   constexpr int N = 4 * TPR;
   const int q = threadIdx.x % TPR;             // which 4-wide n group
   const int64_t row0 = (int64_t)blockIdx.x * (RPB * RPT) + threadIdx.x / TPR;
+  // the state quads of all RPT rows go out first (evict-first: touched once)
   float4 hv[RPT];
-  float bq[RPT][4], cq[RPT][4], xv[RPT], e[RPT], coef[RPT], dsk[RPT];
   bool ok[RPT];
 #pragma unroll
   for (int r = 0; r < RPT; ++r) {
     const int64_t row = row0 + (int64_t)r * RPB;
     ok[r] = row < rows;
-    const int64_t rr = ok[r] ? row : 0;
-    const int64_t sh = rr / P;                 // (s, h) pair
-    const int p = (int)(rr - sh * P);
-    const int64_t s = sh / Hh;
-    const int hh = (int)(sh - s * Hh);
-    hv[r] = ok[r] ? ld_stream_f4(reinterpret_cast<const float4*>(h + rr * N) + q)
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
-    quad<IO>::load(B + sh * N + 4 * q, bq[r]);
-    quad<IO>::load(C + sh * N + 4 * q, cq[r]);
-    xv[r] = ldf(x + rr);
-    const float a = -expf(__ldg(A_log + hh));
-    const float xx = __ldg(dt + s) * a;
-    e[r] = expf(xx);
-    coef[r] = zoh_coeff(xx, e[r], a);
-    dsk[r] = __ldg(Dskip + (int64_t)hh * P + p);
+    hv[r] = ok[r] ? ld_stream_f4(reinterpret_cast<const float4*>(h + row * N) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  // per-row scalars (indices, decay, input coefficient, x, skip) computed once per
+  // row by the group's first lane and broadcast to its TPR lanes
 #pragma unroll
   for (int r = 0; r < RPT; ++r) {
+    const int64_t row = ok[r] ? row0 + (int64_t)r * RPB : 0;
+    int sh = 0;
+    float e = 0.f, coef = 0.f, xv = 0.f, dsk = 0.f;
+    if (q == 0) {
+      sh = (int)(row / P);                     // (s, h) pair; S*H < 2^31 (host-checked)
+      const int p = (int)(row - (int64_t)sh * P);
+      const int s = sh / Hh;
+      const int hh = sh - s * Hh;
+      const float a = -expf(__ldg(A_log + hh));
+      const float xx = __ldg(dt + s) * a;
+      e = expf(xx);
+      coef = zoh_coeff(xx, e, a);
+      xv = ldf(x + row);
+      dsk = __ldg(Dskip + (int64_t)hh * P + p);
+    }
+    sh = __shfl_sync(0xffffffffu, sh, 0, TPR);
+    e = __shfl_sync(0xffffffffu, e, 0, TPR);
+    coef = __shfl_sync(0xffffffffu, coef, 0, TPR);
+    xv = __shfl_sync(0xffffffffu, xv, 0, TPR);
+    float bq[4], cq[4];
+    quad<IO>::load(B + (int64_t)sh * N + 4 * q, bq);
+    quad<IO>::load(C + (int64_t)sh * N + 4 * q, cq);
     float hs[4] = {hv[r].x, hv[r].y, hv[r].z, hv[r].w};
     float part = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      hs[k] = e[r] * hs[k] + (coef[r] * bq[r][k]) * xv[r];
-      part += cq[r][k] * hs[k];
+      hs[k] = e * hs[k] + (coef * bq[k]) * xv;
+      part += cq[k] * hs[k];
     }
 #pragma unroll
     for (int off = TPR >> 1; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off, TPR);
     if (ok[r]) {
-      const int64_t row = row0 + (int64_t)r * RPB;
       st_stream_f4(reinterpret_cast<float4*>(h + row * N) + q, make_float4(hs[0], hs[1], hs[2], hs[3]));
-      if (q == 0) stf(y + row, part + dsk[r] * xv[r]);
+      if (q == 0) stf(y + row, part + dsk * xv);
     }
   }
 }
@@ -127,7 +136,7 @@ template <typename IO, int TPR>
 int launch_step(const void* x, const void* dt, void* h, const void* A_log, const void* B,
                 const void* C, const void* Dskip, void* y, int64_t rows, int Hh, int P,
                 cudaStream_t st) {
-  constexpr int RPT = 2;
+  constexpr int RPT = 4;
   constexpr int RPB = 256 / TPR;
   const int64_t blocks = cdiv(rows, RPB * RPT);
   streaming_step_kernel<IO, TPR, RPT><<<(unsigned)blocks, 256, 0, st>>>(
@@ -196,7 +205,7 @@ extern "C" int tssm_streaming_step(const void* x, const void* dt, void* h, const
   // The vector path needs 16-byte state rows and 4-element aligned B, C rows.
   const bool vec_ok = aligned16(h) && (reinterpret_cast<uintptr_t>(B) % (4 * isz)) == 0 &&
                       (reinterpret_cast<uintptr_t>(C) % (4 * isz)) == 0;
-  TSSM_REQUIRE(Hh < (1 << 30) && P < (1 << 30), "streaming_step: H or P too large");
+  TSSM_REQUIRE(Hh < (1 << 30) && P < (1 << 30) && S * Hh < (int64_t(1) << 31), "streaming_step: S, H or P too large");
   const int64_t rows = S * Hh * P;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (io_dtype == TSSM_BF16)
