@@ -234,9 +234,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
           const uint32_t X = smem_u32(stage_ptr(s));
           const uint64_t dB = make_desc_sw128(X + TILE, 16), dC = make_desc_sw128(X + TILE * (1 + NB), 16);
 #pragma unroll
-          for (int kk = 0; kk < NST / 16; ++kk) {
-            const uint64_t ko = ((kk >> 2) * TILE + (kk & 3) * 32) >> 4;   // descriptor units of 16 bytes
-            umma_bf16(tmem + col_g(kb), dC + ko, dB + ko, ID_KK, kk > 0);
+          for (int kb4 = 0; kb4 < NST / 64; ++kb4) {   // 64-wide K blocks (tiles) of n
+            const uint64_t ko = (uint64_t)(kb4 * TILE) >> 4;
+            umma_bf16_x4(tmem + col_g(kb), dC + ko, dC + ko + 2, dC + ko + 4, dC + ko + 6, dB + ko, dB + ko + 2,
+                         dB + ko + 4, dB + ko + 6, ID_KK, kb4 > 0);
           }
           umma_commit(&gfull[kb]);
           SSD_TRACE(mc, 3);
@@ -359,8 +360,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         SSD_TRACE(k, 10);
         const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
         const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_y1(kb), dM + 2 * kk, dX + 128 * kk, ID_KM, kk > 0);
+        umma_bf16_x4(tmem + col_y1(kb), dM, dM + 2, dM + 4, dM + 6, dX, dX + 128, dX + 256, dX + 384, ID_KM, 0);
         umma_commit(&y1full[kb]);
         SSD_TRACE(k, 11);
         SSD_TRACE_DONE(&y1full[kb], (k >> 1) & 1, k, 22);
@@ -385,8 +385,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         {
           const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
           const uint64_t dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma_bf16(tmem + col_s(kb), dBh + 128 * kk, dX + 128 * kk, ID_MM, kk > 0);
+          umma_bf16_x4(tmem + col_s(kb), dBh, dBh + 128, dBh + 256, dBh + 384, dX, dX + 128, dX + 256, dX + 384, ID_MM,
+                       0);
         }
         umma_commit(&sfull[kb]);
         SSD_TRACE(k, 9);
@@ -402,9 +402,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         const uint64_t dC = make_desc_sw128(smem_u32(stage_ptr(s)) + TILE * (1 + NB), 16);
         const uint64_t dH = make_desc_sw128(smem_u32(hs_ptr(kb)), TILE);
 #pragma unroll
-        for (int kk = 0; kk < NST / 16; ++kk) {
-          const uint64_t ko = ((kk >> 2) * TILE + (kk & 3) * 32) >> 4;
-          umma_bf16(tmem + col_y2(kb), dC + ko, dH + 128 * kk, ID_KM, kk > 0);
+        for (int kb4 = 0; kb4 < NST / 64; ++kb4) {   // 64-wide K blocks of n: C tiles; 16 state rows per step
+          const uint64_t ko = (uint64_t)(kb4 * TILE) >> 4;
+          const uint64_t ho = 512 * kb4;
+          umma_bf16_x4(tmem + col_y2(kb), dC + ko, dC + ko + 2, dC + ko + 4, dC + ko + 6, dH + ho, dH + ho + 128,
+                       dH + ho + 256, dH + ho + 384, ID_KM, kb4 > 0);
         }
         umma_commit(&y2full[kb]);
         SSD_TRACE(k, 13);

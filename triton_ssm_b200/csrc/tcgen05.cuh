@@ -245,6 +245,22 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint6
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Four MMAs into one accumulator (K steps 0..3) from one asm block: the first
+// one overwrites the accumulator unless `accumulate`, the others add.
+__device__ __forceinline__ void umma_bf16_x4(uint32_t d_tmem, uint64_t a0, uint64_t a1, uint64_t a2, uint64_t a3,
+                                             uint64_t b0, uint64_t b1, uint64_t b2, uint64_t b3, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %10, 0;\n\t"
+      "setp.eq.b32 q, %9, %9;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, q;\n\t}" ::"r"(d_tmem),
+      "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Whole-warp forms: every lane of a converged warp executes them and elect.sync
 // picks one lane (the same one each time) to issue, so descriptors computed by
 // the warp stay warp-uniform and the issue path is shorter than from a lane-0 branch.
