@@ -80,7 +80,12 @@ def make_c3(Bt, T, Dm, N, Lq, seed, p_obs=0.7):
 
 @pytest.mark.parametrize("Bt,T,Dm,N,Lq,p_obs", [(2, 300, 256, 16, 600, 0.7), (3, 100, 70, 5, 257, 0.02),
                                                  (1, 64, 33, 64, 64, 0.3), (4, 300, 64, 16, 500, 0.7),
-                                                 (2, 90, 192, 16, 120, 0.02)])
+                                                 (2, 90, 192, 16, 120, 0.02),
+                                                 # sparse queries: every 32-query block spans more rows than
+                                                 # are staged, so values are gathered from global memory
+                                                 (2, 2000, 64, 16, 100, 0.7),
+                                                 (2, 300, 96, 5, 700, 0.3), (1, 200, 64, 3, 333, 0.7),
+                                                 (3, 150, 32, 16, 33, 0.7), (1, 40, 32, 16, 5, 0.7)])
 def test_interp_ssm_query_grid_vs_oracle(cuda_ops, Bt, T, Dm, N, Lq, p_obs):
     V, M, tau, A_log, B, C, D = make_c3(Bt, T, Dm, N, Lq, seed=T + N, p_obs=p_obs)
     # the same query times on both sides (a device-built grid may differ in the last ulp)
@@ -92,6 +97,22 @@ def test_interp_ssm_query_grid_vs_oracle(cuda_ops, Bt, T, Dm, N, Lq, p_obs):
     y, h, vh = cuda_ops.fused_interp_ssm(cu(V), cu(M), cu(tau), cu(A_log), cu(B), cu(C), q=cu(q), dt=cu(dt),
                                          D=cu(D), return_state=True, return_vhat=True, workspace=ws)
     ry, rh, rvh = oracle.interp_ssm(V, M, tau, A_log, B, C, dt, q=q, D=D, return_vhat=True)
+    assert torch.equal(vh.cpu(), rvh)
+    assert rel_err(y, ry) < TOL_FP32
+    assert rel_err(h, rh) < TOL_FP32
+
+
+@pytest.mark.parametrize("FTILE,p_obs", [(32, 0.05), (64, 0.02), (96, 0.7), (48, 0.3)])
+def test_interp_ssm_feature_tiles(cuda_ops, FTILE, p_obs):
+    """Neighbour tables per tile of FTILE features: each run of 32 features reads
+    its own tile's table (FTILE 96 puts runs of one CTA in different tiles)."""
+    Bt, T, Dm, N, Lq = 2, 400, 192, 16, 900
+    V, M, tau, A_log, B, C, D = make_c3(Bt, T, Dm, N, Lq, seed=FTILE, p_obs=p_obs)
+    q = oracle.linspace_queries(tau, Lq)
+    dt = (tau[:, -1] - tau[:, 0]) / (Lq - 1)
+    y, h, vh = cuda_ops.fused_interp_ssm(cu(V), cu(M), cu(tau), cu(A_log), cu(B), cu(C), q=cu(q), dt=cu(dt),
+                                         D=cu(D), FTILE=FTILE, return_state=True, return_vhat=True)
+    ry, rh, rvh = oracle.interp_ssm(V, M, tau, A_log, B, C, dt, q=q, D=D, FTILE=FTILE, return_vhat=True)
     assert torch.equal(vh.cpu(), rvh)
     assert rel_err(y, ry) < TOL_FP32
     assert rel_err(h, rh) < TOL_FP32

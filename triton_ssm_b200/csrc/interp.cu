@@ -17,6 +17,8 @@
 
 #include "common.cuh"
 #include "tcgen05.cuh"
+#include "tmap.cuh"
+#include <type_traits>
 
 namespace tssm {
 #ifdef TSSM_INTERP_TRACE
@@ -221,10 +223,46 @@ struct Nbr {
   float w;
 };
 
+// Blocked form of the neighbour table read by the chunked scan kernel: per
+// block of WQB consecutive queries, WQB entries (a, b, w, 1-w) and a header
+// (lo, span).  The block's operands are rows lo .. lo+span-1 of the
+// observations; an entry's a and b are offsets (row - lo) * 32 into those rows
+// staged as [span][32 features], with the reference's priority resolved here
+// (pair -> lerp; else prev, next, cur -> a, b = the zero row after WRB staged
+// rows, w = 0), so the scan evaluates round((1-w)*row[a]) + round(w*row[b])
+// for every query.  span = -1: the rows span more than WRB; a and b then hold
+// absolute rows (-1: zero) and the scan gathers from global memory.
+constexpr int WQB = 32;   // queries per block
+constexpr int WRB = 40;   // rows the scan stages per block (a zero row follows them)
+
+// Warp-collective: lane i holds query i of a block (p, n, c = prev/next/cur or -1).
+__device__ __forceinline__ int4 blocked_entry(int p, int n, int c, float w, int& lo_out, int& span_out) {
+  constexpr unsigned FULL = 0xffffffffu;
+  int mn = 0x7fffffff, mx = -1;
+  if (p >= 0) { mn = min(mn, p); mx = max(mx, p); }
+  if (n >= 0) { mn = min(mn, n); mx = max(mx, n); }
+  if (c >= 0) { mn = min(mn, c); mx = max(mx, c); }
+  const int hi = __reduce_max_sync(FULL, mx);
+  const int lo = hi >= 0 ? __reduce_min_sync(FULL, mn) : 0;
+  const int span = hi >= 0 ? hi - lo + 1 : 0;
+  const bool direct = span > WRB;
+  int sp, sn;
+  float ww, om;
+  if (p >= 0 && n >= 0) { sp = p; sn = n; ww = w; om = 1.0f - w; }
+  else { sp = p >= 0 ? p : (n >= 0 ? n : c); sn = -1; ww = 0.f; om = 1.f; }
+  int op, on;
+  if (direct) { op = sp; on = sn; }
+  else { op = sp >= 0 ? (sp - lo) * 32 : WRB * 32; on = sn >= 0 ? (sn - lo) * 32 : WRB * 32; }
+  lo_out = lo;
+  span_out = direct ? -1 : span;
+  return make_int4(op, on, __float_as_int(ww), __float_as_int(om));
+}
+
 // Kernel 2: per (tile, b, query slice): last/next flagged index scans in shared
 // memory, then one entry per query.  Each thread walks a contiguous run of
 // sorted queries with two monotone pointers (lo = #{tau < q}, hi = #{tau <= q}).
 constexpr int NB_THREADS = 256;
+template <bool BLOCKED>
 __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint8_t* __restrict__ flags,
                                                                       const float* __restrict__ tau,
                                                                       const float* __restrict__ q,
@@ -276,8 +314,60 @@ __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint
   for (int i = s1 - 1; i >= s0; --i) { runn = min(runn, nextf[i]); nextf[i] = runn; }
   __syncthreads();
 
-  Nbr* out = tab + ((int64_t)b * ntiles + tile) * Lq;
   const float* qb = q ? q + (int64_t)b * Lq : nullptr;
+  if (BLOCKED) {
+    // one warp per block of WQB queries, one query per lane (binary searches)
+    const int nblk = (Lq + WQB - 1) / WQB;
+    int4* outb = reinterpret_cast<int4*>(tab) + ((int64_t)b * ntiles + tile) * nblk * (WQB + 1);
+    const int per_cta = (nblk + gridDim.z - 1) / gridDim.z;
+    const int jb1 = min(nblk, (int)blockIdx.z * per_cta + per_cta);
+    for (int jb = blockIdx.z * per_cta + warp; jb < jb1; jb += NB_THREADS / 32) {
+      const int j = jb * WQB + lane;
+      int prev = -1, next = -1, cur = -1;
+      float w = 0.f;
+      if (j < Lq) {
+        float tq;
+        if (!qb) {
+          cur = j;
+          tq = stau[j];
+          if (j >= 1) {
+            const int p = lastf[j - 1];
+            if (p >= 0 && p >= j - K) prev = p;
+          }
+          if (j + 1 < T) {
+            const int n = nextf[j + 1];
+            if (n < T && n <= j + K) next = n;
+          }
+        } else {
+          tq = qb[j];
+          int l = 0, h = T;
+          while (l < h) { const int m = (l + h) >> 1; if (stau[m] < tq) l = m + 1; else h = m; }
+          const int lo = l;
+          h = T;
+          while (l < h) { const int m = (l + h) >> 1; if (stau[m] <= tq) l = m + 1; else h = m; }
+          const int hiq = l;
+          if (hiq > lo) cur = hiq - 1;
+          if (lo >= 1) {
+            const int p = lastf[lo - 1];
+            if (p >= 0 && p >= lo - K) prev = p;
+          }
+          if (hiq < T) {
+            const int n = nextf[hiq];
+            if (n < T && n <= hiq + K - 1) next = n;
+          }
+        }
+        const float tp = prev >= 0 ? stau[prev] : 0.f;
+        const float tn = next >= 0 ? stau[next] : 0.f;
+        w = weight_ref(tq, tp, tn);
+      }
+      int lo, span;
+      const int4 e = blocked_entry(prev, next, cur, w, lo, span);
+      outb[(int64_t)jb * (WQB + 1) + lane] = e;
+      if (lane == 0) outb[(int64_t)jb * (WQB + 1) + WQB] = make_int4(lo, span, 0, 0);
+    }
+    return;
+  }
+  Nbr* out = tab + ((int64_t)b * ntiles + tile) * Lq;
   const int per_cta = (Lq + gridDim.z - 1) / gridDim.z;
   const int qa = blockIdx.z * per_cta, qe = min(Lq, qa + per_cta);
   const int per_thr = (qe - qa + NB_THREADS - 1) / NB_THREADS;
@@ -606,8 +696,346 @@ __global__ void __launch_bounds__(SCAN_THREADS) interp_ssm_scan_kernel(
 
 constexpr size_t kScanSmem = 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr) + 2 * QB * 33 * 4 + SCAN_SW * QB * 33 * 4;
 
+// ---------------------------------------------------------------------------
+// Kernel 3b, for N <= 16 with runs of 32 features inside one tile (Dm % 32 ==
+// 0, FTILE % 32 == 0), reading the blocked table.  CTA = (b, 32 features),
+// four warps; each warp owns EVERY state of its 32 features (lane = feature,
+// N/2 packed pairs in registers: nothing is exchanged between warps) and walks
+// one quarter (a "chunk") of the query blocks.  The walk is FP32-pipe bound
+// (two FMAs per state and query), so the four chunks per row are what keeps
+// two warps on every scheduler.
+//
+// A chunk needs the state at its first query.  The recurrence forgets at rate
+// Abar: after W steps an earlier state contributes at most amax^W of itself,
+// amax = the largest Abar of the CTA's features and states.  A chunk therefore
+// starts its walk W queries early from a zero state (W: amax^W <= 2^-40,
+// rounded up to whole blocks) and writes outputs from its own first query
+// on; the dropped term is below 2^-40 of the state, far inside fp32 rounding.
+// When W exceeds a chunk (slow decay: small dt*|A|), the four chunks run one
+// after another instead, each starting from the previous chunk's final state.
+//
+// Per warp, blocks of WQB = 32 queries: the warp's lane 0 streams its blocked
+// table (entries + header; one bulk copy per block) CTS blocks ahead and each
+// block's observation rows (one TMA tile of WRB rows x 32 features from the
+// header's first row) CRA blocks ahead, both completing on mbarriers; the
+// warp runs block k's recurrence and readout interleaved with block k+1's
+// interpolation (values pass through a per-lane column of shared memory), and
+// block k's outputs leave as one TMA tile store of 32 queries x 32 features.
+constexpr int CH_WARPS = 4;   // chunks (warps) per CTA
+constexpr int CRA = 2;        // rows of block k+CRA are requested while block k runs
+constexpr int CTS = 4;        // table of block k+CTS likewise
+
+struct alignas(128) ChunkWarpSmem {
+  float rows[CRA][WRB + 1][32];   // staged observation rows; row WRB stays zero
+  float ystage[WQB][32];          // outputs of one block, stored by TMA
+  float2 vcol[WQB][32];           // interpolated values (v, v), one column per lane
+  int4 tab[CTS][WQB + 1];         // blocked table entries + header
+  uint64_t tbar[CTS];
+  uint64_t rbar[CRA];
+};
+struct alignas(128) ChunkSmem {
+  ChunkWarpSmem w[CH_WARPS];
+  float2 carry[8][32];            // final state of the previous chunk (sequential mode)
+};
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          sm100::smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(sm100::smem_u32(bar))
+      : "memory");
+}
+
+// Polling wait bounded by `timeout_ns` of wall time, kept out of line.
+static __device__ __noinline__ bool mbar_poll_slow(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  const uint64_t t0 = sm100::globaltimer_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (sm100::mbar_test(bar, parity)) return true;
+    if (sm100::globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, uint64_t timeout_ns = 2000000000ull) {
+  return sm100::mbar_test(bar, parity) || mbar_poll_slow(bar, parity, timeout_ns);
+}
+
+template <int NP2, bool VHAT>
+__global__ void __launch_bounds__(CH_WARPS * 32) interp_ssm_scan_chunk_kernel(
+    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmY,
+    const float* __restrict__ Vp, const int4* __restrict__ tabq, const float* __restrict__ A_log,
+    const float* __restrict__ Bp, const float* __restrict__ Cp, const float* __restrict__ Dskip,
+    const float* __restrict__ dt, float* __restrict__ h_last, float* __restrict__ vhat_out,
+    int* __restrict__ status, int T, int Dm, int N, int Lq, int FTILE, int ntiles) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  ChunkSmem& CS = *reinterpret_cast<ChunkSmem*>(dsm + ((128u - (sm100::smem_u32(dsm) & 127u)) & 127u));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  ChunkWarpSmem& S = CS.w[warp];
+  const int dpr = Dm / 32;
+  const int b = blockIdx.x / dpr, d0 = (blockIdx.x % dpr) * 32, d = d0 + lane;
+  const int nblk = (Lq + WQB - 1) / WQB;
+  const int4* tq = tabq + ((int64_t)b * ntiles + d0 / FTILE) * nblk * (WQB + 1);
+  const float* Vb = Vp + (int64_t)b * T * Dm;
+  constexpr unsigned FULL = 0xffffffffu;
+
+  if (lane == 0) {
+    for (int i = 0; i < CTS; ++i) sm100::mbar_init(&S.tbar[i], 1);
+    for (int i = 0; i < CRA; ++i) sm100::mbar_init(&S.rbar[i], 1);
+    sm100::fence_mbar_init();
+    sm100::prefetch_tmap(&tmV);
+    sm100::prefetch_tmap(&tmY);
+  }
+#pragma unroll
+  for (int i = 0; i < CRA; ++i) S.rows[i][WRB][lane] = 0.f;
+  __syncwarp();
+
+  // this lane's states: Abar and C*Bbar as packed pairs; amax over the CTA's
+  const float dtb = dt[b];
+  auto coeffs = [&](int n, float& ab, float& bb) {
+    const float a = -expf(A_log[(int64_t)d * N + n]);
+    const float x = dtb * a;
+    const float e = expf(x);
+    ab = e;
+    bb = zoh_coeff(x, e, a) * Bp[(int64_t)d * N + n];
+  };
+  float2 a2[NP2], c2[NP2], g2[NP2];
+  float amax = 0.f;
+  bool bad = false;   // NaN coefficients: no decay bound, run the chunks in order
+#pragma unroll
+  for (int k = 0; k < 2 * NP2; ++k) {
+    float ab = 0.f, bb = 0.f, cb = 0.f;
+    if (k < N) {
+      coeffs(k, ab, bb);
+      cb = Cp[(int64_t)d * N + k] * bb;
+      amax = fmaxf(amax, fabsf(ab));
+      bad |= ab != ab;
+    }
+    if (k & 1) { a2[k / 2].y = ab; c2[k / 2].y = cb; }
+    else { a2[k / 2].x = ab; c2[k / 2].x = cb; }
+  }
+#pragma unroll
+  for (int k = 0; k < NP2; ++k) g2[k] = make_float2(0.f, 0.f);
+  const float dsk = Dskip ? Dskip[d] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
+  if (__any_sync(FULL, bad)) amax = 1.0f;
+  // warm-up length in blocks; every warp of the CTA computes the same value
+  const int chb = (nblk + CH_WARPS - 1) / CH_WARPS;   // blocks per chunk
+  int wb = 0x7fffffff;
+  if (amax < 1.0f) {
+    const float steps = amax > 0.f ? ceilf(40.0f / -log2f(amax)) : 0.f;
+    if (steps < (float)(1 << 30)) wb = ((int)steps + WQB - 1) / WQB;
+  }
+  const bool sequential = wb >= chb && nblk > chb;
+  const int jc0 = min(nblk, warp * chb), jc1 = min(nblk, jc0 + chb);   // this chunk's output blocks
+
+  bool alive = true;
+  int t_issued = 0, t_done = 0, r_issued = 0, r_done = 0;   // this warp's copies: issued / waited
+  auto wait_bar = [&](uint64_t* bar, int use, int code) {
+    const bool ok = __all_sync(FULL, mbar_poll(bar, (uint32_t)(use & 1)));
+    if (!ok) {
+      if (lane == 0) atomicExch(status, code);
+      alive = false;
+    }
+    return ok;
+  };
+
+  // walk blocks js .. je-1 from the state in g2, writing outputs for blocks >= jo
+  auto walk = [&](int js, int jo, int je) {
+    const int nb = je - js;
+    // table entries + header of walk block i -> slot i % CTS (the slot's last
+    // reads are behind a __syncwarp)
+    auto issue_table = [&](int i) {
+      if (lane == 0) {
+        constexpr uint32_t bytes = (WQB + 1) * sizeof(int4);
+        sm100::fence_proxy_async_smem();
+        sm100::mbar_arrive_expect_tx(&S.tbar[i % CTS], bytes);
+        bulk_g2s(S.tab[i % CTS], tq + (int64_t)(js + i) * (WQB + 1), bytes, &S.tbar[i % CTS]);
+      }
+      ++t_issued;
+    };
+    // rows of walk block i (its table landed) -> rows buffer i % CRA
+    auto stage_rows = [&](int i) -> bool {
+      if (!wait_bar(&S.tbar[i % CTS], i / CTS, 9301)) return false;
+      ++t_done;
+      if (lane == 0) {
+        const int4 h = S.tab[i % CTS][WQB];
+        uint64_t* rb = &S.rbar[i % CRA];
+        if (h.y > 0) {
+          sm100::fence_proxy_async_smem();
+          sm100::mbar_arrive_expect_tx(rb, (uint32_t)(WRB * 32 * sizeof(float)));
+          sm100::tma_load_3d(S.rows[i % CRA], &tmV, d0, h.x, b, rb);
+        } else {
+          sm100::mbar_arrive(rb);
+        }
+      }
+      ++r_issued;
+      return true;
+    };
+    float2* col = &S.vcol[0][lane];
+    float* ys = &S.ystage[0][lane];
+    auto interp_staged = [&](int i) {
+      const int4* e = S.tab[i % CTS];
+      const float* rw = &S.rows[i % CRA][0][lane];
+#pragma unroll 8
+      for (int q = 0; q < WQB; ++q) {
+        const int4 x = e[q];
+        const float v = __fadd_rn(__fmul_rn(__int_as_float(x.w), rw[x.x]), __fmul_rn(__int_as_float(x.z), rw[x.y]));
+        col[q * 32] = make_float2(v, v);
+      }
+    };
+    auto interp_direct = [&](int i) {
+      const int4* e = S.tab[i % CTS];
+#pragma unroll 4
+      for (int q = 0; q < WQB; ++q) {
+        const int4 x = e[q];
+        const float vp = x.x >= 0 ? Vb[(int64_t)x.x * Dm + d] : 0.f;
+        const float vn = x.y >= 0 ? Vb[(int64_t)x.y * Dm + d] : 0.f;
+        const float v = __fadd_rn(__fmul_rn(__int_as_float(x.w), vp), __fmul_rn(__int_as_float(x.z), vn));
+        col[q * 32] = make_float2(v, v);
+      }
+    };
+    // recurrence of walk block i: OUT adds the readout (+ D*v) into the staged
+    // outputs; INTERP interleaves block i+1's staged interpolation
+    auto run_block = [&](auto out_c, auto interp_c, int i) {
+      constexpr bool OUT = decltype(out_c)::value, INTERP = decltype(interp_c)::value;
+      const int j = js + i;
+      const int nq = min(WQB, Lq - j * WQB);
+      float* vrow = VHAT ? vhat_out + ((int64_t)b * Lq + (int64_t)j * WQB) * Dm + d : nullptr;
+      auto step = [&](float2 v2, int q) {
+        float2 acc;
+#pragma unroll
+        for (int k = 0; k < NP2; ++k) {
+          g2[k] = ffma2(a2[k], g2[k], v2);
+          if (OUT) acc = k == 0 ? fmul2(c2[k], g2[k]) : ffma2(c2[k], g2[k], acc);
+        }
+        if (OUT) {
+          ys[q * 32] = fmaf(dsk, v2.x, acc.x + acc.y);
+          if (VHAT) vrow[(int64_t)q * Dm] = v2.x;
+        }
+      };
+      if (INTERP) {
+        const int4* e = S.tab[(i + 1) % CTS];
+        const float* rw = &S.rows[(i + 1) % CRA][0][lane];
+#pragma unroll 1
+        for (int g0 = 0; g0 < WQB; g0 += 8) {
+          int4 x[8];
+          float vp[8], vn[8];
+          float2 vc[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] = e[g0 + u];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) { vp[u] = rw[x[u].x]; vn[u] = rw[x[u].y]; }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) vc[u] = col[(g0 + u) * 32];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float v =
+                __fadd_rn(__fmul_rn(__int_as_float(x[u].w), vp[u]), __fmul_rn(__int_as_float(x[u].z), vn[u]));
+            col[(g0 + u) * 32] = make_float2(v, v);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) step(vc[u], g0 + u);
+        }
+      } else if (nq == WQB) {
+#pragma unroll 8
+        for (int q = 0; q < WQB; ++q) step(col[q * 32], q);
+      } else {
+#pragma unroll 1
+        for (int q = 0; q < nq; ++q) step(col[q * 32], q);
+      }
+    };
+    // block i's outputs: staged tile -> TMA store (rows past Lq are clipped)
+    auto store_block = [&](int i) {
+      sm100::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        sm100::tma_store_3d(&tmY, S.ystage, d0, (js + i) * WQB, b);
+        sm100::bulk_commit();
+      }
+    };
+    auto run = [&](bool out, bool interp, int i) {
+      if (out) {
+        // the previous block's store has read the staging tile
+        if (lane == 0) sm100::bulk_wait_read<0>();
+        __syncwarp();
+        if (interp) run_block(std::true_type{}, std::true_type{}, i);
+        else run_block(std::true_type{}, std::false_type{}, i);
+        store_block(i);
+      } else {
+        if (interp) run_block(std::false_type{}, std::true_type{}, i);
+        else run_block(std::false_type{}, std::false_type{}, i);
+      }
+    };
+
+    for (int i = 0; i < min(nb, CTS); ++i) issue_table(i);
+    for (int i = 0; i < min(nb, CRA); ++i)
+      if (!stage_rows(i)) return;
+    if (!wait_bar(&S.rbar[0], 0, 9302)) return;
+    ++r_done;
+    if (S.tab[0][WQB].y < 0) interp_direct(0); else interp_staged(0);
+    for (int i = 0; i < nb; ++i) {
+      __syncwarp();   // block i's rows and entries were read by every lane
+      if (i + CRA < nb && !stage_rows(i + CRA)) return;
+      if (i + CTS < nb) issue_table(i + CTS);
+      const bool out = js + i >= jo;
+      if (i + 1 < nb) {
+        if (!wait_bar(&S.rbar[(i + 1) % CRA], (i + 1) / CRA, 9302)) return;
+        ++r_done;
+        if (S.tab[(i + 1) % CTS][WQB].y >= 0) {
+          run(out, true, i);
+        } else {
+          run(out, false, i);
+          interp_direct(i + 1);
+        }
+      } else {
+        run(out, false, i);
+      }
+    }
+  };
+
+  if (!sequential) {
+    if (jc0 < jc1) walk(max(0, jc0 - wb), jc0, jc1);
+  } else {
+    for (int p = 0; p < CH_WARPS; ++p) {
+      if (warp == p && jc0 < jc1) {
+        if (p > 0) {
+#pragma unroll
+          for (int k = 0; k < NP2; ++k) g2[k] = CS.carry[k][lane];
+        }
+        walk(jc0, jc0, jc1);
+#pragma unroll
+        for (int k = 0; k < NP2; ++k) CS.carry[k][lane] = g2[k];
+      }
+      __syncthreads();
+    }
+  }
+  if (!alive) {
+    // copies still in flight after a failed wait: wait for them (bounded) before the CTA exits
+    for (; t_done < t_issued; ++t_done) mbar_poll(&S.tbar[t_done % CTS], (uint32_t)((t_done / CTS) & 1), 100000000ull);
+    for (; r_done < r_issued; ++r_done) mbar_poll(&S.rbar[r_done % CRA], (uint32_t)((r_done / CRA) & 1), 100000000ull);
+  }
+  if (lane == 0) sm100::bulk_wait<0>();   // every output tile stored before the CTA exits
+  if (alive && h_last && jc0 < jc1 && jc1 == nblk) {
+#pragma unroll
+    for (int k = 0; k < 2 * NP2; ++k) {
+      const float gk = (k & 1) ? g2[k / 2].y : g2[k / 2].x;
+      if (k < N) {
+        float ab, bb;
+        coeffs(k, ab, bb);
+        h_last[((int64_t)b * Dm + d) * N + k] = bb * gk;
+      }
+    }
+  }
+}
+
 size_t ws_flags_bytes(int64_t Bsz, int64_t T, int64_t ntiles) { return (size_t)((Bsz * ntiles * T + 255) / 256 * 256); }
-size_t ws_table_bytes(int64_t Bsz, int64_t Lq, int64_t ntiles) { return (size_t)(Bsz * ntiles * Lq * sizeof(Nbr)); }
+// the per-query table, or its blocked form (WQB entries + a header per block), whichever is larger
+size_t ws_table_bytes(int64_t Bsz, int64_t Lq, int64_t ntiles) {
+  const int64_t raw = Bsz * ntiles * Lq * (int64_t)sizeof(Nbr);
+  const int64_t blocked = Bsz * ntiles * cdiv(Lq, WQB) * (WQB + 1) * (int64_t)sizeof(int4);
+  return (size_t)std::max(raw, blocked);
+}
 
 }  // namespace
 }  // namespace tssm
@@ -725,18 +1153,56 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       return TSSM_ERR_INVALID;
     }
   }
+  // N <= 16 with whole 32-feature runs per tile: blocked table + chunked scan
+  const bool chunked = N <= 16 && Dm % 32 == 0 && FTILE % 32 == 0 && aligned16(V) && aligned16(y);
   {
     const size_t shm = (size_t)T * 12;
-    if (shm > 48 * 1024 &&
-        cudaFuncSetAttribute(interp_neighbors_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm) != cudaSuccess)
+    auto nk = chunked ? interp_neighbors_kernel<true> : interp_neighbors_kernel<false>;
+    if (shm > 48 * 1024 && cudaFuncSetAttribute(nk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm) != cudaSuccess)
       return check_launch("interp_ssm: neighbour smem");
     const int qsplit = (int)std::max<int64_t>(1, std::min<int64_t>(8, cdiv(Lq, 512)));
-    interp_neighbors_kernel<<<dim3((unsigned)ntiles, (unsigned)Bsz, (unsigned)qsplit), NB_THREADS, shm, st>>>(
+    nk<<<dim3((unsigned)ntiles, (unsigned)Bsz, (unsigned)qsplit), NB_THREADS, shm, st>>>(
         flags, (const float*)tau, (const float*)q, tab, (int)T, (int)Lq, (int)K, ntiles);
+  }
+  const float* Vf = (const float*)V;
+  if (chunked) {
+    int* status = device_status_ptr();
+    if (!status) {
+      set_error("interp_ssm: device status word unavailable");
+      return TSSM_ERR_CUDA;
+    }
+    TSSM_REQUIRE(Bsz * (Dm / 32) < (int64_t(1) << 31), "interp_ssm: size exceeds the grid");
+    CUtensorMap tmV, tmY;
+    if (!tmap3d_f32(&tmV, V, (uint64_t)Dm, (uint64_t)T, (uint64_t)Bsz, 32, WRB) ||
+        !tmap3d_f32(&tmY, y, (uint64_t)Dm, (uint64_t)Lq, (uint64_t)Bsz, 32, WQB)) {
+      set_error("interp_ssm: cuTensorMapEncodeTiled failed");
+      return TSSM_ERR_CUDA;
+    }
+    const size_t shm = sizeof(ChunkSmem) + 128;   // + alignment slack
+#define CHUNK_SCAN_LAUNCH(NP2, VH)                                                                              \
+  do {                                                                                                          \
+    if (cudaFuncSetAttribute(interp_ssm_scan_chunk_kernel<NP2, VH>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             (int)shm) != cudaSuccess)                                                          \
+      return check_launch("interp_ssm: scan smem");                                                             \
+    interp_ssm_scan_chunk_kernel<NP2, VH><<<(unsigned)(Bsz * (Dm / 32)), CH_WARPS * 32, shm, st>>>(            \
+        tmV, tmY, Vf, reinterpret_cast<const int4*>(tab), (const float*)A_log, (const float*)B, (const float*)C, \
+        (const float*)Dskip, (const float*)dt, (float*)h_last, (float*)vhat, status, (int)T, (int)Dm, (int)N,   \
+        (int)Lq, (int)FTILE, ntiles);                                                                           \
+  } while (0)
+    if (vhat) {
+      if (N <= 4) CHUNK_SCAN_LAUNCH(2, true);
+      else if (N <= 8) CHUNK_SCAN_LAUNCH(4, true);
+      else CHUNK_SCAN_LAUNCH(8, true);
+    } else {
+      if (N <= 4) CHUNK_SCAN_LAUNCH(2, false);
+      else if (N <= 8) CHUNK_SCAN_LAUNCH(4, false);
+      else CHUNK_SCAN_LAUNCH(8, false);
+    }
+#undef CHUNK_SCAN_LAUNCH
+    return check_launch("interp_ssm");
   }
   dim3 grid((unsigned)cdiv(Dm, 32), (unsigned)Bsz);
   const int npt = (int)cdiv(N, SCAN_SW);
-  const float* Vf = (const float*)V;
   const float* al = (const float*)A_log;
   const float* bp = (const float*)B;
   const float* cp = (const float*)C;

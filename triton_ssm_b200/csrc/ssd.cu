@@ -39,6 +39,7 @@
 
 #include "common.cuh"
 #include "tcgen05.cuh"
+#include "tmap.cuh"
 
 namespace tssm {
 #ifdef TSSM_SSD_TRACE
@@ -677,21 +678,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
 // 3-D bf16 map over [d2][d1][d0] (d0 contiguous) with a {64, 64, 1} box and 128B swizzle.
 bool map3d_bf16(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2) {
-  auto fn = encode_fn();
+  auto fn = tmap_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {d0, d1, d2};
   cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
