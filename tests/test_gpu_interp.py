@@ -118,6 +118,21 @@ def test_interp_ssm_feature_tiles(cuda_ops, FTILE, p_obs):
     assert rel_err(h, rh) < TOL_FP32
 
 
+@pytest.mark.parametrize("dt_scale", [1e-3, 1.0])
+def test_interp_ssm_slow_and_fast_decay(cuda_ops, dt_scale):
+    """A small dt (Abar near 1, slow decay) makes the scan carry state across the
+    whole query range; a large one forgets within a few queries."""
+    Bt, T, Dm, N, Lq = 2, 500, 64, 16, 2000
+    V, M, tau, A_log, B, C, D = make_c3(Bt, T, Dm, N, Lq, seed=11)
+    q = oracle.linspace_queries(tau, Lq)
+    dt = torch.full((Bt,), dt_scale)
+    y, h = cuda_ops.fused_interp_ssm(cu(V), cu(M), cu(tau), cu(A_log), cu(B), cu(C), q=cu(q), dt=cu(dt),
+                                     D=cu(D), return_state=True)
+    ry, rh = oracle.interp_ssm(V, M, tau, A_log, B, C, dt, q=q, D=D)
+    assert rel_err(y, ry) < TOL_FP32
+    assert rel_err(h, rh) < TOL_FP32
+
+
 def test_interp_ssm_regular_grid_argument(cuda_ops):
     V, M, tau, A_log, B, C, D = make_c3(2, 200, 64, 16, 400, seed=8)
     y = cuda_ops.fused_interp_ssm(cu(V), cu(M), cu(tau), cu(A_log), cu(B), cu(C), L_q=400)

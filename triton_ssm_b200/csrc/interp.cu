@@ -225,18 +225,20 @@ struct Nbr {
 
 // Blocked form of the neighbour table read by the chunked scan kernel: per
 // block of WQB consecutive queries, WQB entries (a, b, w, 1-w) and a header
-// (lo, span).  The block's operands are rows lo .. lo+span-1 of the
-// observations; an entry's a and b are offsets (row - lo) * 32 into those rows
-// staged as [span][32 features], with the reference's priority resolved here
-// (pair -> lerp; else prev, next, cur -> a, b = the zero row after WRB staged
-// rows, w = 0), so the scan evaluates round((1-w)*row[a]) + round(w*row[b])
-// for every query.  span = -1: the rows span more than WRB; a and b then hold
-// absolute rows (-1: zero) and the scan gathers from global memory.
+// (lo, span).  The block's operands are rows lo .. lo+span-1 of the batch
+// row's observations, which the scan stages as [WRB][32 features] followed by
+// a zero row; a and b are offsets (row - lo) * 32 into that tile, with the
+// reference's priority resolved here (pair -> a = prev, b = next; else
+// a = prev, next or cur, b = the zero row, w = 0; no operand at all -> the
+// zero row), so the scan evaluates round((1-w)*row[a]) + round(w*row[b]) for
+// every query.  span = -1: the rows span more than WRB; a and b are then
+// element offsets row * Dm (-1: no operand) and the scan gathers from global
+// memory.
 constexpr int WQB = 32;   // queries per block
 constexpr int WRB = 40;   // rows the scan stages per block (a zero row follows them)
 
 // Warp-collective: lane i holds query i of a block (p, n, c = prev/next/cur or -1).
-__device__ __forceinline__ int4 blocked_entry(int p, int n, int c, float w, int& lo_out, int& span_out) {
+__device__ __forceinline__ void blocked_entry(int p, int n, int c, float w, int Dm, int4& entry, int4& header) {
   constexpr unsigned FULL = 0xffffffffu;
   int mn = 0x7fffffff, mx = -1;
   if (p >= 0) { mn = min(mn, p); mx = max(mx, p); }
@@ -251,11 +253,10 @@ __device__ __forceinline__ int4 blocked_entry(int p, int n, int c, float w, int&
   if (p >= 0 && n >= 0) { sp = p; sn = n; ww = w; om = 1.0f - w; }
   else { sp = p >= 0 ? p : (n >= 0 ? n : c); sn = -1; ww = 0.f; om = 1.f; }
   int op, on;
-  if (direct) { op = sp; on = sn; }
+  if (direct) { op = sp >= 0 ? sp * Dm : -1; on = sn >= 0 ? sn * Dm : -1; }
   else { op = sp >= 0 ? (sp - lo) * 32 : WRB * 32; on = sn >= 0 ? (sn - lo) * 32 : WRB * 32; }
-  lo_out = lo;
-  span_out = direct ? -1 : span;
-  return make_int4(op, on, __float_as_int(ww), __float_as_int(om));
+  entry = make_int4(op, on, __float_as_int(ww), __float_as_int(om));
+  header = make_int4(lo, direct ? -1 : span, 0, 0);
 }
 
 // Kernel 2: per (tile, b, query slice): last/next flagged index scans in shared
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint
                                                                       const float* __restrict__ tau,
                                                                       const float* __restrict__ q,
                                                                       Nbr* __restrict__ tab, int T, int Lq, int K,
-                                                                      int ntiles) {
+                                                                      int ntiles, int Dm) {
   extern __shared__ int shi[];
   int* lastf = shi;          // [T] largest j <= i with flag[j], else -1
   int* nextf = shi + T;      // [T] smallest j >= i with flag[j], else T (none)
@@ -360,10 +361,11 @@ __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint
         const float tn = next >= 0 ? stau[next] : 0.f;
         w = weight_ref(tq, tp, tn);
       }
-      int lo, span;
-      const int4 e = blocked_entry(prev, next, cur, w, lo, span);
+      // lanes past Lq hold (-1, -1, -1): no operand (a partial block never takes the pair-only path)
+      int4 e, hdr;
+      blocked_entry(prev, next, cur, w, Dm, e, hdr);
       outb[(int64_t)jb * (WQB + 1) + lane] = e;
-      if (lane == 0) outb[(int64_t)jb * (WQB + 1) + WQB] = make_int4(lo, span, 0, 0);
+      if (lane == 0) outb[(int64_t)jb * (WQB + 1) + WQB] = hdr;
     }
     return;
   }
@@ -699,11 +701,12 @@ constexpr size_t kScanSmem = 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr) + 2 * QB *
 // ---------------------------------------------------------------------------
 // Kernel 3b, for N <= 16 with runs of 32 features inside one tile (Dm % 32 ==
 // 0, FTILE % 32 == 0), reading the blocked table.  CTA = (b, 32 features),
-// four warps; each warp owns EVERY state of its 32 features (lane = feature,
-// N/2 packed pairs in registers: nothing is exchanged between warps) and walks
-// one quarter (a "chunk") of the query blocks.  The walk is FP32-pipe bound
-// (two FMAs per state and query), so the four chunks per row are what keeps
-// two warps on every scheduler.
+// eight warps; each warp owns EVERY state of its 32 features (lane = feature,
+// N/2 packed pairs in registers, nothing exchanged between warps) and walks
+// one eighth (a "chunk") of the query blocks.  The walk is FP32-pipe bound
+// (two FMAs per state and query) and one warp issues well below the pipe's
+// rate, so the kernel is shaped for occupancy: ~12 KB of shared memory per
+// warp, two CTAs (sixteen warps) per SM.
 //
 // A chunk needs the state at its first query.  The recurrence forgets at rate
 // Abar: after W steps an earlier state contributes at most amax^W of itself,
@@ -711,27 +714,24 @@ constexpr size_t kScanSmem = 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr) + 2 * QB *
 // starts its walk W queries early from a zero state (W: amax^W <= 2^-40,
 // rounded up to whole blocks) and writes outputs from its own first query
 // on; the dropped term is below 2^-40 of the state, far inside fp32 rounding.
-// When W exceeds a chunk (slow decay: small dt*|A|), the four chunks run one
-// after another instead, each starting from the previous chunk's final state.
+// When W exceeds a chunk (slow decay: small dt*|A|), the chunks run one after
+// another instead, each starting from the previous chunk's final state.
 //
-// Per warp, blocks of WQB = 32 queries: the warp's lane 0 streams its blocked
-// table (entries + header; one bulk copy per block) CTS blocks ahead and each
-// block's observation rows (one TMA tile of WRB rows x 32 features from the
-// header's first row) CRA blocks ahead, both completing on mbarriers; the
-// warp runs block k's recurrence and readout interleaved with block k+1's
-// interpolation (values pass through a per-lane column of shared memory), and
-// block k's outputs leave as one TMA tile store of 32 queries x 32 features.
-constexpr int CH_WARPS = 4;   // chunks (warps) per CTA
-constexpr int CRA = 2;        // rows of block k+CRA are requested while block k runs
-constexpr int CTS = 4;        // table of block k+CTS likewise
+// Per warp, blocks of WQB = 32 queries: lane 0 streams the blocked table
+// (entries + header, one bulk copy per block) two blocks ahead and, once a
+// block's table has landed, its observation rows (one TMA tile of WRB rows x
+// 32 features) one block ahead, both completing on mbarriers; each block's
+// values are interpolated from the staged rows into registers eight queries
+// at a time, and the outputs go out as coalesced 128-byte rows.
+constexpr int CH_WARPS = 8;   // chunks (warps) per CTA
+constexpr int CTS = 3;        // table slots: block k running, k+1 landed, k+2 in flight
+constexpr int CRB = 2;        // row buffers: block k running, k+1 in flight
 
 struct alignas(128) ChunkWarpSmem {
-  float rows[CRA][WRB + 1][32];   // staged observation rows; row WRB stays zero
-  float ystage[WQB][32];          // outputs of one block, stored by TMA
-  float2 vcol[WQB][32];           // interpolated values (v, v), one column per lane
+  float rows[CRB][WRB + 1][32];   // staged observation rows; row WRB stays zero
   int4 tab[CTS][WQB + 1];         // blocked table entries + header
   uint64_t tbar[CTS];
-  uint64_t rbar[CRA];
+  uint64_t rbar[CRB];
 };
 struct alignas(128) ChunkSmem {
   ChunkWarpSmem w[CH_WARPS];
@@ -761,13 +761,12 @@ __device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, uint64
 }
 
 template <int NP2, bool VHAT>
-__global__ void __launch_bounds__(CH_WARPS * 32) interp_ssm_scan_chunk_kernel(
-    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmY,
-    const float* __restrict__ Vp, const int4* __restrict__ tabq, const float* __restrict__ A_log,
-    const float* __restrict__ Bp, const float* __restrict__ Cp, const float* __restrict__ Dskip,
-    const float* __restrict__ dt, float* __restrict__ h_last, float* __restrict__ vhat_out,
-    int* __restrict__ status, int T, int Dm, int N, int Lq, int FTILE, int ntiles) {
-  extern __shared__ __align__(128) uint8_t dsm[];
+__global__ void __launch_bounds__(CH_WARPS * 32, 2) interp_ssm_scan_chunk_kernel(
+    const __grid_constant__ CUtensorMap tmV, const float* __restrict__ Vp, const int4* __restrict__ tabq,
+    const float* __restrict__ A_log, const float* __restrict__ Bp, const float* __restrict__ Cp,
+    const float* __restrict__ Dskip, const float* __restrict__ dt, float* __restrict__ y, float* __restrict__ h_last,
+    float* __restrict__ vhat_out, int* __restrict__ status, int T, int Dm, int N, int Lq, int FTILE, int ntiles) {
+  extern __shared__ __align__(16) uint8_t dsm[];
   ChunkSmem& CS = *reinterpret_cast<ChunkSmem*>(dsm + ((128u - (sm100::smem_u32(dsm) & 127u)) & 127u));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   ChunkWarpSmem& S = CS.w[warp];
@@ -775,18 +774,17 @@ __global__ void __launch_bounds__(CH_WARPS * 32) interp_ssm_scan_chunk_kernel(
   const int b = blockIdx.x / dpr, d0 = (blockIdx.x % dpr) * 32, d = d0 + lane;
   const int nblk = (Lq + WQB - 1) / WQB;
   const int4* tq = tabq + ((int64_t)b * ntiles + d0 / FTILE) * nblk * (WQB + 1);
-  const float* Vb = Vp + (int64_t)b * T * Dm;
+  const float* Vl = Vp + (int64_t)b * T * Dm + d;   // this lane's feature; + row * Dm
   constexpr unsigned FULL = 0xffffffffu;
 
   if (lane == 0) {
     for (int i = 0; i < CTS; ++i) sm100::mbar_init(&S.tbar[i], 1);
-    for (int i = 0; i < CRA; ++i) sm100::mbar_init(&S.rbar[i], 1);
+    for (int i = 0; i < CRB; ++i) sm100::mbar_init(&S.rbar[i], 1);
     sm100::fence_mbar_init();
-    sm100::prefetch_tmap(&tmV);
-    sm100::prefetch_tmap(&tmY);
+    if (warp == 0) sm100::prefetch_tmap(&tmV);
   }
 #pragma unroll
-  for (int i = 0; i < CRA; ++i) S.rows[i][WRB][lane] = 0.f;
+  for (int i = 0; i < CRB; ++i) S.rows[i][WRB][lane] = 0.f;
   __syncwarp();
 
   // this lane's states: Abar and C*Bbar as packed pairs; amax over the CTA's
@@ -843,8 +841,8 @@ __global__ void __launch_bounds__(CH_WARPS * 32) interp_ssm_scan_chunk_kernel(
   // walk blocks js .. je-1 from the state in g2, writing outputs for blocks >= jo
   auto walk = [&](int js, int jo, int je) {
     const int nb = je - js;
-    // table entries + header of walk block i -> slot i % CTS (the slot's last
-    // reads are behind a __syncwarp)
+    // table entries + header of walk block i -> slot i % CTS (its last reads are
+    // behind a __syncwarp)
     auto issue_table = [&](int i) {
       if (lane == 0) {
         constexpr uint32_t bytes = (WQB + 1) * sizeof(int4);
@@ -854,17 +852,17 @@ __global__ void __launch_bounds__(CH_WARPS * 32) interp_ssm_scan_chunk_kernel(
       }
       ++t_issued;
     };
-    // rows of walk block i (its table landed) -> rows buffer i % CRA
+    // table of walk block i landed -> its rows into row buffer i % CRB (last read behind a __syncwarp)
     auto stage_rows = [&](int i) -> bool {
       if (!wait_bar(&S.tbar[i % CTS], i / CTS, 9301)) return false;
       ++t_done;
       if (lane == 0) {
         const int4 h = S.tab[i % CTS][WQB];
-        uint64_t* rb = &S.rbar[i % CRA];
+        uint64_t* rb = &S.rbar[i % CRB];
         if (h.y > 0) {
           sm100::fence_proxy_async_smem();
           sm100::mbar_arrive_expect_tx(rb, (uint32_t)(WRB * 32 * sizeof(float)));
-          sm100::tma_load_3d(S.rows[i % CRA], &tmV, d0, h.x, b, rb);
+          sm100::tma_load_3d(S.rows[i % CRB], &tmV, d0, h.x, b, rb);
         } else {
           sm100::mbar_arrive(rb);
         }
@@ -872,150 +870,121 @@ __global__ void __launch_bounds__(CH_WARPS * 32) interp_ssm_scan_chunk_kernel(
       ++r_issued;
       return true;
     };
-    float2* col = &S.vcol[0][lane];
-    float* ys = &S.ystage[0][lane];
-    auto interp_staged = [&](int i) {
-      const int4* e = S.tab[i % CTS];
-      const float* rw = &S.rows[i % CRA][0][lane];
-#pragma unroll 8
-      for (int q = 0; q < WQB; ++q) {
-        const int4 x = e[q];
-        const float v = __fadd_rn(__fmul_rn(__int_as_float(x.w), rw[x.x]), __fmul_rn(__int_as_float(x.z), rw[x.y]));
-        col[q * 32] = make_float2(v, v);
+    // one query: readout of the state after the previous query (lagged one
+    // step: every dependent readout FMA has an independent update FMA beside
+    // it), then the update by v
+    auto readout_update = [&](float2& acc, float2 v2) {
+#pragma unroll
+      for (int k = 0; k < NP2; ++k) {
+        acc = k == 0 ? fmul2(c2[k], g2[k]) : ffma2(c2[k], g2[k], acc);
+        g2[k] = ffma2(a2[k], g2[k], v2);
       }
     };
-    auto interp_direct = [&](int i) {
-      const int4* e = S.tab[i % CTS];
-#pragma unroll 4
-      for (int q = 0; q < WQB; ++q) {
-        const int4 x = e[q];
-        const float vp = x.x >= 0 ? Vb[(int64_t)x.x * Dm + d] : 0.f;
-        const float vn = x.y >= 0 ? Vb[(int64_t)x.y * Dm + d] : 0.f;
-        const float v = __fadd_rn(__fmul_rn(__int_as_float(x.w), vp), __fmul_rn(__int_as_float(x.z), vn));
-        col[q * 32] = make_float2(v, v);
-      }
-    };
-    // recurrence of walk block i: OUT adds the readout (+ D*v) into the staged
-    // outputs; INTERP interleaves block i+1's staged interpolation
-    auto run_block = [&](auto out_c, auto interp_c, int i) {
-      constexpr bool OUT = decltype(out_c)::value, INTERP = decltype(interp_c)::value;
+    auto run_block = [&](int i, bool out) {
       const int j = js + i;
       const int nq = min(WQB, Lq - j * WQB);
+      const int4* e = S.tab[i % CTS];
+      const bool direct = e[WQB].y < 0;
+      const float* rw = &S.rows[i % CRB][0][lane];
+      float* yrow = y + ((int64_t)b * Lq + (int64_t)j * WQB) * Dm + d;
       float* vrow = VHAT ? vhat_out + ((int64_t)b * Lq + (int64_t)j * WQB) * Dm + d : nullptr;
-      auto step = [&](float2 v2, int q) {
-        float2 acc;
-#pragma unroll
-        for (int k = 0; k < NP2; ++k) {
-          g2[k] = ffma2(a2[k], g2[k], v2);
-          if (OUT) acc = k == 0 ? fmul2(c2[k], g2[k]) : ffma2(c2[k], g2[k], acc);
-        }
-        if (OUT) {
-          ys[q * 32] = fmaf(dsk, v2.x, acc.x + acc.y);
-          if (VHAT) vrow[(int64_t)q * Dm] = v2.x;
-        }
-      };
-      if (INTERP) {
-        const int4* e = S.tab[(i + 1) % CTS];
-        const float* rw = &S.rows[(i + 1) % CRA][0][lane];
+      float vprev = 0.f;
+      if (out && nq == WQB && !direct) {
+        // hot path: eight queries per group, values straight into registers
 #pragma unroll 1
         for (int g0 = 0; g0 < WQB; g0 += 8) {
           int4 x[8];
           float vp[8], vn[8];
-          float2 vc[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) x[u] = e[g0 + u];
 #pragma unroll
           for (int u = 0; u < 8; ++u) { vp[u] = rw[x[u].x]; vn[u] = rw[x[u].y]; }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) vc[u] = col[(g0 + u) * 32];
+          float* yg = yrow + (int64_t)(g0 - 1) * Dm;   // the readout of query q lands one step later
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const float v =
                 __fadd_rn(__fmul_rn(__int_as_float(x[u].w), vp[u]), __fmul_rn(__int_as_float(x[u].z), vn[u]));
-            col[(g0 + u) * 32] = make_float2(v, v);
+            float2 acc;
+            readout_update(acc, make_float2(v, v));
+            if (u > 0 || g0 > 0) {
+              *yg = fmaf(dsk, vprev, acc.x + acc.y);
+              if (VHAT) vrow[(int64_t)(g0 + u - 1) * Dm] = vprev;
+            }
+            yg += Dm;
+            vprev = v;
           }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) step(vc[u], g0 + u);
         }
-      } else if (nq == WQB) {
-#pragma unroll 8
-        for (int q = 0; q < WQB; ++q) step(col[q * 32], q);
       } else {
+        // cold path: warm-up blocks, a partial last block, gathered blocks
 #pragma unroll 1
-        for (int q = 0; q < nq; ++q) step(col[q * 32], q);
+        for (int q = 0; q < nq; ++q) {
+          const int4 x = e[q];
+          float vp, vn;
+          if (!direct) {
+            vp = rw[x.x];
+            vn = rw[x.y];
+          } else {
+            vp = x.x >= 0 ? Vl[x.x] : 0.f;
+            vn = x.y >= 0 ? Vl[x.y] : 0.f;
+          }
+          const float v = __fadd_rn(__fmul_rn(__int_as_float(x.w), vp), __fmul_rn(__int_as_float(x.z), vn));
+          if (out) {
+            float2 acc;
+            readout_update(acc, make_float2(v, v));
+            if (q > 0) {
+              yrow[(int64_t)(q - 1) * Dm] = fmaf(dsk, vprev, acc.x + acc.y);
+              if (VHAT) vrow[(int64_t)(q - 1) * Dm] = vprev;
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < NP2; ++k) g2[k] = ffma2(a2[k], g2[k], make_float2(v, v));
+          }
+          vprev = v;
+        }
       }
-    };
-    // block i's outputs: staged tile -> TMA store (rows past Lq are clipped)
-    auto store_block = [&](int i) {
-      sm100::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        sm100::tma_store_3d(&tmY, S.ystage, d0, (js + i) * WQB, b);
-        sm100::bulk_commit();
-      }
-    };
-    auto run = [&](bool out, bool interp, int i) {
-      if (out) {
-        // the previous block's store has read the staging tile
-        if (lane == 0) sm100::bulk_wait_read<0>();
-        __syncwarp();
-        if (interp) run_block(std::true_type{}, std::true_type{}, i);
-        else run_block(std::true_type{}, std::false_type{}, i);
-        store_block(i);
-      } else {
-        if (interp) run_block(std::false_type{}, std::true_type{}, i);
-        else run_block(std::false_type{}, std::false_type{}, i);
+      if (out && nq > 0) {   // the block's last readout
+        float2 acc;
+#pragma unroll
+        for (int k = 0; k < NP2; ++k) acc = k == 0 ? fmul2(c2[k], g2[k]) : ffma2(c2[k], g2[k], acc);
+        yrow[(int64_t)(nq - 1) * Dm] = fmaf(dsk, vprev, acc.x + acc.y);
+        if (VHAT) vrow[(int64_t)(nq - 1) * Dm] = vprev;
       }
     };
 
-    for (int i = 0; i < min(nb, CTS); ++i) issue_table(i);
-    for (int i = 0; i < min(nb, CRA); ++i)
-      if (!stage_rows(i)) return;
-    if (!wait_bar(&S.rbar[0], 0, 9302)) return;
-    ++r_done;
-    if (S.tab[0][WQB].y < 0) interp_direct(0); else interp_staged(0);
+    for (int i = 0; i < min(nb, CTS - 1); ++i) issue_table(i);
+    if (!stage_rows(0)) return;
     for (int i = 0; i < nb; ++i) {
-      __syncwarp();   // block i's rows and entries were read by every lane
-      if (i + CRA < nb && !stage_rows(i + CRA)) return;
-      if (i + CTS < nb) issue_table(i + CTS);
-      const bool out = js + i >= jo;
-      if (i + 1 < nb) {
-        if (!wait_bar(&S.rbar[(i + 1) % CRA], (i + 1) / CRA, 9302)) return;
-        ++r_done;
-        if (S.tab[(i + 1) % CTS][WQB].y >= 0) {
-          run(out, true, i);
-        } else {
-          run(out, false, i);
-          interp_direct(i + 1);
-        }
-      } else {
-        run(out, false, i);
-      }
+      __syncwarp();   // block i-1's rows and entries were read by every lane
+      if (i + CTS - 1 < nb) issue_table(i + CTS - 1);
+      if (i + 1 < nb && !stage_rows(i + 1)) return;
+      if (!wait_bar(&S.rbar[i % CRB], i / CRB, 9302)) return;
+      ++r_done;
+      run_block(i, js + i >= jo);
     }
   };
 
-  if (!sequential) {
-    if (jc0 < jc1) walk(max(0, jc0 - wb), jc0, jc1);
-  } else {
-    for (int p = 0; p < CH_WARPS; ++p) {
-      if (warp == p && jc0 < jc1) {
-        if (p > 0) {
+  // warm-up mode: every warp walks its chunk at once; sequential mode: the
+  // chunks in order, each starting from the previous one's final state
+#pragma unroll 1
+  for (int p = 0; p < (sequential ? CH_WARPS : 1); ++p) {
+    if (jc0 < jc1 && (!sequential || warp == p)) {
+      if (sequential && p > 0) {
 #pragma unroll
-          for (int k = 0; k < NP2; ++k) g2[k] = CS.carry[k][lane];
-        }
-        walk(jc0, jc0, jc1);
+        for (int k = 0; k < NP2; ++k) g2[k] = CS.carry[k][lane];
+      }
+      walk(sequential ? jc0 : max(0, jc0 - wb), jc0, jc1);
+      if (sequential) {
 #pragma unroll
         for (int k = 0; k < NP2; ++k) CS.carry[k][lane] = g2[k];
       }
-      __syncthreads();
     }
+    if (sequential) __syncthreads();
   }
   if (!alive) {
     // copies still in flight after a failed wait: wait for them (bounded) before the CTA exits
     for (; t_done < t_issued; ++t_done) mbar_poll(&S.tbar[t_done % CTS], (uint32_t)((t_done / CTS) & 1), 100000000ull);
-    for (; r_done < r_issued; ++r_done) mbar_poll(&S.rbar[r_done % CRA], (uint32_t)((r_done / CRA) & 1), 100000000ull);
+    for (; r_done < r_issued; ++r_done) mbar_poll(&S.rbar[r_done % CRB], (uint32_t)((r_done / CRB) & 1), 100000000ull);
   }
-  if (lane == 0) sm100::bulk_wait<0>();   // every output tile stored before the CTA exits
   if (alive && h_last && jc0 < jc1 && jc1 == nblk) {
 #pragma unroll
     for (int k = 0; k < 2 * NP2; ++k) {
@@ -1154,7 +1123,7 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
     }
   }
   // N <= 16 with whole 32-feature runs per tile: blocked table + chunked scan
-  const bool chunked = N <= 16 && Dm % 32 == 0 && FTILE % 32 == 0 && aligned16(V) && aligned16(y);
+  const bool chunked = N <= 16 && Dm % 32 == 0 && FTILE % 32 == 0 && T * Dm < (int64_t(1) << 31) && aligned16(V);
   {
     const size_t shm = (size_t)T * 12;
     auto nk = chunked ? interp_neighbors_kernel<true> : interp_neighbors_kernel<false>;
@@ -1162,7 +1131,7 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       return check_launch("interp_ssm: neighbour smem");
     const int qsplit = (int)std::max<int64_t>(1, std::min<int64_t>(8, cdiv(Lq, 512)));
     nk<<<dim3((unsigned)ntiles, (unsigned)Bsz, (unsigned)qsplit), NB_THREADS, shm, st>>>(
-        flags, (const float*)tau, (const float*)q, tab, (int)T, (int)Lq, (int)K, ntiles);
+        flags, (const float*)tau, (const float*)q, tab, (int)T, (int)Lq, (int)K, ntiles, (int)Dm);
   }
   const float* Vf = (const float*)V;
   if (chunked) {
@@ -1172,24 +1141,23 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       return TSSM_ERR_CUDA;
     }
     TSSM_REQUIRE(Bsz * (Dm / 32) < (int64_t(1) << 31), "interp_ssm: size exceeds the grid");
-    CUtensorMap tmV, tmY;
-    if (!tmap3d_f32(&tmV, V, (uint64_t)Dm, (uint64_t)T, (uint64_t)Bsz, 32, WRB) ||
-        !tmap3d_f32(&tmY, y, (uint64_t)Dm, (uint64_t)Lq, (uint64_t)Bsz, 32, WQB)) {
+    CUtensorMap tmV;
+    if (!tmap3d_f32(&tmV, V, (uint64_t)Dm, (uint64_t)T, (uint64_t)Bsz, 32, WRB)) {
       set_error("interp_ssm: cuTensorMapEncodeTiled failed");
       return TSSM_ERR_CUDA;
     }
     const size_t shm = sizeof(ChunkSmem) + 128;   // + alignment slack
 #define CHUNK_SCAN_LAUNCH(NP2, VH)                                                                              \
   do {                                                                                                          \
-    if (cudaFuncSetAttribute(interp_ssm_scan_chunk_kernel<NP2, VH>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)shm) != cudaSuccess)                                                          \
+    auto kern = interp_ssm_scan_chunk_kernel<NP2, VH>;                                                         \
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm) != cudaSuccess)       \
       return check_launch("interp_ssm: scan smem");                                                             \
-    interp_ssm_scan_chunk_kernel<NP2, VH><<<(unsigned)(Bsz * (Dm / 32)), CH_WARPS * 32, shm, st>>>(            \
-        tmV, tmY, Vf, reinterpret_cast<const int4*>(tab), (const float*)A_log, (const float*)B, (const float*)C, \
-        (const float*)Dskip, (const float*)dt, (float*)h_last, (float*)vhat, status, (int)T, (int)Dm, (int)N,   \
-        (int)Lq, (int)FTILE, ntiles);                                                                           \
+    kern<<<(unsigned)(Bsz * (Dm / 32)), CH_WARPS * 32, shm, st>>>(                                              \
+        tmV, Vf, reinterpret_cast<const int4*>(tab), (const float*)A_log, (const float*)B, (const float*)C,     \
+        (const float*)Dskip, (const float*)dt, (float*)y, (float*)h_last, (float*)vhat, status, (int)T,         \
+        (int)Dm, (int)N, (int)Lq, (int)FTILE, ntiles);                                                          \
   } while (0)
-    if (vhat) {
+    if (vhat) {   // states per lane as pairs
       if (N <= 4) CHUNK_SCAN_LAUNCH(2, true);
       else if (N <= 8) CHUNK_SCAN_LAUNCH(4, true);
       else CHUNK_SCAN_LAUNCH(8, true);
