@@ -210,9 +210,20 @@ __global__ void __launch_bounds__(256) interp_flags_u8x16_kernel(const uint4* __
   }
   for (int o = wpt >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o, wpt);
   if (i < nwords && (i % wpt) == 0) {
-    const int64_t row = i / wpr;                 // b*T + t
-    const int tile = (int)((i - row * wpr) / wpt);
-    const int64_t b = row / T, t = row - b * T;
+    int64_t row, b, t;
+    int tile;
+    if (nwords < (int64_t(1) << 31)) {   // 32-bit index arithmetic (64-bit division is slow)
+      const uint32_t ii = (uint32_t)i, r32 = ii / (uint32_t)wpr;
+      tile = (int)((ii - r32 * (uint32_t)wpr) / (uint32_t)wpt);
+      const uint32_t b32 = r32 / (uint32_t)T;
+      b = b32;
+      t = r32 - b32 * (uint32_t)T;
+    } else {
+      row = i / wpr;                 // b*T + t
+      tile = (int)((i - row * wpr) / wpt);
+      b = row / T;
+      t = row - b * T;
+    }
     flags[(b * ntiles + tile) * T + t] = sum > 0;
   }
 }
@@ -263,28 +274,27 @@ __device__ __forceinline__ void blocked_entry(int p, int n, int c, float w, int 
 // memory, then one entry per query.  Each thread walks a contiguous run of
 // sorted queries with two monotone pointers (lo = #{tau < q}, hi = #{tau <= q}).
 constexpr int NB_THREADS = 256;
-template <bool BLOCKED>
-__global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint8_t* __restrict__ flags,
-                                                                      const float* __restrict__ tau,
-                                                                      const float* __restrict__ q,
-                                                                      Nbr* __restrict__ tab, int T, int Lq, int K,
-                                                                      int ntiles, int Dm) {
+template <bool BLOCKED, int NT>
+__global__ void __launch_bounds__(NT) interp_neighbors_kernel(const uint8_t* __restrict__ flags,
+                                                              const float* __restrict__ tau,
+                                                              const float* __restrict__ q, Nbr* __restrict__ tab,
+                                                              int T, int Lq, int K, int ntiles, int Dm) {
   extern __shared__ int shi[];
   int* lastf = shi;          // [T] largest j <= i with flag[j], else -1
   int* nextf = shi + T;      // [T] smallest j >= i with flag[j], else T (none)
   float* stau = reinterpret_cast<float*>(shi + 2 * T);
-  __shared__ int agg_l[NB_THREADS], agg_n[NB_THREADS];
+  __shared__ int agg_l[NT / 32], agg_n[NT / 32];
   const int tile = blockIdx.x, b = blockIdx.y;
   const uint8_t* fl = flags + ((int64_t)b * ntiles + tile) * T;
   const float* tb = tau + (int64_t)b * T;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < T; i += NB_THREADS) {
+  for (int i = tid; i < T; i += NT) {
     lastf[i] = fl[i] ? i : -1;
     nextf[i] = fl[i] ? i : T;
     stau[i] = tb[i];
   }
   __syncthreads();
-  const int seg = (T + NB_THREADS - 1) / NB_THREADS;
+  const int seg = (T + NT - 1) / NT;
   const int s0 = min(T, tid * seg), s1 = min(T, s0 + seg);
   int runl = -1, runn = T;
   for (int i = s0; i < s1; ++i) runl = max(runl, lastf[i]);
@@ -303,7 +313,7 @@ __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint
   __syncthreads();
   int cl = -1, cn = T;
   for (int w = 0; w < warp; ++w) cl = max(cl, agg_l[w]);
-  for (int w = NB_THREADS / 32 - 1; w > warp; --w) cn = min(cn, agg_n[w]);
+  for (int w = NT / 32 - 1; w > warp; --w) cn = min(cn, agg_n[w]);
   int excl_l = __shfl_up_sync(0xffffffffu, incl_l, 1);
   int excl_n = __shfl_down_sync(0xffffffffu, incl_n, 1);
   excl_l = lane == 0 ? cl : max(cl, excl_l);
@@ -322,10 +332,26 @@ __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint
     int4* outb = reinterpret_cast<int4*>(tab) + ((int64_t)b * ntiles + tile) * nblk * (WQB + 1);
     const int per_cta = (nblk + gridDim.z - 1) / gridDim.z;
     const int jb1 = min(nblk, (int)blockIdx.z * per_cta + per_cta);
-    for (int jb = blockIdx.z * per_cta + warp; jb < jb1; jb += NB_THREADS / 32) {
+    for (int jb = blockIdx.z * per_cta + warp; jb < jb1; jb += NT / 32) {
       const int j = jb * WQB + lane;
       int prev = -1, next = -1, cur = -1;
       float w = 0.f;
+      // [blo, bhi]: rows holding #{tau < q} .. #{tau <= q} of every query of the block
+      int blo = 0, bhi = T;
+      if (qb) {
+        const int jl = min(Lq - 1, jb * WQB + WQB - 1);
+        const float tf = qb[jb * WQB], tl = qb[jl];
+        int l = 0, h = T;
+        const float key = lane == 0 ? tf : tl;   // lane 0: first query, lane 1: last query
+        if (lane < 2) {
+          while (l < h) {
+            const int m = (l + h) >> 1;
+            if (lane == 0 ? stau[m] < key : stau[m] <= key) l = m + 1; else h = m;
+          }
+        }
+        blo = __shfl_sync(0xffffffffu, l, 0);
+        bhi = __shfl_sync(0xffffffffu, l, 1);
+      }
       if (j < Lq) {
         float tq;
         if (!qb) {
@@ -341,10 +367,12 @@ __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint
           }
         } else {
           tq = qb[j];
-          int l = 0, h = T;
+          // the block's queries are sorted: its first and last lanes bracket the
+          // row range, every lane then searches inside it
+          int l = blo, h = bhi;
           while (l < h) { const int m = (l + h) >> 1; if (stau[m] < tq) l = m + 1; else h = m; }
           const int lo = l;
-          h = T;
+          h = bhi;
           while (l < h) { const int m = (l + h) >> 1; if (stau[m] <= tq) l = m + 1; else h = m; }
           const int hiq = l;
           if (hiq > lo) cur = hiq - 1;
@@ -372,7 +400,7 @@ __global__ void __launch_bounds__(NB_THREADS) interp_neighbors_kernel(const uint
   Nbr* out = tab + ((int64_t)b * ntiles + tile) * Lq;
   const int per_cta = (Lq + gridDim.z - 1) / gridDim.z;
   const int qa = blockIdx.z * per_cta, qe = min(Lq, qa + per_cta);
-  const int per_thr = (qe - qa + NB_THREADS - 1) / NB_THREADS;
+  const int per_thr = (qe - qa + NT - 1) / NT;
   const int j0 = qa + tid * per_thr, j1 = min(qe, j0 + per_thr);
   int lo = 0, hiq = 0;
   if (qb && j0 < j1) {   // binary searches for the first query of the run
@@ -1103,12 +1131,15 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
   const int ntiles = (int)cdiv(Dm, FTILE);
   uint8_t* flags = static_cast<uint8_t*>(workspace);
   Nbr* tab = reinterpret_cast<Nbr*>(flags + ws_flags_bytes(Bsz, T, ntiles));
+  // the word groups of one (row, tile) line up with the rows only when every tile is full
+  const bool vec = m_dtype == TSSM_U8 && Dm % FTILE == 0 && FTILE % 16 == 0 && FTILE / 16 <= 32 &&
+                   ((FTILE / 16) & (FTILE / 16 - 1)) == 0 && (reinterpret_cast<uintptr_t>(Mk) & 15) == 0;
+  // N <= 16 with whole 32-feature runs per tile: blocked table + chunked scan
+  const bool chunked = N <= 16 && Dm % 32 == 0 && FTILE % 32 == 0 && T * Dm < (int64_t(1) << 31) && aligned16(V);
+  const size_t nb_shm = (size_t)T * 12;
   {
     const int64_t rows = T * ntiles;   // one warp per (t, tile) row, 8 warps per block
     dim3 grid((unsigned)std::max<int64_t>(1, cdiv(rows, 8)), (unsigned)Bsz);
-    // the word groups of one (row, tile) line up with the rows only when every tile is full
-    const bool vec = m_dtype == TSSM_U8 && Dm % FTILE == 0 && FTILE % 16 == 0 && FTILE / 16 <= 32 &&
-                     ((FTILE / 16) & (FTILE / 16 - 1)) == 0 && (reinterpret_cast<uintptr_t>(Mk) & 15) == 0;
     if (vec) {
       const int64_t nwords = Bsz * T * Dm / 16;
       interp_flags_u8x16_kernel<<<(unsigned)cdiv(nwords, 256), 256, 0, st>>>(
@@ -1121,16 +1152,12 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       set_error("interp_ssm: mask dtype must be u8 or f32");
       return TSSM_ERR_INVALID;
     }
-  }
-  // N <= 16 with whole 32-feature runs per tile: blocked table + chunked scan
-  const bool chunked = N <= 16 && Dm % 32 == 0 && FTILE % 32 == 0 && T * Dm < (int64_t(1) << 31) && aligned16(V);
-  {
-    const size_t shm = (size_t)T * 12;
-    auto nk = chunked ? interp_neighbors_kernel<true> : interp_neighbors_kernel<false>;
-    if (shm > 48 * 1024 && cudaFuncSetAttribute(nk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm) != cudaSuccess)
+    auto nk = chunked ? interp_neighbors_kernel<true, NB_THREADS> : interp_neighbors_kernel<false, NB_THREADS>;
+    if (nb_shm > 48 * 1024 &&
+        cudaFuncSetAttribute(nk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nb_shm) != cudaSuccess)
       return check_launch("interp_ssm: neighbour smem");
     const int qsplit = (int)std::max<int64_t>(1, std::min<int64_t>(8, cdiv(Lq, 512)));
-    nk<<<dim3((unsigned)ntiles, (unsigned)Bsz, (unsigned)qsplit), NB_THREADS, shm, st>>>(
+    nk<<<dim3((unsigned)ntiles, (unsigned)Bsz, (unsigned)qsplit), NB_THREADS, nb_shm, st>>>(
         flags, (const float*)tau, (const float*)q, tab, (int)T, (int)Lq, (int)K, ntiles, (int)Dm);
   }
   const float* Vf = (const float*)V;
