@@ -18,7 +18,6 @@
 #include "common.cuh"
 #include "tcgen05.cuh"
 #include "tmap.cuh"
-#include <type_traits>
 
 namespace tssm {
 #ifdef TSSM_INTERP_TRACE
@@ -271,8 +270,11 @@ __device__ __forceinline__ void blocked_entry(int p, int n, int c, float w, int 
 }
 
 // Kernel 2: per (tile, b, query slice): last/next flagged index scans in shared
-// memory, then one entry per query.  Each thread walks a contiguous run of
-// sorted queries with two monotone pointers (lo = #{tau < q}, hi = #{tau <= q}).
+// memory, then the table.  Per-query form (BLOCKED = false, read by kernel 3):
+// each thread walks a contiguous run of sorted queries with two monotone
+// pointers (lo = #{tau < q}, hi = #{tau <= q}).  Blocked form (read by kernel
+// 3b): one warp per block of WQB queries, one query per lane, binary searches
+// inside the row range that the block's first and last queries bracket.
 constexpr int NB_THREADS = 256;
 template <bool BLOCKED, int NT>
 __global__ void __launch_bounds__(NT) interp_neighbors_kernel(const uint8_t* __restrict__ flags,
