@@ -130,11 +130,13 @@ def test_streaming_step_golden(cuda_ops):
     assert rel_err(h, g["h_final"]) < TOL_FP32
 
 
-@pytest.mark.parametrize("N", [3, 4, 16, 64, 128])
+@pytest.mark.parametrize("N,P", [(3, 10), (4, 10), (16, 10), (64, 10), (128, 10),
+                                 # P a multiple of the rows one CTA covers: per-thread (s, h) scalars
+                                 (64, 64), (16, 256), (128, 128), (64, 192)])
 @pytest.mark.parametrize("io", [torch.bfloat16, torch.float32])
-def test_streaming_step_random_vs_oracle(cuda_ops, N, io):
-    g = torch.Generator().manual_seed(N)
-    S, H, P = 37, 3, 10
+def test_streaming_step_random_vs_oracle(cuda_ops, N, P, io):
+    g = torch.Generator().manual_seed(N + P)
+    S, H = 37, 3
     x = torch.randn(S, H, P, generator=g).to(io)
     dt = torch.empty(S).exponential_(1.0, generator=g)
     dt[:3] = torch.tensor([1e-7, 2e-6, 1e-5])

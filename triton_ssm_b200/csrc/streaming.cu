@@ -45,7 +45,10 @@ template <> struct quad<float> {
   }
 };
 
-template <typename IO, int TPR, int RPT>
+// SAME: P is a multiple of the rows a block covers, so every row of a thread
+// (and of its block) belongs to one (s, h) pair: the decay, the input
+// coefficient and the B, C quads are computed once per thread, not per row.
+template <typename IO, int TPR, int RPT, bool SAME>
 __global__ void __launch_bounds__(256) streaming_step_kernel(
     const IO* __restrict__ x, const float* __restrict__ dt, float* __restrict__ h,
     const float* __restrict__ A_log, const IO* __restrict__ B, const IO* __restrict__ C,
@@ -63,6 +66,38 @@ __global__ void __launch_bounds__(256) streaming_step_kernel(
     ok[r] = row < rows;
     hv[r] = ok[r] ? ld_stream_f4(reinterpret_cast<const float4*>(h + row * N) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  if constexpr (SAME) {
+    const int64_t sh = row0 / P;                 // (s, h) pair of all this thread's rows
+    const int s = (int)(sh / Hh), hh = (int)(sh - (int64_t)s * Hh);
+    const float a = -expf(__ldg(A_log + hh));
+    const float xx = __ldg(dt + s) * a;
+    const float e = expf(xx);
+    const float coef = zoh_coeff(xx, e, a);
+    float bq[4], cq[4], cb[4];
+    quad<IO>::load(B + sh * N + 4 * q, bq);
+    quad<IO>::load(C + sh * N + 4 * q, cq);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) cb[k] = coef * bq[k];
+    const float* dskr = Dskip + (int64_t)hh * P;
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+      const int64_t row = row0 + (int64_t)r * RPB;
+      const float xv = ok[r] ? ldf(x + row) : 0.f;
+      float hs[4] = {hv[r].x, hv[r].y, hv[r].z, hv[r].w};
+      float part = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        hs[k] = e * hs[k] + cb[k] * xv;
+        part += cq[k] * hs[k];
+      }
+#pragma unroll
+      for (int off = TPR >> 1; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off, TPR);
+      if (ok[r]) {
+        st_stream_f4(reinterpret_cast<float4*>(h + row * N) + q, make_float4(hs[0], hs[1], hs[2], hs[3]));
+        if (q == 0) stf(y + row, part + __ldg(dskr + (row - sh * P)) * xv);
+      }
+    }
+  } else {
   // per-row scalars (indices, decay, input coefficient, x, skip) computed once per
   // row by the group's first lane and broadcast to its TPR lanes
 #pragma unroll
@@ -103,6 +138,7 @@ __global__ void __launch_bounds__(256) streaming_step_kernel(
       if (q == 0) stf(y + row, part + dsk * xv);
     }
   }
+  }
 }
 
 // Any N (and any alignment): one thread per (s,h,p) row, scalar accesses.
@@ -139,9 +175,10 @@ int launch_step(const void* x, const void* dt, void* h, const void* A_log, const
   constexpr int RPT = 4;
   constexpr int RPB = 256 / TPR;
   const int64_t blocks = cdiv(rows, RPB * RPT);
-  streaming_step_kernel<IO, TPR, RPT><<<(unsigned)blocks, 256, 0, st>>>(
-      (const IO*)x, (const float*)dt, (float*)h, (const float*)A_log, (const IO*)B, (const IO*)C,
-      (const float*)Dskip, (IO*)y, rows, Hh, P);
+  auto kern = P % (RPB * RPT) == 0 ? streaming_step_kernel<IO, TPR, RPT, true>
+                                   : streaming_step_kernel<IO, TPR, RPT, false>;
+  kern<<<(unsigned)blocks, 256, 0, st>>>((const IO*)x, (const float*)dt, (float*)h, (const float*)A_log,
+                                         (const IO*)B, (const IO*)C, (const float*)Dskip, (IO*)y, rows, Hh, P);
   return check_launch("streaming_step");
 }
 
