@@ -318,7 +318,7 @@ def run_ours_c5(args, rank, world, local):
            "global_batch": S * world, "seq_len": 1, "parallelism": "streams, %d rank(s)" % world,
            "l2": "state (%d MB) larger than the 126 MB L2" % (S * H * P * N * 4 // 2**20)}
     return _line(args, world, METRIC, world * upd / t_step, t_step, "f32", cfg,
-                 workloads.stream_bytes(S, H, P, N), "streaming_step_kernel<bf16,16,2>", "streaming_step_c5.md",
+                 workloads.stream_bytes(S, H, P, N), "streaming_step_kernel<bf16,16,4,true>", "streaming_step_c5.md",
                  clocks, extra={"steps_per_sec": 1.0 / t_step, "p50_step_ms": lat[len(lat) // 2],
                                 "p99_step_ms": lat[int(len(lat) * 0.99) - 1]})
 
