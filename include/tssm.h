@@ -331,6 +331,21 @@ int tssm_ssd_carry_fixup(const void* S_all, const void* decay_log2_all, int64_t 
                          int64_t L, int64_t H, int64_t P, int64_t N, tssm_stream_t stream);
 
 /*
+ * The same chaining for `pieces` equal in-device pieces of each sequence
+ * (the block-level carry of ssm_scan.py:53-65 and :68-98 applied to pieces
+ * rather than ranks).  Piece k of sequence b is sequence b*pieces + k of the
+ * views x [Bsz*pieces, L/pieces, H*P] ... that one tssm_multihead_ssd call
+ * scanned from zero states:
+ *   S [Bsz*pieces,H,P,N] f32, decay_log2 [Bsz*pieces,H] f32: its outputs;
+ *   C [Bsz,L,H,N] bf16, dt [Bsz,L,H] f32, A_log [H] f32: the whole sequences;
+ *   y [Bsz,L,H*P] bf16: fixed in place for pieces 1 .. pieces-1.
+ * L % pieces == 0; P = 64, N in {64, 128}.
+ */
+int tssm_ssd_carry_fixup_pieces(const void* S, const void* decay_log2, int64_t pieces, const void* C,
+                                const void* dt, const void* A_log, void* y, int64_t Bsz, int64_t L, int64_t H,
+                                int64_t P, int64_t N, tssm_stream_t stream);
+
+/*
  * Multi-head scan with the reference's own diagonal state h[b,head,p].
  * Replaces multihead_ssm_fwd_local_kernel / multihead_ssm_carry_scan_kernel /
  * multihead_ssm_output_kernel (multihead_ssm_kernel.py:19-187, with the

@@ -43,3 +43,25 @@ def test_decay_output_matches_dt_sum(cuda_ops):
                                      return_state=True, return_decay=True)
     ref = dt.sum(1) * (-torch.exp(A_log)) * 1.4426950408889634
     assert rel_err(d, ref) < 1e-5
+
+
+@pytest.mark.parametrize("Bt,L,H,N,K", [(2, 4096, 3, 64, 4), (1, 2048, 2, 128, 2), (1, 8192, 2, 64, 8)])
+def test_in_device_pieces_equal_whole_sequence(cuda_ops, Bt, L, H, N, K):
+    """Scanning each sequence as K pieces at once and chaining them with the
+    pieces fix-up gives the whole-sequence outputs, final state and decay."""
+    x, dt, A_log, B, C, D = make_inputs(Bt, L, H, 64, N, seed=L + K, dt_lo=1e-3)
+    args = [t.to(dev) for t in (x, A_log, B, C, dt, D)]
+    y1, h1, d1 = cuda_ops.multihead_ssm(*args, return_state=True, return_decay=True)
+    yk, hk, dk = cuda_ops.multihead_ssm(*args, return_state=True, return_decay=True, pieces=K)
+    cuda_ops.check_device_status()
+    assert rel_err(yk, y1) < TOL_BF16
+    assert rel_err(hk, h1) < 1e-4
+    assert rel_err(dk, d1) < 1e-5
+    ref, _ = oracle.ssd_scan_chunked(x, dt, A_log, B, C, D, chunk=128)
+    assert rel_err(yk, ref) < TOL_BF16
+
+
+def test_in_device_pieces_rejects_bad_split(cuda_ops):
+    x, dt, A_log, B, C, D = make_inputs(1, 1000, 2, 64, 64, seed=3)
+    with pytest.raises(ValueError):
+        cuda_ops.multihead_ssm(*(t.to(dev) for t in (x, A_log, B, C, dt, D)), pieces=4)

@@ -43,6 +43,7 @@ SIGNATURES = {
     "tssm_multihead_ssd": ([P] * 10 + [I64] * 5 + [I32, P], I32),
     "tssm_multihead_diag": ([P] * 7 + [I64] * 4 + [I32, I32, P], I32),
     "tssm_ssd_carry_fixup": ([P, P, I64, I64, P, P, P, P] + [I64] * 5 + [P], I32),
+    "tssm_ssd_carry_fixup_pieces": ([P, P, I64, P, P, P, P] + [I64] * 5 + [P], I32),
     "tssm_check_device_status": ([P], I32),
     "tssm_selftest_wait_timeout": ([I64, P], I32),
     "tssm_time_aware_interp": ([P] * 4 + [I64] * 3 + [I64] * 7 + [I64] * 2 + [I32, I32, P], I32),

@@ -20,23 +20,30 @@ namespace {
 constexpr int FQ = 64;   // tokens per fix-up chunk
 constexpr int FP = 64;   // head dim
 
+// Slices and sequences: slice j of sequence b has its state at S_all + j*sj +
+// b*sb (+ h*P*N) and its log2 decay at d_all + j*dj + b*db (+ h).  The slice
+// being fixed is `rank` (or, with pieces > 0, blockIdx.z + 1 of `pieces`
+// in-device pieces); its C, dt and y rows are sequence vb = b*vbs + vbo of
+// tensors [*, L, ...].
 template <int NST>
 __global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
-    const float* __restrict__ S_all, const float* __restrict__ d_all, int rank, int Bsz,
-    const __nv_bfloat16* __restrict__ C, const float* __restrict__ dt, const float* __restrict__ A_log,
-    __nv_bfloat16* __restrict__ y, int L, int H) {
+    const float* __restrict__ S_all, const float* __restrict__ d_all, int rank, int pieces, int64_t sj, int64_t sb,
+    int64_t dj, int64_t db, const __nv_bfloat16* __restrict__ C, const float* __restrict__ dt,
+    const float* __restrict__ A_log, __nv_bfloat16* __restrict__ y, int L, int H) {
   extern __shared__ __align__(16) float fsm[];
   float* carry = fsm;                   // [FP][NST + 1] (padded rows: no bank conflicts)
   float* cs = carry + FP * (NST + 1);   // [FQ][NST + 1]
   float* es = cs + FQ * (NST + 1);      // [FQ] decay factor per token
   __shared__ float s_run;
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int h = blockIdx.x, tid = threadIdx.x;
+  const int slice = pieces > 0 ? (int)blockIdx.z + 1 : rank;
+  const int64_t bo = blockIdx.y;
+  const int b = pieces > 0 ? (int)(bo * pieces + slice) : (int)bo;   // sequence of C, dt, y
   // carry entering this slice
-  const int64_t per_rank = (int64_t)Bsz * H * FP * NST;
-  const int64_t base = (((int64_t)b * H + h) * FP) * NST;
+  const int64_t base = bo * sb + (int64_t)h * FP * NST;
   for (int e = tid; e < FP * NST; e += 256) {
     float c = 0.f;
-    for (int j = 0; j < rank; ++j) c = exp2f(d_all[(int64_t)j * Bsz * H + (int64_t)b * H + h]) * c + S_all[j * per_rank + base + e];
+    for (int j = 0; j < slice; ++j) c = exp2f(d_all[(int64_t)j * dj + bo * db + h]) * c + S_all[j * sj + base + e];
     carry[(e / NST) * (NST + 1) + (e % NST)] = c;
   }
   if (tid == 0) s_run = 0.f;
@@ -109,6 +116,31 @@ __global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
 }  // namespace
 }  // namespace tssm
 
+namespace tssm {
+namespace {
+int launch_fixup(const void* S_all, const void* d_all, int rank, int pieces, int64_t sj, int64_t sb, int64_t dj,
+                 int64_t db, const void* C, const void* dt, const void* A_log, void* y, dim3 grid, int64_t L,
+                 int64_t H, int64_t N, cudaStream_t st) {
+  if (N == 64) {
+    const size_t smem = sizeof(float) * (64 * 65 + 64 * 65 + 64);
+    if (cudaFuncSetAttribute(ssd_carry_fixup_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return check_launch("ssd_carry_fixup: smem");
+    ssd_carry_fixup_kernel<64><<<grid, 256, smem, st>>>((const float*)S_all, (const float*)d_all, rank, pieces, sj,
+                                                        sb, dj, db, (const __nv_bfloat16*)C, (const float*)dt,
+                                                        (const float*)A_log, (__nv_bfloat16*)y, (int)L, (int)H);
+  } else {
+    const size_t smem = sizeof(float) * (64 * 129 + 64 * 129 + 64);
+    if (cudaFuncSetAttribute(ssd_carry_fixup_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return check_launch("ssd_carry_fixup: smem");
+    ssd_carry_fixup_kernel<128><<<grid, 256, smem, st>>>((const float*)S_all, (const float*)d_all, rank, pieces, sj,
+                                                         sb, dj, db, (const __nv_bfloat16*)C, (const float*)dt,
+                                                         (const float*)A_log, (__nv_bfloat16*)y, (int)L, (int)H);
+  }
+  return check_launch("ssd_carry_fixup");
+}
+}  // namespace
+}  // namespace tssm
+
 extern "C" int tssm_ssd_carry_fixup(const void* S_all, const void* decay_log2_all, int64_t rank, int64_t nranks,
                                     const void* C, const void* dt, const void* A_log, void* y, int64_t Bsz,
                                     int64_t L, int64_t H, int64_t P, int64_t N, tssm_stream_t stream) {
@@ -118,23 +150,22 @@ extern "C" int tssm_ssd_carry_fixup(const void* S_all, const void* decay_log2_al
   if (rank == 0 || Bsz * L * H == 0) return TSSM_OK;
   TSSM_REQUIRE(S_all && decay_log2_all && C && dt && A_log && y, "ssd_carry_fixup: null pointer");
   TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31), "ssd_carry_fixup: size out of range");
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  dim3 grid((unsigned)H, (unsigned)Bsz);
-  if (N == 64) {
-    const size_t smem = sizeof(float) * (64 * 65 + 64 * 65 + 64);
-    if (cudaFuncSetAttribute(ssd_carry_fixup_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return check_launch("ssd_carry_fixup: smem");
-    ssd_carry_fixup_kernel<64><<<grid, 256, smem, st>>>((const float*)S_all, (const float*)decay_log2_all, (int)rank,
-                                                        (int)Bsz, (const __nv_bfloat16*)C, (const float*)dt,
-                                                        (const float*)A_log, (__nv_bfloat16*)y, (int)L, (int)H);
-  } else {
-    const size_t smem = sizeof(float) * (64 * 129 + 64 * 129 + 64);
-    if (cudaFuncSetAttribute(ssd_carry_fixup_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return check_launch("ssd_carry_fixup: smem");
-    ssd_carry_fixup_kernel<128><<<grid, 256, smem, st>>>((const float*)S_all, (const float*)decay_log2_all,
-                                                         (int)rank, (int)Bsz, (const __nv_bfloat16*)C,
-                                                         (const float*)dt, (const float*)A_log,
-                                                         (__nv_bfloat16*)y, (int)L, (int)H);
-  }
-  return check_launch("ssd_carry_fixup");
+  return launch_fixup(S_all, decay_log2_all, (int)rank, 0, Bsz * H * P * N, H * P * N, Bsz * H, H, C, dt, A_log, y,
+                      dim3((unsigned)H, (unsigned)Bsz), L, H, N, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tssm_ssd_carry_fixup_pieces(const void* S, const void* decay_log2, int64_t pieces, const void* C,
+                                           const void* dt, const void* A_log, void* y, int64_t Bsz, int64_t L,
+                                           int64_t H, int64_t P, int64_t N, tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(pieces >= 1 && pieces <= 65535, "ssd_carry_fixup_pieces: pieces in [1, 65535]");
+  TSSM_REQUIRE(P == 64 && (N == 64 || N == 128), "ssd_carry_fixup_pieces: P must be 64 and N 64 or 128");
+  TSSM_REQUIRE(Bsz >= 0 && L >= 0 && H >= 0 && L % pieces == 0, "ssd_carry_fixup_pieces: L must split into pieces");
+  if (pieces == 1 || Bsz * L * H == 0) return TSSM_OK;
+  TSSM_REQUIRE(S && decay_log2 && C && dt && A_log && y, "ssd_carry_fixup_pieces: null pointer");
+  TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31), "ssd_carry_fixup_pieces: size out of range");
+  // piece k of sequence b is sequence b*pieces + k of the [Bsz*pieces, L/pieces, ...] views
+  return launch_fixup(S, decay_log2, 0, (int)pieces, H * P * N, pieces * H * P * N, H, pieces * H, C, dt, A_log, y,
+                      dim3((unsigned)H, (unsigned)Bsz, (unsigned)(pieces - 1)), L / pieces, H, N,
+                      reinterpret_cast<cudaStream_t>(stream));
 }

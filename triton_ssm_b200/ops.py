@@ -353,7 +353,7 @@ def streaming_interp_then_ssm(ring_V, ring_M, ring_tau, ring_head, v_new, m_new,
 
 
 def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h0=None,
-                  return_state=False, y=None, return_decay=False):
+                  return_state=False, y=None, return_decay=False, pieces=1):
     """Multi-head chunked scan (``multihead_ssm_kernel.py:19-187``).
 
     mode="diag": the reference's own diagonal state h[b,h,p]
@@ -368,8 +368,16 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
       whole-sequence decay per (b, h), [Bt,H] f32.  P = 64, N in {64, 128}.
     ``BLK_L`` is accepted for signature compatibility (the kernel's chunk is
     64 tokens; results do not depend on it beyond rounding).
+    ``pieces`` (mode "ssd", no h0, L a multiple of 64*pieces): each sequence
+    is scanned as that many equal pieces at once, each from a zero state, and
+    the pieces are chained by ``tssm_ssd_carry_fixup_pieces`` (the bf16
+    outputs of a piece's leading tokens are rounded twice).  For few long
+    sequences this spreads the work over more SMs.
     """
     del BLK_L
+    if pieces != 1:
+        return _multihead_ssd_pieces(u, A_log, B, C, dt, D, int(pieces), bdisc, h0, return_state, y,
+                                     return_decay)
     if bdisc not in _BDISC:
         raise ValueError("multihead_ssm: bdisc must be 'euler' or 'zoh'")
     if mode == "diag":
@@ -408,6 +416,38 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
         out.append(hl)
     if return_decay:
         out.append(dl)
+    return out[0] if len(out) == 1 else tuple(out)
+
+
+def _multihead_ssd_pieces(u, A_log, B, C, dt, D, K, bdisc, h0, return_state, y, return_decay):
+    if K < 1 or h0 is not None:
+        raise ValueError("multihead_ssm: pieces must be >= 1 and h0 None when pieces > 1")
+    _cuda(u, A_log, B, C, dt, D)
+    Bt, L, HP = u.shape
+    if B.dim() != 4 or L % (64 * K):
+        raise ValueError("multihead_ssm: L must be a multiple of 64*pieces")
+    H, N = B.shape[2], B.shape[3]
+    P = HP // H
+    u, B, C = (t.contiguous() for t in (u, B, C))
+    dt = dt.float().contiguous()
+    A_log = A_log.float().contiguous()
+    if y is None:
+        y = torch.empty_like(u)
+    Lp = L // K
+    _, S, d = multihead_ssm(u.view(Bt * K, Lp, HP), A_log, B.view(Bt * K, Lp, H, N), C.view(Bt * K, Lp, H, N),
+                            dt.view(Bt * K, Lp, H), D, bdisc=bdisc, y=y.view(Bt * K, Lp, HP),
+                            return_state=True, return_decay=True)
+    call("tssm_ssd_carry_fixup_pieces", ptr(S), ptr(d), K, ptr(C), ptr(dt), ptr(A_log), ptr(y), Bt, L, H, P,
+         N, stream_of(y))
+    out = [y]
+    if return_state:   # the pieces' states chained in order, as the fix-up chains them
+        Sv, dv = S.view(Bt, K, H, P, N), d.view(Bt, K, H)
+        hl = Sv[:, 0].clone()
+        for k in range(1, K):
+            hl = torch.exp2(dv[:, k])[..., None, None] * hl + Sv[:, k]
+        out.append(hl)
+    if return_decay:
+        out.append(d.view(Bt, K, H).sum(1))
     return out[0] if len(out) == 1 else tuple(out)
 
 

@@ -10,6 +10,8 @@
   before it with ``ssd_carry_fixup``.  The arithmetic is the reference's
   block carry scan (ssm_scan.py:53-98) lifted from blocks to slices.
 """
+import math
+
 import torch
 import torch.distributed as dist
 
@@ -35,6 +37,23 @@ def _all_gather_packed(S, d, group):
     return S_all, d_all
 
 
+def ssd_local_pieces(Bt, H, L, sms):
+    """In-device pieces per sequence for a long slice: the power of two up to 8
+    whose Bt*H*pieces CTAs (one per SM at a time) fill the last wave best,
+    keeping pieces of at least 16384 tokens so that the carry fix-up (which
+    stops once the decay underflows, typically within a few thousand tokens)
+    stays a small fraction of the work."""
+    best, best_eff = 1, 0.0
+    for K in (1, 2, 4, 8):
+        if L % (64 * K) or (K > 1 and L // K < 16384):
+            continue
+        n = Bt * H * K
+        eff = n / (math.ceil(n / sms) * sms)
+        if eff > best_eff + 1e-9:
+            best, best_eff = K, eff
+    return best
+
+
 def ssd_sequence_parallel(x, dt, A_log, B, C, D, group=None, bdisc="euler", y=None,
                           local_scan=None, fixup=None):
     """Multi-head scan of a sequence sharded over the ranks of `group`.
@@ -53,8 +72,10 @@ def ssd_sequence_parallel(x, dt, A_log, B, C, D, group=None, bdisc="euler", y=No
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     if local_scan is None:
         def local_scan(x, dt, A_log, B, C, D):
+            sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+            K = ssd_local_pieces(x.shape[0], B.shape[2], x.shape[1], sms)
             return ops.multihead_ssm(x, A_log, B, C, dt, D, bdisc=bdisc, y=y, return_state=True,
-                                     return_decay=True)
+                                     return_decay=True, pieces=K)
     if fixup is None:
         fixup = ops.ssd_carry_fixup
     yl, S, d = local_scan(x, dt, A_log, B, C, D)
