@@ -40,37 +40,81 @@ __device__ __forceinline__ void zoh_one(float a, float dtv, float bc, float& aba
   bbar = em1 / (a + 1e-12f) * bc;
 }
 
+// CTA = (ZR consecutive (b, t) rows, 256*W channels): each thread owns W
+// channels (W = 4: one 128-bit / 64-bit vector) and walks the CTA's rows, so
+// the per-channel a = -exp(A_log) is computed once per thread and (b, t) is
+// stepped rather than divided out.
+constexpr int ZR = 8;
+
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(256) zoh_discretize_kernel(
     const float* __restrict__ A_log, const T* __restrict__ B, const float* __restrict__ dt,
     T* __restrict__ Abar, T* __restrict__ Bbar, int64_t Bsz, int64_t Tn, int64_t H,
     int64_t sBb, int64_t sBt, int64_t sdb, int64_t sdt, int64_t sab, int64_t sat,
     int64_t sbb, int64_t sbt) {
-  const int64_t hv = VEC ? (H >> 2) : H;
-  const int64_t items = Bsz * Tn * hv;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < items; i += stride) {
-    const int64_t row = i / hv;
-    const int64_t hi = i - row * hv;
-    const int64_t b = row / Tn;
-    const int64_t t = row - b * Tn;
-    const float dtv = __ldg(dt + b * sdb + t * sdt);
-    if constexpr (VEC) {
-      const int64_t h0 = hi << 2;
-      const float4 al = __ldg(reinterpret_cast<const float4*>(A_log + h0));
-      const float alv[4] = {al.x, al.y, al.z, al.w};
-      float bc[4], ab[4], bb[4];
-      vec4<T>::unpack(*reinterpret_cast<const typename vec4<T>::type*>(B + b * sBb + t * sBt + h0), bc);
+  constexpr int W = VEC ? 4 : 1;
+  const int64_t h0 = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * W;
+  const int64_t rows = Bsz * Tn;
+  const int64_t r0 = (int64_t)blockIdx.x * ZR;
+  if (h0 >= H || r0 >= rows) return;
+  float a[W];
+  if constexpr (VEC) {
+    const float4 al = __ldg(reinterpret_cast<const float4*>(A_log + h0));
+    a[0] = -expf(al.x); a[1] = -expf(al.y); a[2] = -expf(al.z); a[3] = -expf(al.w);
+  } else {
+    a[0] = -expf(__ldg(A_log + h0));
+  }
+  const int64_t b0 = r0 / Tn, t0 = r0 - b0 * Tn;
+  const int nr = (int)min((int64_t)ZR, rows - r0);
+  // every row's loads go out first (ZR of them in flight per thread), then the math and stores
+  int64_t bs[ZR], ts[ZR];
+  {
+    int64_t b = b0, t = t0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) zoh_one<T>(-expf(alv[k]), dtv, bc[k], ab[k], bb[k]);
-      *reinterpret_cast<typename vec4<T>::type*>(Abar + b * sab + t * sat + h0) = vec4<T>::pack(ab);
-      *reinterpret_cast<typename vec4<T>::type*>(Bbar + b * sbb + t * sbt + h0) = vec4<T>::pack(bb);
-    } else {
-      const float a = -expf(__ldg(A_log + hi));
-      float ab, bb;
-      zoh_one<T>(a, dtv, ldf(B + b * sBb + t * sBt + hi), ab, bb);
-      stf(Abar + b * sab + t * sat + hi, ab);
-      stf(Bbar + b * sbb + t * sbt + hi, bb);
+    for (int r = 0; r < ZR; ++r) {
+      bs[r] = b;
+      ts[r] = t;
+      if (++t == Tn) { t = 0; ++b; }
+    }
+  }
+  if constexpr (VEC) {
+    typename vec4<T>::type bv[ZR];
+    float dtv[ZR];
+#pragma unroll
+    for (int r = 0; r < ZR; ++r) {
+      if (r < nr) {
+        bv[r] = *reinterpret_cast<const typename vec4<T>::type*>(B + bs[r] * sBb + ts[r] * sBt + h0);
+        dtv[r] = __ldg(dt + bs[r] * sdb + ts[r] * sdt);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < ZR; ++r) {
+      if (r < nr) {
+        float bc[4], ab[4], bb[4];
+        vec4<T>::unpack(bv[r], bc);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) zoh_one<T>(a[k], dtv[r], bc[k], ab[k], bb[k]);
+        *reinterpret_cast<typename vec4<T>::type*>(Abar + bs[r] * sab + ts[r] * sat + h0) = vec4<T>::pack(ab);
+        *reinterpret_cast<typename vec4<T>::type*>(Bbar + bs[r] * sbb + ts[r] * sbt + h0) = vec4<T>::pack(bb);
+      }
+    }
+  } else {
+    float bv[ZR], dtv[ZR];
+#pragma unroll
+    for (int r = 0; r < ZR; ++r) {
+      if (r < nr) {
+        bv[r] = ldf(B + bs[r] * sBb + ts[r] * sBt + h0);
+        dtv[r] = __ldg(dt + bs[r] * sdb + ts[r] * sdt);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < ZR; ++r) {
+      if (r < nr) {
+        float ab, bb;
+        zoh_one<T>(a[0], dtv[r], bv[r], ab, bb);
+        stf(Abar + bs[r] * sab + ts[r] * sat + h0, ab);
+        stf(Bbar + bs[r] * sbb + ts[r] * sbt + h0, bb);
+      }
     }
   }
 }
@@ -83,16 +127,16 @@ int launch(const float* A_log, const T* B, const float* dt, T* Abar, T* Bbar, in
   auto al = [&](const void* p) { return (reinterpret_cast<uintptr_t>(p) % vbytes) == 0; };
   const bool vec = (H % 4 == 0) && sBb % 4 == 0 && sBt % 4 == 0 && sab % 4 == 0 && sat % 4 == 0 &&
                    sbb % 4 == 0 && sbt % 4 == 0 && al(B) && al(Abar) && al(Bbar) && aligned16(A_log);
-  const int64_t items = Bsz * Tn * (vec ? H / 4 : H);
-  if (items == 0) return TSSM_OK;
-  const int threads = 256;
-  const int64_t blocks = std::min<int64_t>(cdiv(items, threads), (int64_t)kNumSMs * 16);
+  if (Bsz * Tn * H == 0) return TSSM_OK;
+  const int64_t gcol = cdiv(vec ? H / 4 : H, 256), grow = cdiv(Bsz * Tn, ZR);
+  TSSM_REQUIRE(gcol <= 65535 && grow <= 0x7fffffff, "zoh_discretize: size exceeds the grid");
+  const dim3 grid((unsigned)grow, (unsigned)gcol);
   if (vec)
-    zoh_discretize_kernel<T, true><<<(unsigned)blocks, threads, 0, st>>>(
-        A_log, B, dt, Abar, Bbar, Bsz, Tn, H, sBb, sBt, sdb, sdt, sab, sat, sbb, sbt);
+    zoh_discretize_kernel<T, true><<<grid, 256, 0, st>>>(A_log, B, dt, Abar, Bbar, Bsz, Tn, H, sBb, sBt, sdb, sdt,
+                                                        sab, sat, sbb, sbt);
   else
-    zoh_discretize_kernel<T, false><<<(unsigned)blocks, threads, 0, st>>>(
-        A_log, B, dt, Abar, Bbar, Bsz, Tn, H, sBb, sBt, sdb, sdt, sab, sat, sbb, sbt);
+    zoh_discretize_kernel<T, false><<<grid, 256, 0, st>>>(A_log, B, dt, Abar, Bbar, Bsz, Tn, H, sBb, sBt, sdb, sdt,
+                                                         sab, sat, sbb, sbt);
   return check_launch("zoh_discretize");
 }
 
