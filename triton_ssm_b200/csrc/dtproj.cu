@@ -67,12 +67,15 @@ __global__ void __launch_bounds__(DTP_THREADS) dt_project_kernel(
       }
     }
   }
-  float bs[4], a[4];
+  // per channel: bias, a = -exp(A_log) and 1 / (a + 1e-12) (the reference divides by
+  // a + 1e-12 for every element; one reciprocal per channel differs by at most an ulp)
+  float bs[4], a[4], ra[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int64_t hh = h0 + hc + k;
     bs[k] = hh < H ? bias[hh] : 0.f;
     a[k] = (DISC && hh < H) ? -expf(A_log[hh]) : -1.f;
+    ra[k] = 1.0f / (a[k] + 1e-12f);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -98,7 +101,7 @@ __global__ void __launch_bounds__(DTP_THREADS) dt_project_kernel(
         const float x = dtv[k] * a[k];
         const float e = expf(x);
         ab[k] = e;
-        bb[k] = expm1_guard_f32(x, e) / (a[k] + 1e-12f) * bin[k];
+        bb[k] = expm1_guard_f32(x, e) * ra[k] * bin[k];
       }
     }
     if (VEC) {
