@@ -59,7 +59,9 @@ def test_ssm_forward_golden(cuda_ops):
         assert rel_err(h, g["h"]) < TOL_FP32, name
 
 
-@pytest.mark.parametrize("shape", [(3, 1000, 70), (1, 1, 1), (2, 4097, 33), (4, 1024, 1024)])
+@pytest.mark.parametrize("shape", [(3, 1000, 70), (1, 1, 1), (2, 4097, 33), (4, 1024, 1024),
+                                   # H % 32 == 0 (f32): rows streamed through shared memory; partial last segment
+                                   (2, 1000, 64), (1, 300, 32), (3, 513, 96)])
 def test_ssm_forward_random_vs_oracle(cuda_ops, shape):
     g = torch.Generator().manual_seed(sum(shape))
     Bt, L, H = shape
