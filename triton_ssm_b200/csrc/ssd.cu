@@ -22,13 +22,16 @@
 //   warp 15     decay: streams dt (cp.async) and writes each chunk's decay prefix
 //               sums and input coefficients into a DSL-slot ring of its own, so it
 //               runs several chunks ahead of the consumers;
-//   warps 13,14 MMA2 | MMA4 + MMA3 issuers (one thread each).  Issuing a tcgen05.mma
-//               costs the issuing thread tens of cycles, so the issue work is spread
-//               over three threads and each MMA goes out as soon as its inputs are ready;
-//   warps 4-7   mask group: G -> M (bf16) for chunk c;
+//   warp 13     MMA4 and MMA2 issue from one non-blocking event loop (MMA4 waits only
+//               for diag(w) B of chunk c and for the state group to have read S of
+//               chunk c-2);
+//   warp 14     MMA3 issue.  Issuing a tcgen05.mma costs the issuing thread tens of
+//               cycles, so the issue work is spread over three threads and each MMA
+//               goes out as soon as its inputs are ready;
+//   warps 4-7   mask group: G -> M (bf16) and diag(w) B (MMA4's A operand) for chunk c;
 //   warps 0-3   state group: H <- exp(s_last) H + S in registers and the bf16 copy
-//               of H for the next MMA3 -- the only serial dependence between chunks --
-//               then diag(w) B for chunk c+2 (MMA4's A operand);
+//               of H for the next MMA3 -- the only serial dependence between chunks,
+//               kept free of every other job;
 //   warps 8-11  output group: y = Y1 + exp(s_i) Y2 + D x into a swizzled tile, one
 //               TMA store per chunk.
 // G, Y1, Y2 and S are double-buffered in TMEM (8 x 64 = 512 columns), M, diag(w) B,
@@ -85,6 +88,11 @@ constexpr uint32_t BAR_STATE = 1, BAR_MSK = 2, BAR_OUT = 3;
 template <int NST>
 struct Layout {
   static constexpr int NB = NST / 64;                  // 64-wide blocks of B and C along n
+  // Who writes diag(w) B (MMA4's A operand).  N=64: the state group, two chunks ahead
+  // (the 6-stage ring holds that B tile long before), which keeps the mask group's
+  // per-chunk work short.  N=128: the mask group for the chunk it masks, because with
+  // 3 stages the B tile two chunks ahead is not loaded yet when the state group runs.
+  static constexpr bool BHAT_IN_STATE = NST == 64;
   static constexpr int STAGE_BYTES = TILE * (1 + 2 * NB);
   static constexpr int STAGES = NST == 64 ? 6 : 3;     // X, B, C ring
   static constexpr int DSL = NST == 64 ? 8 : 4;        // decay-data ring
@@ -140,17 +148,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   float* dsk = reinterpret_cast<float*>(smem + LY::OFF_DSK);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
   uint64_t* full = bars;               // [ST]  TMA bytes of X, B, C landed
-  uint64_t* empty = full + ST;         // [ST]  stage released (output group + state group)
+  uint64_t* empty = full + ST;         // [ST]  stage released (output group + MMA4 complete)
   uint64_t* dfull = empty + ST;        // [DSL] decay data written
   uint64_t* dempty = dfull + DSL;      // [DSL] decay slot released (state + output groups)
   uint64_t* gfull = dempty + DSL;      // [2]   MMA1 done
   uint64_t* gfree = gfull + 2;         // [2]   G read by the mask group
-  uint64_t* bready = gfull + 4;        // [2]   diag(w) B written
-  uint64_t* mready = gfull + 6;        // [2]   M written
+  uint64_t* bready = gfull + 4;        // [2]   diag(w) B written (state group, BHAT_IN_STATE)
+  uint64_t* mready = gfull + 6;        // [2]   M (and, unless BHAT_IN_STATE, diag(w) B) written
   uint64_t* sfull = gfull + 8;         // [2]   MMA4 done
   uint64_t* y1full = gfull + 10;       // [2]   MMA2 done
   uint64_t* y2full = gfull + 12;       // [2]   MMA3 done
-  // gfull + 14, + 15: spare
+  uint64_t* sfree = gfull + 14;        // [2]   S read by the state group
   uint64_t* yfree = gfull + 16;        // [2]   Y1, Y2 read by the output group
   uint64_t* hready = gfull + 18;       // [2]   bf16 state tile for MMA3 written
   uint64_t* drain = gfull + 20;        // [3]   final commit of each MMA issuer
@@ -347,52 +355,74 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     asm volatile("cp.async.wait_all;" ::: "memory");   // no copy may outlive the loop
     if (decay_log2 && lane == 0 && !*abort_flag) decay_log2[(int64_t)b * H + h] = total_log2;
   } else if (warp == 13) {
-    // ================================================================ MMA2 issuer
+    // ================================================================ MMA4 + MMA2 issuer
+    // Two independent issue streams in one non-blocking event loop, so neither waits
+    // behind the other:
+    //   MMA4 (S^T = (diag(w) B)^T X) once diag(w) B of chunk k4 is written and the state
+    //        group has read S of chunk k4-2 out of TMEM buffer k4&1;
+    //   MMA2 (Y1 = M X) once M of chunk k2 is written and the output group has read
+    //        Y1 of chunk k2-2.
+    // A commit covers every earlier MMA of this thread, so each barrier below is reached
+    // no earlier than the MMA it names completes.
     if (lane == 0) {
+      constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
-      for (int k = 0; k < nchunks; ++k) {
-        const int s = k % ST, kb = k & 1;
-        if (!mbar_wait_n(abort_flag, &mready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1,
-                         &full[s], (k / ST) & 1)) {
-          if (!*abort_flag) fail(1015);
-          break;
+      int k4 = 0, k2 = 0;
+      uint64_t t_prog = globaltimer_ns();
+      while (k4 < nchunks || k2 < nchunks) {
+        bool prog = false;
+        if (k4 < nchunks) {
+          const int s = k4 % ST, kb = k4 & 1;
+          if (mbar_test(LY::BHAT_IN_STATE ? &bready[kb] : &mready[kb], (k4 >> 1) & 1) &&
+              (k4 < 2 || mbar_test(&sfree[kb], ((k4 - 2) >> 1) & 1)) && mbar_test(&full[s], (k4 / ST) & 1)) {
+            tc_fence_after();
+            SSD_TRACE(k4, 8);
+            const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
+            const uint64_t dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
+            umma_bf16_x4(tmem + col_s(kb), dBh, dBh + 128, dBh + 256, dBh + 384, dX, dX + 128, dX + 256, dX + 384,
+                         ID_MM, 0);
+            umma_commit(&sfull[kb]);
+            umma_commit(&empty[s]);   // MMA4 is the last reader of X apart from the output group
+            SSD_TRACE(k4, 9);
+            ++k4;
+            prog = true;
+          }
         }
-        tc_fence_after();
-        SSD_TRACE(k, 10);
-        const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
-        const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
-        umma_bf16_x4(tmem + col_y1(kb), dM, dM + 2, dM + 4, dM + 6, dX, dX + 128, dX + 256, dX + 384, ID_KM, 0);
-        umma_commit(&y1full[kb]);
-        SSD_TRACE(k, 11);
-        SSD_TRACE_DONE(&y1full[kb], (k >> 1) & 1, k, 22);
+        if (k2 < nchunks) {
+          const int s = k2 % ST, kb = k2 & 1;
+          if (mbar_test(&mready[kb], (k2 >> 1) & 1) && (k2 < 2 || mbar_test(&yfree[kb], ((k2 - 2) >> 1) & 1)) &&
+              mbar_test(&full[s], (k2 / ST) & 1)) {
+            tc_fence_after();
+            SSD_TRACE(k2, 10);
+            const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
+            const uint64_t dM = make_desc_sw128(smem_u32(mt_ptr(kb)), 16);
+            umma_bf16_x4(tmem + col_y1(kb), dM, dM + 2, dM + 4, dM + 6, dX, dX + 128, dX + 256, dX + 384, ID_KM, 0);
+            umma_commit(&y1full[kb]);
+            SSD_TRACE(k2, 11);
+            ++k2;
+            prog = true;
+          }
+        }
+        if (prog) {
+          t_prog = globaltimer_ns();
+        } else {
+          if (*abort_flag) break;
+          if (globaltimer_ns() - t_prog > 2000000000ull) {
+            fail(1004);
+            break;
+          }
+        }
       }
       drain_mmas(&drain[1]);
     }
   } else if (warp == 14) {
-    // ================================================================ MMA4 + MMA3 issuer
+    // ================================================================ MMA3 issuer
     if (lane == 0) {
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
-      constexpr uint32_t ID_MM = make_idesc_bf16(NST, 64, true, true);
       for (int k = 0; k < nchunks; ++k) {
         const int s = k % ST, kb = k & 1;
-        // MMA4 (S^T = diag(w)B^T X).  bready(k) also means S of chunk k-2 was consumed
-        // (the state group writes diag(w) B of chunk k after reading it).
-        if (!mbar_wait_n(abort_flag, &bready[kb], (k >> 1) & 1, &full[s], (k / ST) & 1)) {
-          if (!*abort_flag) fail(1004);
-          break;
-        }
-        tc_fence_after();
-        SSD_TRACE(k, 8);
-        {
-          const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
-          const uint64_t dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
-          umma_bf16_x4(tmem + col_s(kb), dBh, dBh + 128, dBh + 256, dBh + 384, dX, dX + 128, dX + 256, dX + 384, ID_MM,
-                       0);
-        }
-        umma_commit(&sfull[kb]);
-        SSD_TRACE(k, 9);
-        SSD_TRACE_DONE(&sfull[kb], (k >> 1) & 1, k, 21);
-        // MMA3 (Y2 = C H^T) once the state tile of chunk k-1 is written
+        // Y2 = C H^T once the state tile of chunk k-1 is written and the output group has
+        // read Y2 of chunk k-2
         if (!mbar_wait_n(abort_flag, &hready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1,
                          &full[s], (k / ST) & 1)) {
           if (!*abort_flag) fail(1006);
@@ -411,7 +441,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         }
         umma_commit(&y2full[kb]);
         SSD_TRACE(k, 13);
-        SSD_TRACE_DONE(&y2full[kb], (k >> 1) & 1, k, 23);
       }
       drain_mmas(&drain[2]);
     }
@@ -425,8 +454,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     for (int c = 0; c < nchunks; ++c) {
       const int kb = c & 1, ds = c % DSL;
       // G of chunk c, its decay data, and mask buffer c&1 free (MMA2 of chunk c-2 done)
+      // G of chunk c, its decay data and B tile, mask buffer c&1 free (MMA2 of chunk c-2 done)
+      // and, unless BHAT_IN_STATE, diag(w) B buffer c&1 free (MMA4 of chunk c-2 done)
       const bool bad = !mbar_wait_n(abort_flag, &gfull[kb], (c >> 1) & 1, &dfull[ds], (c / DSL) & 1,
-                                    c >= 2 ? &y1full[kb] : nullptr, ((c - 2) >> 1) & 1);
+                                    c >= 2 ? &y1full[kb] : nullptr, ((c - 2) >> 1) & 1, &full[c % ST],
+                                    (c / ST) & 1) ||
+                       (!LY::BHAT_IN_STATE && c >= 2 && !mbar_wait(&sfull[kb], ((c - 2) >> 1) & 1, abort_flag));
       if (bad && !*abort_flag) fail(1007);
       if (named_bar_or(BAR_MSK, 128, bad)) break;
       const float* sm = small_ptr(ds);
@@ -436,6 +469,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       //     M_ij = G_ij * exp2(s_i - s_ref(J)) * v_j for j <= i (J = 4-token sub-block of j)
       float g[32];
       tmem_ld16x2_32(tmem + lane_base + col_g(kb), g);
+      // diag(w) B of chunk c (MMA4's A operand), w_j = exp2(s_last - s_j) beta_j, while G loads
+      if (!LY::BHAT_IN_STATE) {
+        const float* wv = sm + 144;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+          const uint8_t* Bt = stage_ptr(c % ST) + TILE * (1 + nb);
+          uint8_t* Bh = bh_ptr(kb) + TILE * nb;
+          uint4 v[4];
+#pragma unroll
+          for (int it = 0; it < 4; ++it) v[it] = *reinterpret_cast<const uint4*>(Bt + (t + it * 128) * 16);
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int idx = t + it * 128;   // 16-byte chunk; row (token) = idx / 8
+            const __nv_bfloat162 w2 = __float2bfloat162_rn(wv[idx >> 3]);
+            __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v[it]);
+            hv[0] = __hmul2(hv[0], w2);
+            hv[1] = __hmul2(hv[1], w2);
+            hv[2] = __hmul2(hv[2], w2);
+            hv[3] = __hmul2(hv[3], w2);
+            *reinterpret_cast<uint4*>(Bh + idx * 16) = v[it];
+          }
+        }
+      }
       {
         const float si = sm[row + (row >= 32 ? 4 : 0)];
         const float4* vv = reinterpret_cast<const float4*>(sm + 72 + half * 36);
@@ -561,57 +617,56 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         *reinterpret_cast<uint4*>(Hs + sw128_chunk(n_own, p0 / 8 + q)) = o;
       }
     };
-    // diag(w) B of chunk j (MMA4's A operand) into buffer j&1 (its B tile and decay data have landed)
+    // diag(w) B of chunk j (MMA4's A operand) into buffer j&1 (BHAT_IN_STATE only; its B
+    // tile and decay data have landed, and MMA4 of chunk j-2 is complete)
     auto bhat_rows = [&](int j) {
       const int sj = j % ST, dj = j % DSL;
       const float* wv = small_ptr(dj) + 144;
+      const uint8_t* Bt = stage_ptr(sj) + TILE;
+      uint8_t* Bh = bh_ptr(j & 1);
+      uint4 v[4];
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        const uint8_t* Bt = stage_ptr(sj) + TILE * (1 + nb);
-        uint8_t* Bh = bh_ptr(j & 1) + TILE * nb;
-        uint4 v[4];
+      for (int it = 0; it < 4; ++it) v[it] = *reinterpret_cast<const uint4*>(Bt + (tid + it * 128) * 16);
 #pragma unroll
-        for (int it = 0; it < 4; ++it) v[it] = *reinterpret_cast<const uint4*>(Bt + (tid + it * 128) * 16);
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-          const int idx = tid + it * 128;          // 16-byte chunk; row (token) = idx / 8
-          const __nv_bfloat162 w2 = __float2bfloat162_rn(wv[idx >> 3]);
-          __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v[it]);
-          hv[0] = __hmul2(hv[0], w2);
-          hv[1] = __hmul2(hv[1], w2);
-          hv[2] = __hmul2(hv[2], w2);
-          hv[3] = __hmul2(hv[3], w2);
-          *reinterpret_cast<uint4*>(Bh + idx * 16) = v[it];
-        }
+      for (int it = 0; it < 4; ++it) {
+        const int idx = tid + it * 128;   // 16-byte chunk; row (token) = idx / 8
+        const __nv_bfloat162 w2 = __float2bfloat162_rn(wv[idx >> 3]);
+        __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v[it]);
+        hv[0] = __hmul2(hv[0], w2);
+        hv[1] = __hmul2(hv[1], w2);
+        hv[2] = __hmul2(hv[2], w2);
+        hv[3] = __hmul2(hv[3], w2);
+        *reinterpret_cast<uint4*>(Bh + idx * 16) = v[it];
       }
-    };
-    auto write_bhat = [&](int j) -> bool {   // standalone (first two chunks); false if a wait gave up
-      const bool bad = !mbar_wait_n(abort_flag, &full[j % ST], (j / ST) & 1, &dfull[j % DSL], (j / DSL) & 1);
-      if (bad && !*abort_flag) fail(1017);
-      if (named_bar_or(BAR_STATE, 128, bad)) return false;
-      bhat_rows(j);
-      fence_proxy_async_smem();
-      named_bar_sync(BAR_STATE, 128);
-      if (tid == 0) {
-        SSD_TRACE(j, 5);
-        mbar_arrive(&bready[j & 1]);
-      }
-      return true;
     };
     write_hs(hs_ptr(0));
+    bool ok = true;
+    if (LY::BHAT_IN_STATE) {   // diag(w) B of the first two chunks
+      for (int j = 0; j < 2 && j < nchunks; ++j) {
+        const bool bad = !mbar_wait_n(abort_flag, &full[j % ST], (j / ST) & 1, &dfull[j % DSL], (j / DSL) & 1);
+        if (bad && !*abort_flag) fail(1017);
+        if (named_bar_or(BAR_STATE, 128, bad)) {
+          ok = false;
+          break;
+        }
+        bhat_rows(j);
+        fence_proxy_async_smem();
+        named_bar_sync(BAR_STATE, 128);
+        if (tid == 0) mbar_arrive(&bready[j & 1]);
+      }
+    }
     fence_proxy_async_smem();
     named_bar_sync(BAR_STATE, 128);
     if (tid == 0) mbar_arrive(&hready[0]);
-    bool ok = true;
-    for (int j = 0; j < 2 && j < nchunks && ok; ++j) ok = write_bhat(j);
     for (int c = 0; c < nchunks && ok; ++c) {
       const int kb = c & 1, ds = c % DSL;
-      const bool nxt = c + 2 < nchunks;   // diag(w) B of chunk c+2 is written in this iteration
+      const bool nxt = LY::BHAT_IN_STATE && c + 2 < nchunks;   // diag(w) B of chunk c+2 written here
       const int jd = nxt ? c + 2 : c;
-      // S of chunk c (MMA4 is committed after MMA3 of chunk c-1 by the same thread, so state
-      // tile (c+1)&1 is no longer read either); decay data up to chunk jd (the decay warp
-      // publishes in order); the B tile of chunk c+2
+      // S of chunk c; decay data up to chunk jd (the decay warp publishes in order); MMA3 of
+      // chunk c-1 complete (it read state tile (c+1)&1, which this iteration overwrites);
+      // with BHAT_IN_STATE the B tile of chunk c+2
       const bool bad = !mbar_wait_n(abort_flag, &sfull[kb], (c >> 1) & 1, &dfull[jd % DSL], (jd / DSL) & 1,
+                                    c >= 1 ? &y2full[(c - 1) & 1] : nullptr, ((c - 1) >> 1) & 1,
                                     nxt ? &full[(c + 2) % ST] : nullptr, ((c + 2) / ST) & 1);
       if (bad && !*abort_flag) fail(1008);
       if (named_bar_or(BAR_STATE, 128, bad)) {
@@ -645,7 +700,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         for (int j = 0; j < 32; ++j) hreg[32 + j] = e_last * hreg[32 + j] + sv[j];
       }
       write_hs(hs_ptr((c + 1) & 1));
-      // S of chunk c is consumed, so buffer c&1 may take diag(w) B of chunk c+2
+      // S of chunk c is read, so MMA4 of chunk c is complete and buffer c&1 may take
+      // diag(w) B of chunk c+2
       if (nxt) bhat_rows(c + 2);
       fence_proxy_async_smem();
       tc_fence_before();
@@ -653,8 +709,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       if (tid == 0) {
         SSD_TRACE(c, 15);
         mbar_arrive(&hready[(c + 1) & 1]);
+        mbar_arrive(&sfree[kb]);
         mbar_arrive(&dempty[ds]);
-        mbar_arrive(&empty[c % ST]);   // MMA4 of chunk c (which read X) is complete
         if (nxt) mbar_arrive(&bready[kb]);
       }
     }
