@@ -52,17 +52,7 @@ __device__ unsigned long long g_ssd_trace[64 * 32];
   do {                                                                               \
     if (blockIdx.x == 0 && blockIdx.y == 0 && (chunk) < 64) g_ssd_trace[(chunk) * 32 + (ev)] = clock64(); \
   } while (0)
-// Debug only: spin (bounded) until the barrier phase completes, then stamp it.
-#define SSD_TRACE_DONE(bar, par, chunk, ev)                                          \
-  do {                                                                               \
-    for (int _i = 0; _i < (1 << 22) && !mbar_test((bar), (par)); ++_i) {            \
-    }                                                                                \
-    SSD_TRACE(chunk, ev);                                                            \
-  } while (0)
 #else
-#define SSD_TRACE_DONE(bar, par, chunk, ev) \
-  do {                                      \
-  } while (0)
 #define SSD_TRACE(chunk, ev) \
   do {                       \
   } while (0)
@@ -153,15 +143,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   uint64_t* dempty = dfull + DSL;      // [DSL] decay slot released (state + output groups)
   uint64_t* gfull = dempty + DSL;      // [2]   MMA1 done
   uint64_t* gfree = gfull + 2;         // [2]   G read by the mask group
-  uint64_t* bready = gfull + 4;        // [2]   diag(w) B written (state group, BHAT_IN_STATE)
-  uint64_t* mready = gfull + 6;        // [2]   M (and, unless BHAT_IN_STATE, diag(w) B) written
+  uint64_t* bready = gfull + 4;        // [2]   diag(w) B written (state or mask group, see BHAT_IN_STATE)
+  uint64_t* mready = gfull + 6;        // [2]   M written
   uint64_t* sfull = gfull + 8;         // [2]   MMA4 done
   uint64_t* y1full = gfull + 10;       // [2]   MMA2 done
   uint64_t* y2full = gfull + 12;       // [2]   MMA3 done
   uint64_t* sfree = gfull + 14;        // [2]   S read by the state group
   uint64_t* yfree = gfull + 16;        // [2]   Y1, Y2 read by the output group
   uint64_t* hready = gfull + 18;       // [2]   bf16 state tile for MMA3 written
-  uint64_t* drain = gfull + 20;        // [3]   final commit of each MMA issuer
+  uint64_t* drain = gfull + 20;        // [3]   final commit of each MMA issuer (1: warp 13, 2: warp 14)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_MISC + 4);
   int* issued = reinterpret_cast<int*>(smem + LY::OFF_MISC + 8);
@@ -209,64 +199,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
   };
 
   if (warp == 12) {
-    // ================================================================ producer + MMA1
+    // ================================================================ producer
+    // Only TMA loads, so a released stage is refilled as soon as it frees up.
     if (lane == 0) {
       prefetch_tmap(&tm_x);
       prefetch_tmap(&tm_b);
       prefetch_tmap(&tm_c);
       prefetch_tmap(&tm_y);
-      constexpr uint32_t ID_KK = make_idesc_bf16(64, 64, false, false);
       int pc = 0;   // next chunk to load
-      int mc = 0;   // next chunk whose MMA1 (G = C B^T) is issued
-      uint64_t t_prog = globaltimer_ns();
-      while (mc < nchunks) {
-        bool prog = false;
-        if (pc < nchunks && (pc < ST || mbar_test(&empty[pc % ST], ((pc / ST) - 1) & 1))) {
-          const int s = pc % ST;
-          SSD_TRACE(pc, 0);
-          uint8_t* st = stage_ptr(s);
-          mbar_arrive_expect_tx(&full[s], LY::STAGE_BYTES);
-          tma_load_3d(st, &tm_x, h * P, pc * Q, b, &full[s]);
-#pragma unroll
-          for (int nb = 0; nb < NB; ++nb) {
-            tma_load_3d(st + TILE * (1 + nb), &tm_b, h * NST + nb * 64, pc * Q, b, &full[s]);
-            tma_load_3d(st + TILE * (1 + NB + nb), &tm_c, h * NST + nb * 64, pc * Q, b, &full[s]);
-          }
-          ++pc;
-          prog = true;
+      for (; pc < nchunks; ++pc) {
+        const int s = pc % ST;
+        if (pc >= ST && !mbar_wait(&empty[s], ((pc / ST) - 1) & 1, abort_flag)) {
+          if (!*abort_flag) fail(1001);
+          break;
         }
-        if (mc < pc && mbar_test(&full[mc % ST], (mc / ST) & 1) &&
-            (mc < 2 || mbar_test(&gfree[mc & 1], ((mc - 2) >> 1) & 1))) {
-          const int s = mc % ST, kb = mc & 1;
-          tc_fence_after();
-          SSD_TRACE(mc, 2);
-          const uint32_t X = smem_u32(stage_ptr(s));
-          const uint64_t dB = make_desc_sw128(X + TILE, 16), dC = make_desc_sw128(X + TILE * (1 + NB), 16);
+        SSD_TRACE(pc, 0);
+        uint8_t* st = stage_ptr(s);
+        mbar_arrive_expect_tx(&full[s], LY::STAGE_BYTES);
+        tma_load_3d(st, &tm_x, h * P, pc * Q, b, &full[s]);
 #pragma unroll
-          for (int kb4 = 0; kb4 < NST / 64; ++kb4) {   // 64-wide K blocks (tiles) of n
-            const uint64_t ko = (uint64_t)(kb4 * TILE) >> 4;
-            umma_bf16_x4(tmem + col_g(kb), dC + ko, dC + ko + 2, dC + ko + 4, dC + ko + 6, dB + ko, dB + ko + 2,
-                         dB + ko + 4, dB + ko + 6, ID_KK, kb4 > 0);
-          }
-          umma_commit(&gfull[kb]);
-          SSD_TRACE(mc, 3);
-          SSD_TRACE_DONE(&gfull[kb], (mc >> 1) & 1, mc, 20);
-          ++mc;
-          prog = true;
-        }
-        if (prog) {
-          t_prog = globaltimer_ns();
-        } else {
-          if (*abort_flag) break;
-          if (globaltimer_ns() - t_prog > 2000000000ull) {
-            fail(1001);
-            break;
-          }
-          __nanosleep(32);
+        for (int nb = 0; nb < NB; ++nb) {
+          tma_load_3d(st + TILE * (1 + nb), &tm_b, h * NST + nb * 64, pc * Q, b, &full[s]);
+          tma_load_3d(st + TILE * (1 + NB + nb), &tm_c, h * NST + nb * 64, pc * Q, b, &full[s]);
         }
       }
       *issued = pc;
-      drain_mmas(&drain[0]);
     }
   } else if (warp == 15) {
     // ================================================================ decay warp
@@ -355,13 +312,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     asm volatile("cp.async.wait_all;" ::: "memory");   // no copy may outlive the loop
     if (decay_log2 && lane == 0 && !*abort_flag) decay_log2[(int64_t)b * H + h] = total_log2;
   } else if (warp == 13) {
-    // ================================================================ MMA4 + MMA2 issuer
+    // ================================================================ MMA2 + MMA4 issuer
     // Two independent issue streams in one non-blocking event loop, so neither waits
-    // behind the other:
-    //   MMA4 (S^T = (diag(w) B)^T X) once diag(w) B of chunk k4 is written and the state
-    //        group has read S of chunk k4-2 out of TMEM buffer k4&1;
+    // behind the other (MMA2, on the way to the output, goes first when both are ready):
     //   MMA2 (Y1 = M X) once M of chunk k2 is written and the output group has read
-    //        Y1 of chunk k2-2.
+    //        Y1 of chunk k2-2;
+    //   MMA4 (S^T = (diag(w) B)^T X) once diag(w) B of chunk k4 is written and the state
+    //        group has read S of chunk k4-2 out of TMEM buffer k4&1.
     // A commit covers every earlier MMA of this thread, so each barrier below is reached
     // no earlier than the MMA it names completes.
     if (lane == 0) {
@@ -371,23 +328,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       uint64_t t_prog = globaltimer_ns();
       while (k4 < nchunks || k2 < nchunks) {
         bool prog = false;
-        if (k4 < nchunks) {
-          const int s = k4 % ST, kb = k4 & 1;
-          if (mbar_test(LY::BHAT_IN_STATE ? &bready[kb] : &mready[kb], (k4 >> 1) & 1) &&
-              (k4 < 2 || mbar_test(&sfree[kb], ((k4 - 2) >> 1) & 1)) && mbar_test(&full[s], (k4 / ST) & 1)) {
-            tc_fence_after();
-            SSD_TRACE(k4, 8);
-            const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
-            const uint64_t dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
-            umma_bf16_x4(tmem + col_s(kb), dBh, dBh + 128, dBh + 256, dBh + 384, dX, dX + 128, dX + 256, dX + 384,
-                         ID_MM, 0);
-            umma_commit(&sfull[kb]);
-            umma_commit(&empty[s]);   // MMA4 is the last reader of X apart from the output group
-            SSD_TRACE(k4, 9);
-            ++k4;
-            prog = true;
-          }
-        }
         if (k2 < nchunks) {
           const int s = k2 % ST, kb = k2 & 1;
           if (mbar_test(&mready[kb], (k2 >> 1) & 1) && (k2 < 2 || mbar_test(&yfree[kb], ((k2 - 2) >> 1) & 1)) &&
@@ -400,6 +340,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
             umma_commit(&y1full[kb]);
             SSD_TRACE(k2, 11);
             ++k2;
+            prog = true;
+          }
+        }
+        if (k4 < nchunks) {
+          const int s = k4 % ST, kb = k4 & 1;
+          if (mbar_test(&bready[kb], (k4 >> 1) & 1) &&
+              (k4 < 2 || mbar_test(&sfree[kb], ((k4 - 2) >> 1) & 1)) && mbar_test(&full[s], (k4 / ST) & 1)) {
+            tc_fence_after();
+            SSD_TRACE(k4, 8);
+            const uint64_t dX = make_desc_sw128(smem_u32(stage_ptr(s)), TILE);
+            const uint64_t dBh = make_desc_sw128(smem_u32(bh_ptr(kb)), TILE);
+            umma_bf16_x4(tmem + col_s(kb), dBh, dBh + 128, dBh + 256, dBh + 384, dX, dX + 128, dX + 256, dX + 384,
+                         ID_MM, 0);
+            umma_commit(&sfull[kb]);
+            umma_commit(&empty[s]);   // MMA4 is the last reader of X apart from the output group
+            SSD_TRACE(k4, 9);
+            ++k4;
             prog = true;
           }
         }
@@ -416,31 +373,66 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       drain_mmas(&drain[1]);
     }
   } else if (warp == 14) {
-    // ================================================================ MMA3 issuer
+    // ================================================================ MMA1 + MMA3 issuer
+    //   MMA1 (G = C B^T) once the tiles of chunk k1 have landed and the mask group has
+    //        read G of chunk k1-2;
+    //   MMA3 (Y2 = C H^T) once the state tile of chunk k3-1 is written and the output
+    //        group has read Y2 of chunk k3-2.
     if (lane == 0) {
+      constexpr uint32_t ID_KK = make_idesc_bf16(64, 64, false, false);
       constexpr uint32_t ID_KM = make_idesc_bf16(64, 64, false, true);
-      for (int k = 0; k < nchunks; ++k) {
-        const int s = k % ST, kb = k & 1;
-        // Y2 = C H^T once the state tile of chunk k-1 is written and the output group has
-        // read Y2 of chunk k-2
-        if (!mbar_wait_n(abort_flag, &hready[kb], (k >> 1) & 1, k >= 2 ? &yfree[kb] : nullptr, ((k - 2) >> 1) & 1,
-                         &full[s], (k / ST) & 1)) {
-          if (!*abort_flag) fail(1006);
-          break;
-        }
-        tc_fence_after();
-        SSD_TRACE(k, 12);
-        const uint64_t dC = make_desc_sw128(smem_u32(stage_ptr(s)) + TILE * (1 + NB), 16);
-        const uint64_t dH = make_desc_sw128(smem_u32(hs_ptr(kb)), TILE);
+      int k1 = 0, k3 = 0;
+      uint64_t t_prog = globaltimer_ns();
+      while (k1 < nchunks || k3 < nchunks) {
+        bool prog = false;
+        if (k1 < nchunks && mbar_test(&full[k1 % ST], (k1 / ST) & 1) &&
+            (k1 < 2 || mbar_test(&gfree[k1 & 1], ((k1 - 2) >> 1) & 1))) {
+          const int s = k1 % ST, kb = k1 & 1;
+          tc_fence_after();
+          SSD_TRACE(k1, 2);
+          const uint32_t X = smem_u32(stage_ptr(s));
+          const uint64_t dB = make_desc_sw128(X + TILE, 16), dC = make_desc_sw128(X + TILE * (1 + NB), 16);
 #pragma unroll
-        for (int kb4 = 0; kb4 < NST / 64; ++kb4) {   // 64-wide K blocks of n: C tiles; 16 state rows per step
-          const uint64_t ko = (uint64_t)(kb4 * TILE) >> 4;
-          const uint64_t ho = 512 * kb4;
-          umma_bf16_x4(tmem + col_y2(kb), dC + ko, dC + ko + 2, dC + ko + 4, dC + ko + 6, dH + ho, dH + ho + 128,
-                       dH + ho + 256, dH + ho + 384, ID_KM, kb4 > 0);
+          for (int kb4 = 0; kb4 < NST / 64; ++kb4) {   // 64-wide K blocks (tiles) of n
+            const uint64_t ko = (uint64_t)(kb4 * TILE) >> 4;
+            umma_bf16_x4(tmem + col_g(kb), dC + ko, dC + ko + 2, dC + ko + 4, dC + ko + 6, dB + ko, dB + ko + 2,
+                         dB + ko + 4, dB + ko + 6, ID_KK, kb4 > 0);
+          }
+          umma_commit(&gfull[kb]);
+          SSD_TRACE(k1, 3);
+          ++k1;
+          prog = true;
         }
-        umma_commit(&y2full[kb]);
-        SSD_TRACE(k, 13);
+        if (k3 < nchunks) {
+          const int s = k3 % ST, kb = k3 & 1;
+          if (mbar_test(&hready[kb], (k3 >> 1) & 1) && (k3 < 2 || mbar_test(&yfree[kb], ((k3 - 2) >> 1) & 1)) &&
+              mbar_test(&full[s], (k3 / ST) & 1)) {
+            tc_fence_after();
+            SSD_TRACE(k3, 12);
+            const uint64_t dC = make_desc_sw128(smem_u32(stage_ptr(s)) + TILE * (1 + NB), 16);
+            const uint64_t dH = make_desc_sw128(smem_u32(hs_ptr(kb)), TILE);
+#pragma unroll
+            for (int kb4 = 0; kb4 < NST / 64; ++kb4) {   // 64-wide K blocks of n: C tiles; 16 state rows per step
+              const uint64_t ko = (uint64_t)(kb4 * TILE) >> 4;
+              const uint64_t ho = 512 * kb4;
+              umma_bf16_x4(tmem + col_y2(kb), dC + ko, dC + ko + 2, dC + ko + 4, dC + ko + 6, dH + ho,
+                           dH + ho + 128, dH + ho + 256, dH + ho + 384, ID_KM, kb4 > 0);
+            }
+            umma_commit(&y2full[kb]);
+            SSD_TRACE(k3, 13);
+            ++k3;
+            prog = true;
+          }
+        }
+        if (prog) {
+          t_prog = globaltimer_ns();
+        } else {
+          if (*abort_flag) break;
+          if (globaltimer_ns() - t_prog > 2000000000ull) {
+            fail(1006);
+            break;
+          }
+        }
       }
       drain_mmas(&drain[2]);
     }
@@ -453,7 +445,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
     const uint32_t lane_base = (uint32_t)(w * 32) << 16;
     for (int c = 0; c < nchunks; ++c) {
       const int kb = c & 1, ds = c % DSL;
-      // G of chunk c, its decay data, and mask buffer c&1 free (MMA2 of chunk c-2 done)
       // G of chunk c, its decay data and B tile, mask buffer c&1 free (MMA2 of chunk c-2 done)
       // and, unless BHAT_IN_STATE, diag(w) B buffer c&1 free (MMA4 of chunk c-2 done)
       const bool bad = !mbar_wait_n(abort_flag, &gfull[kb], (c >> 1) & 1, &dfull[ds], (c / DSL) & 1,
@@ -469,29 +460,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
       //     M_ij = G_ij * exp2(s_i - s_ref(J)) * v_j for j <= i (J = 4-token sub-block of j)
       float g[32];
       tmem_ld16x2_32(tmem + lane_base + col_g(kb), g);
-      // diag(w) B of chunk c (MMA4's A operand), w_j = exp2(s_last - s_j) beta_j, while G loads
-      if (!LY::BHAT_IN_STATE) {
-        const float* wv = sm + 144;
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-          const uint8_t* Bt = stage_ptr(c % ST) + TILE * (1 + nb);
-          uint8_t* Bh = bh_ptr(kb) + TILE * nb;
-          uint4 v[4];
-#pragma unroll
-          for (int it = 0; it < 4; ++it) v[it] = *reinterpret_cast<const uint4*>(Bt + (t + it * 128) * 16);
-#pragma unroll
-          for (int it = 0; it < 4; ++it) {
-            const int idx = t + it * 128;   // 16-byte chunk; row (token) = idx / 8
-            const __nv_bfloat162 w2 = __float2bfloat162_rn(wv[idx >> 3]);
-            __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v[it]);
-            hv[0] = __hmul2(hv[0], w2);
-            hv[1] = __hmul2(hv[1], w2);
-            hv[2] = __hmul2(hv[2], w2);
-            hv[3] = __hmul2(hv[3], w2);
-            *reinterpret_cast<uint4*>(Bh + idx * 16) = v[it];
-          }
-        }
-      }
       {
         const float si = sm[row + (row >= 32 ? 4 : 0)];
         const float4* vv = reinterpret_cast<const float4*>(sm + 72 + half * 36);
@@ -526,6 +494,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) ssd_chunk_scan_kernel(
         SSD_TRACE(c, 7);
         mbar_arrive(&gfree[kb]);
         mbar_arrive(&mready[kb]);
+      }
+      // then diag(w) B of chunk c (MMA4's A operand), w_j = exp2(s_last - s_j) beta_j
+      if (!LY::BHAT_IN_STATE) {
+        const float* wv = sm + 144;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+          const uint8_t* Bt = stage_ptr(c % ST) + TILE * (1 + nb);
+          uint8_t* Bh = bh_ptr(kb) + TILE * nb;
+          uint4 v[4];
+#pragma unroll
+          for (int it = 0; it < 4; ++it) v[it] = *reinterpret_cast<const uint4*>(Bt + (t + it * 128) * 16);
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int idx = t + it * 128;   // 16-byte chunk; row (token) = idx / 8
+            const __nv_bfloat162 w2 = __float2bfloat162_rn(wv[idx >> 3]);
+            __nv_bfloat162* hv = reinterpret_cast<__nv_bfloat162*>(&v[it]);
+            hv[0] = __hmul2(hv[0], w2);
+            hv[1] = __hmul2(hv[1], w2);
+            hv[2] = __hmul2(hv[2], w2);
+            hv[3] = __hmul2(hv[3], w2);
+            *reinterpret_cast<uint4*>(Bh + idx * 16) = v[it];
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(BAR_MSK, 128);
+        if (t == 0) mbar_arrive(&bready[kb]);
       }
     }
   } else if (warp >= 8) {
