@@ -495,7 +495,8 @@ def run_ours_c4(args, rank, world, local):
            "global_batch": Bt, "seq_len": L, "parallelism": "sequence (L) x %d" % world,
            "nvlink_bytes_per_rank": Bt * H * P * N * 4 + Bt * H * 4}
     out = _line(args, world, METRIC, upd / t_step, t_step, "bf16", cfg, alg // world,
-                "ssd_chunk_scan_kernel<128,false> + ssd_carry_fixup_kernel<128>", None, clocks,
+                "ssd_chunk_scan_kernel<128,false> + ssd_carry_fixup_kernel<128>",
+                "ssd_chunk_scan_c4.md" if world == 1 and L == c["L"] else None, clocks,
                 launches=(2 if world > 1 else 1) * args.steps)
     out["scaling"] = "strong"
     out["roofline"]["note"] = "algorithmic bytes per rank (1/world of the whole sequence)"
