@@ -348,7 +348,7 @@ def run_ours_c1(args, rank, world, local):
             Ab, Bb = ts.zoh_discretize(Al, B_exp, dt)
             ts.ssm_forward(u_exp, Ab, Bb, C_exp, Dz)
         alg = 151019520
-        kern = "zoh_discretize_kernel + ssm_forward_kernel"
+        kern = "zoh_discretize_kernel + ssm_forward_tma_kernel"
         launches = 2 * args.steps
     elif args.c1_mode == "pool":
         # the pair with the mean-pooled logit head fused into the scan's epilogue

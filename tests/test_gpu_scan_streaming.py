@@ -60,8 +60,9 @@ def test_ssm_forward_golden(cuda_ops):
 
 
 @pytest.mark.parametrize("shape", [(3, 1000, 70), (1, 1, 1), (2, 4097, 33), (4, 1024, 1024),
-                                   # H % 32 == 0 (f32): rows streamed through shared memory; partial last segment
-                                   (2, 1000, 64), (1, 300, 32), (3, 513, 96)])
+                                   # 16-byte row pitch (TMA-staged kernel): partial last 128-step tile,
+                                   # a partial last 32-channel tile (H=36), a single step
+                                   (2, 1000, 64), (1, 300, 32), (3, 513, 96), (2, 300, 36), (1, 1, 32)])
 def test_ssm_forward_random_vs_oracle(cuda_ops, shape):
     g = torch.Generator().manual_seed(sum(shape))
     Bt, L, H = shape

@@ -9,7 +9,17 @@
 // and (3) replays its steps from that exclusive prefix, writing h and y.  All
 // inputs are read from HBM once; there are no intermediate buffers and no
 // inter-CTA communication.
+//
+// When the rows are TMA-addressable (16-byte aligned bases and row pitch), the
+// same scan runs with its inputs staged by TMA (ssm_forward_tma_kernel): a
+// producer warp keeps a ring of 128-step x 32-channel tiles of A, u, B and C in
+// flight while 16 compute warps scan the previous tile out of shared memory,
+// so the HBM latency is hidden instead of being paid once per super-segment.
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
+#include "tcgen05.cuh"
+#include "tmap.cuh"
 
 namespace tssm {
 namespace {
@@ -286,6 +296,207 @@ int dispatch_diag(const void* u, const void* A_log, const void* B, const void* C
   return launch_diag<T, 4>(u, A_log, B, C, dt, D, y, Bsz, L, nh, hd, zoh, st);
 }
 
+
+// ---------------------------------------------------------------- TMA-staged ssm_forward
+constexpr int FT_CH = 128;            // steps per staged tile
+constexpr int FT_NW = 16;             // compute warps
+constexpr int FT_S = FT_CH / FT_NW;   // steps per compute warp and tile
+constexpr uint32_t FT_BAR = 1;        // named barrier of the compute warps
+
+template <typename T>
+struct FtLayout {
+  static constexpr int STAGES = sizeof(T) == 4 ? 3 : 6;
+  static constexpr int TILE = FT_CH * 32 * (int)sizeof(T);   // one array's [FT_CH][32] tile
+  static constexpr int STAGE = 4 * TILE;                      // A, u, B, C
+  static constexpr int OFF_AGG = STAGES * STAGE;              // [2][2][FT_NW][32] f32 aggregates
+  static constexpr int OFF_BAR = OFF_AGG + 2 * 2 * FT_NW * 32 * 4;
+  static constexpr int OFF_MISC = OFF_BAR + 2 * STAGES * 8;   // abort flag, issued, consumed
+  static constexpr int BYTES = OFF_MISC + 16 + 128;           // + slack to align the base to 128
+  static_assert(BYTES <= 232448, "ssm_forward_tma shared-memory layout exceeds the per-CTA limit");
+};
+
+// CTA = (32 channels, one batch row); warp FT_NW is the TMA producer.  Tiles are
+// [FT_CH steps][32 channels] boxes of the [Bsz][L][H] tensors; steps past L and
+// channels past H read as zero from the tensor map and are masked here.
+template <typename T>
+__global__ void __launch_bounds__((FT_NW + 1) * 32, 1) ssm_forward_tma_kernel(
+    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmU,
+    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
+    const T* __restrict__ D, T* __restrict__ y, T* __restrict__ h, int L, int H, int* __restrict__ status) {
+  using LY = FtLayout<T>;
+  constexpr int ST = LY::STAGES;
+  extern __shared__ uint8_t ft_raw[];
+  uint8_t* smem = ft_raw + ((128u - (sm100::smem_u32(ft_raw) & 127u)) & 127u);
+  float* agg = reinterpret_cast<float*>(smem + LY::OFF_AGG);   // [buf][a|x][warp][lane]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
+  uint64_t* empty = full + ST;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_MISC);
+  int* issued = reinterpret_cast<int*>(smem + LY::OFF_MISC + 4);
+  int* consumed = reinterpret_cast<int*>(smem + LY::OFF_MISC + 8);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ch0 = blockIdx.x * 32, b = blockIdx.y;
+  const int nt = (L + FT_CH - 1) / FT_CH;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], FT_NW);
+    }
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == FT_NW) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      sm100::prefetch_tmap(&tmA);
+      sm100::prefetch_tmap(&tmU);
+      sm100::prefetch_tmap(&tmB);
+      sm100::prefetch_tmap(&tmC);
+      int k = 0;
+      for (; k < nt; ++k) {
+        const int s = k % ST;
+        if (k >= ST && !sm100::mbar_wait(&empty[s], ((k / ST) - 1) & 1, abort_flag)) {
+          if (!*abort_flag) {
+            *abort_flag = 1;
+            atomicExch(status, 2001);
+          }
+          break;
+        }
+        uint8_t* st = smem + s * LY::STAGE;
+        sm100::mbar_arrive_expect_tx(&full[s], LY::STAGE);
+        sm100::tma_load_3d(st, &tmA, ch0, k * FT_CH, b, &full[s]);
+        sm100::tma_load_3d(st + LY::TILE, &tmU, ch0, k * FT_CH, b, &full[s]);
+        sm100::tma_load_3d(st + 2 * LY::TILE, &tmB, ch0, k * FT_CH, b, &full[s]);
+        sm100::tma_load_3d(st + 3 * LY::TILE, &tmC, ch0, k * FT_CH, b, &full[s]);
+      }
+      *issued = k;
+    }
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int ch = ch0 + lane;
+    const bool valid = ch < H;
+    const float dv = valid ? ldf(D + ch) : 0.f;
+    const int64_t base = (int64_t)b * L * H + ch;
+    float carry = 0.f;
+    int k = 0;
+    for (; k < nt; ++k) {
+      const int s = k % ST, pb = k & 1;
+      const bool bad = !sm100::mbar_wait(&full[s], (k / ST) & 1, abort_flag);
+      const T* tA = reinterpret_cast<const T*>(smem + s * LY::STAGE);
+      const T* tU = tA + FT_CH * 32;
+      const T* tB = tU + FT_CH * 32;
+      const T* tC = tB + FT_CH * 32;
+      const int r0 = warp * FT_S;            // this warp's rows of the tile
+      const int t0 = k * FT_CH + r0;         // and their first step
+      float a[FT_S], bu[FT_S], uu[FT_S];
+      float ag_a = 1.f, ag_x = 0.f;
+      if (!bad) {
+#pragma unroll
+        for (int i = 0; i < FT_S; ++i) {
+          const int r = (r0 + i) * 32 + lane;
+          if (valid && t0 + i < L) {
+            a[i] = ldf(tA + r);
+            uu[i] = ldf(tU + r);
+            bu[i] = ldf(tB + r) * uu[i];
+          } else {
+            a[i] = 1.f;
+            bu[i] = 0.f;
+            uu[i] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < FT_S; ++i) {
+          ag_x = a[i] * ag_x + bu[i];
+          ag_a *= a[i];
+        }
+        agg[((pb * 2 + 0) * FT_NW + warp) * 32 + lane] = ag_a;
+        agg[((pb * 2 + 1) * FT_NW + warp) * 32 + lane] = ag_x;
+      } else if (!*abort_flag) {
+        *abort_flag = 1;
+        atomicExch(status, 2002);
+      }
+      // one barrier per tile: the aggregates are double-buffered by tile parity, and a
+      // warp writes buffer pb again only after every warp has passed tile k+1's barrier
+      if (sm100::named_bar_or(FT_BAR, FT_NW * 32, bad)) break;
+      // exclusive prefix for this warp and the carry into the next tile, folded in
+      // registers from all warps' aggregates (loaded at once)
+      float wa[FT_NW], wx[FT_NW];
+#pragma unroll
+      for (int w = 0; w < FT_NW; ++w) {
+        wa[w] = agg[((pb * 2 + 0) * FT_NW + w) * 32 + lane];
+        wx[w] = agg[((pb * 2 + 1) * FT_NW + w) * 32 + lane];
+      }
+      float hs = carry, nxt = carry;
+#pragma unroll
+      for (int w = 0; w < FT_NW; ++w) {
+        if (w == warp) hs = nxt;
+        nxt = wa[w] * nxt + wx[w];
+      }
+      carry = nxt;
+#pragma unroll
+      for (int i = 0; i < FT_S; ++i) {
+        hs = a[i] * hs + bu[i];
+        const int t = t0 + i;
+        if (valid && t < L) {
+          const int64_t off = base + (int64_t)t * H;
+          if (h) stf(h + off, hs);
+          stf(y + off, ldf(tC + (r0 + i) * 32 + lane) * hs + dv * uu[i]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty[s]);   // this warp is done with stage s
+    }
+    if (threadIdx.x == 0) *consumed = k;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    // loads issued but never consumed must land before the CTA exits
+    for (int c = *consumed; c < *issued; ++c) sm100::mbar_wait(&full[c % ST], (c / ST) & 1, nullptr, 100000000ull);
+  }
+}
+
+// 3-D map over [Bsz][L][H] (H contiguous), box {32 channels, FT_CH steps, 1}, no swizzle.
+inline bool ft_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, int64_t Bsz, int64_t L,
+                   int64_t H) {
+  auto fn = tmap_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)H, (cuuint64_t)L, (cuuint64_t)Bsz};
+  cuuint64_t strides[2] = {(cuuint64_t)(H * esize), (cuuint64_t)(L * H * esize)};
+  cuuint32_t box[3] = {32, FT_CH, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Launches the TMA-staged scan when the tensors are TMA-addressable; returns
+// TSSM_ERR_UNSUPPORTED (nothing launched) otherwise, so the caller falls back.
+template <typename T>
+int launch_ssm_forward_tma(const void* u, const void* A, const void* B, const void* C, const void* D, void* y,
+                           void* h, int64_t Bsz, int64_t L, int64_t H, cudaStream_t st) {
+  constexpr int es = (int)sizeof(T);
+  if (!aligned16(u) || !aligned16(A) || !aligned16(B) || !aligned16(C) || (H * es) % 16 != 0 ||
+      L >= (int64_t(1) << 31) || H >= (int64_t(1) << 31))
+    return TSSM_ERR_UNSUPPORTED;
+  const CUtensorMapDataType dt = es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap mA, mU, mB, mC;
+  if (!ft_map(&mA, A, dt, es, Bsz, L, H) || !ft_map(&mU, u, dt, es, Bsz, L, H) || !ft_map(&mB, B, dt, es, Bsz, L, H) ||
+      !ft_map(&mC, C, dt, es, Bsz, L, H))
+    return TSSM_ERR_UNSUPPORTED;
+  int* status = device_status_ptr();
+  if (!status) return TSSM_ERR_UNSUPPORTED;
+  constexpr int bytes = FtLayout<T>::BYTES;
+  auto kern = ssm_forward_tma_kernel<T>;
+  // The dynamic shared-memory opt-in is per device; it is cheap, so set it on every launch.
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return check_launch("ssm_forward_tma: set smem attribute");
+  dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
+  kern<<<grid, (FT_NW + 1) * 32, bytes, st>>>(mA, mU, mB, mC, (const T*)D, (T*)y, (T*)h, (int)L, (int)H, status);
+  return check_launch("ssm_forward_tma");
+}
 }  // namespace
 }  // namespace tssm
 
@@ -307,6 +518,11 @@ int ssm_forward_impl(const void* u, const void* A, const void* B, const void* C,
   // loads in flight (measured: +18 us against +6 us at config-1 size).
   const bool pool = pool_out != nullptr;
   const int nthr = pool ? 32 * 32 : NW * 32;
+  if (!pool && (dtype == TSSM_F32 || dtype == TSSM_BF16)) {
+    const int r = dtype == TSSM_F32 ? launch_ssm_forward_tma<float>(u, A, B, C, D, y, h, Bsz, L, H, st)
+                                    : launch_ssm_forward_tma<__nv_bfloat16>(u, A, B, C, D, y, h, Bsz, L, H, st);
+    if (r != TSSM_ERR_UNSUPPORTED) return r;   // launched (or failed): otherwise the register-staged kernel
+  }
   if (dtype == TSSM_F32) {
     auto kern = pool ? ssm_forward_kernel<float, 8, 32, true> : ssm_forward_kernel<float, S, NW, false>;
     kern<<<grid, nthr, 0, st>>>((const float*)u, (const float*)A, (const float*)B, (const float*)C,
