@@ -51,8 +51,9 @@ def test_ssm_forward_fused_pool(cuda_ops, dty, Bt, L, H):
     ins = [cu(t.to(dty)) for t in (u, A, B, C, D)]
     y, h, logits = cuda_ops.ssm_forward(*ins, pool=(cu(W), cu(bias)))
     y2, h2 = cuda_ops.ssm_forward(*ins)
-    # the pooled variant splits the sequence into shorter per-warp runs, so the
-    # scan's float association (not its math) differs from the plain kernel
+    # where rows are not TMA-addressable (H=5) the pooled variant splits the sequence
+    # into shorter per-warp runs, so the scan's float association (not its math)
+    # differs from the plain kernel there
     tol = 1e-5 if dty == torch.float32 else 1e-2
     assert rel_err(y.float(), y2.float()) < tol and rel_err(h.float(), h2.float()) < tol
     ref = oracle.mean_pool_logit(y.float().cpu(), W, bias)     # pooling what the output holds

@@ -311,18 +311,21 @@ struct FtLayout {
   static constexpr int OFF_AGG = STAGES * STAGE;              // [2][2][FT_NW][32] f32 aggregates
   static constexpr int OFF_BAR = OFF_AGG + 2 * 2 * FT_NW * 32 * 4;
   static constexpr int OFF_MISC = OFF_BAR + 2 * STAGES * 8;   // abort flag, issued, consumed
-  static constexpr int BYTES = OFF_MISC + 16 + 128;           // + slack to align the base to 128
+  static constexpr int OFF_POOL = OFF_MISC + 16;              // [FT_NW] per-warp pooled sums
+  static constexpr int BYTES = OFF_POOL + FT_NW * 4 + 128;    // + slack to align the base to 128
   static_assert(BYTES <= 232448, "ssm_forward_tma shared-memory layout exceeds the per-CTA limit");
 };
 
 // CTA = (32 channels, one batch row); warp FT_NW is the TMA producer.  Tiles are
 // [FT_CH steps][32 channels] boxes of the [Bsz][L][H] tensors; steps past L and
-// channels past H read as zero from the tensor map and are masked here.
-template <typename T>
+// channels past H read as zero from the tensor map and are masked here.  POOL adds
+// the fused mean-pooled logit head, as in ssm_forward_kernel.
+template <typename T, bool POOL>
 __global__ void __launch_bounds__((FT_NW + 1) * 32, 1) ssm_forward_tma_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmU,
     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
-    const T* __restrict__ D, T* __restrict__ y, T* __restrict__ h, int L, int H, int* __restrict__ status) {
+    const T* __restrict__ D, T* __restrict__ y, T* __restrict__ h, int L, int H, const float* __restrict__ poolW,
+    const float* __restrict__ pool_bias, float* __restrict__ pool_out, float pool_inv, int* __restrict__ status) {
   using LY = FtLayout<T>;
   constexpr int ST = LY::STAGES;
   extern __shared__ uint8_t ft_raw[];
@@ -379,6 +382,8 @@ __global__ void __launch_bounds__((FT_NW + 1) * 32, 1) ssm_forward_tma_kernel(
     const int ch = ch0 + lane;
     const bool valid = ch < H;
     const float dv = valid ? ldf(D + ch) : 0.f;
+    const float pw = (POOL && valid) ? poolW[ch] : 0.f;
+    float pacc = 0.f;
     const int64_t base = (int64_t)b * L * H + ch;
     float carry = 0.f;
     int k = 0;
@@ -443,13 +448,27 @@ __global__ void __launch_bounds__((FT_NW + 1) * 32, 1) ssm_forward_tma_kernel(
         if (valid && t < L) {
           const int64_t off = base + (int64_t)t * H;
           if (h) stf(h + off, hs);
-          stf(y + off, ldf(tC + (r0 + i) * 32 + lane) * hs + dv * uu[i]);
+          const float yv = ldf(tC + (r0 + i) * 32 + lane) * hs + dv * uu[i];
+          stf(y + off, yv);
+          if (POOL) pacc += pw * io_round<T>(yv);
         }
       }
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&empty[s]);   // this warp is done with stage s
     }
     if (threadIdx.x == 0) *consumed = k;
+    if (POOL && k == nt) {   // every tile scanned (k < nt only after an abort, uniformly)
+      float* spool = reinterpret_cast<float*>(smem + LY::OFF_POOL);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) pacc += __shfl_xor_sync(0xffffffffu, pacc, o);
+      if (lane == 0) spool[warp] = pacc;
+      sm100::named_bar_sync(FT_BAR, FT_NW * 32);
+      if (threadIdx.x == 0) {
+        float s2 = 0.f;
+        for (int w = 0; w < FT_NW; ++w) s2 += spool[w];
+        atomicAdd(pool_out + b, s2 * pool_inv + (blockIdx.x == 0 ? pool_bias[0] : 0.f));
+      }
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) {
@@ -476,7 +495,8 @@ inline bool ft_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int
 // TSSM_ERR_UNSUPPORTED (nothing launched) otherwise, so the caller falls back.
 template <typename T>
 int launch_ssm_forward_tma(const void* u, const void* A, const void* B, const void* C, const void* D, void* y,
-                           void* h, int64_t Bsz, int64_t L, int64_t H, cudaStream_t st) {
+                           void* h, const void* poolW, const void* pool_bias, void* pool_out, float pool_inv,
+                           int64_t Bsz, int64_t L, int64_t H, cudaStream_t st) {
   constexpr int es = (int)sizeof(T);
   if (!aligned16(u) || !aligned16(A) || !aligned16(B) || !aligned16(C) || (H * es) % 16 != 0 ||
       L >= (int64_t(1) << 31) || H >= (int64_t(1) << 31))
@@ -489,12 +509,14 @@ int launch_ssm_forward_tma(const void* u, const void* A, const void* B, const vo
   int* status = device_status_ptr();
   if (!status) return TSSM_ERR_UNSUPPORTED;
   constexpr int bytes = FtLayout<T>::BYTES;
-  auto kern = ssm_forward_tma_kernel<T>;
+  auto kern = pool_out ? ssm_forward_tma_kernel<T, true> : ssm_forward_tma_kernel<T, false>;
   // The dynamic shared-memory opt-in is per device; it is cheap, so set it on every launch.
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
     return check_launch("ssm_forward_tma: set smem attribute");
   dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
-  kern<<<grid, (FT_NW + 1) * 32, bytes, st>>>(mA, mU, mB, mC, (const T*)D, (T*)y, (T*)h, (int)L, (int)H, status);
+  kern<<<grid, (FT_NW + 1) * 32, bytes, st>>>(mA, mU, mB, mC, (const T*)D, (T*)y, (T*)h, (int)L, (int)H,
+                                              (const float*)poolW, (const float*)pool_bias, (float*)pool_out,
+                                              pool_inv, status);
   return check_launch("ssm_forward_tma");
 }
 }  // namespace
@@ -513,14 +535,17 @@ int ssm_forward_impl(const void* u, const void* A, const void* B, const void* C,
   constexpr int S = 16, NW = 16;
   dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
   const float pool_inv = (float)(1.0 / ((double)L * (double)H + 1e-9));
-  // With the pooled head the kernel walks shorter per-warp runs (S=8) with twice
-  // the warps: at S=16 the extra accumulator leaves too few registers for the
-  // loads in flight (measured: +18 us against +6 us at config-1 size).
+  // Register-staged fallback: with the pooled head it walks shorter per-warp runs
+  // (S=8) with twice the warps: at S=16 the extra accumulator leaves too few
+  // registers for the loads in flight (measured: +18 us against +6 us at config-1 size).
   const bool pool = pool_out != nullptr;
   const int nthr = pool ? 32 * 32 : NW * 32;
-  if (!pool && (dtype == TSSM_F32 || dtype == TSSM_BF16)) {
-    const int r = dtype == TSSM_F32 ? launch_ssm_forward_tma<float>(u, A, B, C, D, y, h, Bsz, L, H, st)
-                                    : launch_ssm_forward_tma<__nv_bfloat16>(u, A, B, C, D, y, h, Bsz, L, H, st);
+  if (dtype == TSSM_F32 || dtype == TSSM_BF16) {
+    const int r = dtype == TSSM_F32
+                      ? launch_ssm_forward_tma<float>(u, A, B, C, D, y, h, poolW, pool_bias, pool_out, pool_inv, Bsz,
+                                                      L, H, st)
+                      : launch_ssm_forward_tma<__nv_bfloat16>(u, A, B, C, D, y, h, poolW, pool_bias, pool_out,
+                                                              pool_inv, Bsz, L, H, st);
     if (r != TSSM_ERR_UNSUPPORTED) return r;   // launched (or failed): otherwise the register-staged kernel
   }
   if (dtype == TSSM_F32) {
