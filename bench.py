@@ -403,7 +403,8 @@ def run_ours_c1bwd(args, rank, world, local):
     alg = n * 4 * 10 + n * 4 * 5 + Bt * L * 4 * 2 + Hp * 4 * 2   # ssm_backward 6R+4W, discretize_bwd 4R+1W
     upd = Bt * L * Hp
     cfg = {"workload": "config1 backward: ssm_backward + zoh_discretize_bwd, B4 L1024 H'=D*N=1024 f32",
-           "global_batch": Bt * world, "seq_len": L, "parallelism": "batch, %d rank(s)" % world}
+           "global_batch": Bt * world, "seq_len": L, "parallelism": "batch, %d rank(s)" % world,
+           "timing": "CUDA-graph replays of the step" if args.graph else "eager launches"}
     return _line(args, world, METRIC, world * upd / t_step, t_step, "f32", cfg, alg,
                  "ssm_backward_kernel + zoh_discretize_bwd_kernel", "ssm_backward_c1.md", clocks,
                  launches=2 * args.steps)
@@ -588,10 +589,10 @@ def main():
     ap.add_argument("--seq-len", type=int, default=None, help="config 4: override L (multiple of 16384)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    # Config 1 is two ~10-20 us kernels: eager Python dispatch of the two operators
+    # Config 1 (forward and backward) is two ~10-30 us kernels: eager Python dispatch of the two operators
     # costs more than they run, so its steps are captured once and replayed as a
     # CUDA graph (the same kernels and bytes; the host launch path is what goes).
-    if args.config == "c1" and not args.no_graph:
+    if args.config in ("c1", "c1bwd") and not args.no_graph:
         args.graph = True
     rank, world, local = dist_env()
     if args.impl == "reference":

@@ -34,7 +34,10 @@ def test_ssm_backward_golden(cuda_ops):
         assert rel_err(t, g[name]) < TOL_FP32, name
 
 
-@pytest.mark.parametrize("Bt,L,H", [(1, 1, 1), (2, 33, 37), (3, 257, 64), (2, 1000, 96), (1, 4099, 33)])
+@pytest.mark.parametrize("Bt,L,H", [(1, 1, 1), (2, 33, 37), (3, 257, 64), (2, 1000, 96), (1, 4099, 33),
+                                    # 16-byte row pitch (TMA-staged kernel): one step, one exact
+                                    # 64-step tile with a partial channel tile, a tile edge plus one
+                                    (1, 1, 4), (2, 64, 36), (1, 129, 32)])
 def test_ssm_backward_vs_oracle(cuda_ops, Bt, L, H):
     ins = _scan_inputs(Bt, L, H, seed=L * 31 + H)
     out = cuda_ops.ssm_backward(*(cu(t) for t in ins))

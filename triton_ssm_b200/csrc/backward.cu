@@ -12,7 +12,10 @@
 // reverse (a, x) aggregate, takes the carry from the warps after it, and
 // replays its steps writing du, dA, dB, dC.  Every input is read from HBM once
 // (A_{t+1} and h_{t-1} at a run's edge come from the neighbouring run's rows,
-// which the cache holds).
+// which the cache holds).  When the rows are TMA-addressable the same reverse
+// scan runs with its inputs staged by TMA (ssm_backward_tma_kernel): a producer
+// warp keeps 64-step tiles of A (shifted one step), u, B, C, dY and a 65-row h
+// tile (from t0-1) in flight while 16 compute warps work on the tile after it.
 //
 // zoh_discretize_bwd (replaces discretize_kernel.py:97-162): per (b, t, h)
 //     a = -exp(A_log), x = dt a, e = exp(x), em1 = guarded exp(x)-1 (bf16 form, :134)
@@ -22,7 +25,11 @@
 // A CTA owns a block of (b, t) rows and all of H, so each row's ddt is reduced
 // inside the CTA (no store/atomic race as in :159-162); dA_log gets one atomic
 // add per (CTA, h).
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
+#include "tcgen05.cuh"
+#include "tmap.cuh"
 
 namespace tssm {
 namespace {
@@ -109,6 +116,218 @@ __global__ void __launch_bounds__(NW * 32, 1) ssm_backward_kernel(
     __syncthreads();
     carry = s_carry[lane];
   }
+}
+
+
+// ---------------------------------------------------------------- TMA-staged ssm_backward
+constexpr int BT_CH = 64;             // steps per staged tile
+constexpr int BT_NW = 16;             // compute warps
+constexpr int BT_S = BT_CH / BT_NW;   // steps per compute warp and tile
+constexpr uint32_t BT_BAR = 1;        // named barrier of the compute warps
+
+template <typename T>
+struct BtLayout {
+  static constexpr int STAGES = sizeof(T) == 4 ? 4 : 8;
+  static constexpr int TILE = BT_CH * 32 * (int)sizeof(T);                      // [BT_CH][32] tile
+  static constexpr int HTILE = ((BT_CH + 1) * 32 * (int)sizeof(T) + 127) / 128 * 128;   // h: rows t0-1 .. t0+63
+  static constexpr int STAGE = 5 * TILE + HTILE;                                // A(+1), u, B, C, dY, h
+  static constexpr int OFF_AGG = STAGES * STAGE;                                // [2][2][BT_NW][32] f32
+  static constexpr int OFF_BAR = OFF_AGG + 2 * 2 * BT_NW * 32 * 4;
+  static constexpr int OFF_MISC = OFF_BAR + 2 * STAGES * 8;                     // abort flag, issued, consumed
+  static constexpr int BYTES = OFF_MISC + 16 + 128;
+  static_assert(BYTES <= 232448, "ssm_backward_tma shared-memory layout exceeds the per-CTA limit");
+};
+
+// CTA = (32 channels, one batch row), walking the tiles from the end of the
+// sequence; warp BT_NW is the TMA producer.  A is loaded one step ahead (row r
+// of the tile is A_{t+1}; A_L reads as zero) and h one step behind (row r is
+// h_{t-1}, row r+1 is h_t; h_{-1} reads as zero).
+template <typename T>
+__global__ void __launch_bounds__((BT_NW + 1) * 32, 1) ssm_backward_tma_kernel(
+    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmU,
+    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
+    const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmH, T* __restrict__ du,
+    T* __restrict__ dA, T* __restrict__ dB, T* __restrict__ dC, int L, int H, int* __restrict__ status) {
+  using LY = BtLayout<T>;
+  constexpr int ST = LY::STAGES;
+  extern __shared__ uint8_t bt_raw[];
+  uint8_t* smem = bt_raw + ((128u - (sm100::smem_u32(bt_raw) & 127u)) & 127u);
+  float* agg = reinterpret_cast<float*>(smem + LY::OFF_AGG);   // [buf][a|x][warp][lane]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
+  uint64_t* empty = full + ST;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_MISC);
+  int* issued = reinterpret_cast<int*>(smem + LY::OFF_MISC + 4);
+  int* consumed = reinterpret_cast<int*>(smem + LY::OFF_MISC + 8);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ch0 = blockIdx.x * 32, b = blockIdx.y;
+  const int nt = (L + BT_CH - 1) / BT_CH;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], BT_NW);
+    }
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == BT_NW) {
+    // ------------------------------------------------------------ producer (last tile first)
+    if (lane == 0) {
+      sm100::prefetch_tmap(&tmA);
+      sm100::prefetch_tmap(&tmU);
+      sm100::prefetch_tmap(&tmB);
+      sm100::prefetch_tmap(&tmC);
+      sm100::prefetch_tmap(&tmY);
+      sm100::prefetch_tmap(&tmH);
+      int k = 0;
+      for (; k < nt; ++k) {
+        const int s = k % ST;
+        const int t0 = (nt - 1 - k) * BT_CH;
+        if (k >= ST && !sm100::mbar_wait(&empty[s], ((k / ST) - 1) & 1, abort_flag)) {
+          if (!*abort_flag) {
+            *abort_flag = 1;
+            atomicExch(status, 2101);
+          }
+          break;
+        }
+        uint8_t* st = smem + s * LY::STAGE;
+        sm100::mbar_arrive_expect_tx(&full[s], 5 * LY::TILE + (BT_CH + 1) * 32 * (int)sizeof(T));
+        sm100::tma_load_3d(st, &tmA, ch0, t0 + 1, b, &full[s]);
+        sm100::tma_load_3d(st + LY::TILE, &tmU, ch0, t0, b, &full[s]);
+        sm100::tma_load_3d(st + 2 * LY::TILE, &tmB, ch0, t0, b, &full[s]);
+        sm100::tma_load_3d(st + 3 * LY::TILE, &tmC, ch0, t0, b, &full[s]);
+        sm100::tma_load_3d(st + 4 * LY::TILE, &tmY, ch0, t0, b, &full[s]);
+        sm100::tma_load_3d(st + 5 * LY::TILE, &tmH, ch0, t0 - 1, b, &full[s]);
+      }
+      *issued = k;
+    }
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int ch = ch0 + lane;
+    const bool valid = ch < H;
+    const int64_t base = (int64_t)b * L * H + ch;
+    float carry = 0.f;   // dH at the first step after the current tile (0 past the end)
+    int k = 0;
+    for (; k < nt; ++k) {
+      const int s = k % ST, pb = k & 1;
+      const int t0 = (nt - 1 - k) * BT_CH;
+      const bool bad = !sm100::mbar_wait(&full[s], (k / ST) & 1, abort_flag);
+      const T* tA = reinterpret_cast<const T*>(smem + s * LY::STAGE);   // A_{t+1}
+      const T* tU = tA + BT_CH * 32;
+      const T* tB = tU + BT_CH * 32;
+      const T* tC = tB + BT_CH * 32;
+      const T* tY = tC + BT_CH * 32;
+      const T* tH = tY + BT_CH * 32;                                      // row r: h_{t-1}, row r+1: h_t
+      const int r0 = warp * BT_S;
+      float a[BT_S], x[BT_S];
+      float ag_a = 1.f, ag_x = 0.f;   // dH at this warp's first step = ag_a * dH after its steps + ag_x
+      if (!bad) {
+#pragma unroll
+        for (int i = 0; i < BT_S; ++i) {
+          const int r = (r0 + i) * 32 + lane;
+          if (valid && t0 + r0 + i < L) {
+            a[i] = ldf(tA + r);
+            x[i] = ldf(tC + r) * ldf(tY + r);
+          } else {
+            a[i] = 1.f;
+            x[i] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int i = BT_S - 1; i >= 0; --i) {
+          ag_x = a[i] * ag_x + x[i];
+          ag_a *= a[i];
+        }
+        agg[((pb * 2 + 0) * BT_NW + warp) * 32 + lane] = ag_a;
+        agg[((pb * 2 + 1) * BT_NW + warp) * 32 + lane] = ag_x;
+      } else if (!*abort_flag) {
+        *abort_flag = 1;
+        atomicExch(status, 2102);
+      }
+      if (sm100::named_bar_or(BT_BAR, BT_NW * 32, bad)) break;
+      // dH after this warp's steps (folded over the warps after it) and the carry into
+      // the previous tile, from all warps' aggregates
+      float wa[BT_NW], wx[BT_NW];
+#pragma unroll
+      for (int w = 0; w < BT_NW; ++w) {
+        wa[w] = agg[((pb * 2 + 0) * BT_NW + w) * 32 + lane];
+        wx[w] = agg[((pb * 2 + 1) * BT_NW + w) * 32 + lane];
+      }
+      float dh = carry, nxt = carry;
+#pragma unroll
+      for (int w = BT_NW - 1; w >= 0; --w) {
+        if (w == warp) dh = nxt;
+        nxt = wa[w] * nxt + wx[w];
+      }
+      carry = nxt;
+#pragma unroll
+      for (int i = BT_S - 1; i >= 0; --i) {
+        dh = a[i] * dh + x[i];
+        const int t = t0 + r0 + i;
+        if (valid && t < L) {
+          const int r = (r0 + i) * 32 + lane;
+          const int64_t off = base + (int64_t)t * H;
+          stf(du + off, ldf(tB + r) * dh);
+          stf(dB + off, ldf(tU + r) * dh);
+          stf(dC + off, ldf(tY + r) * ldf(tH + r + 32));
+          stf(dA + off, ldf(tH + r) * dh);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty[s]);
+    }
+    if (threadIdx.x == 0) *consumed = k;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    for (int c = *consumed; c < *issued; ++c) sm100::mbar_wait(&full[c % ST], (c / ST) & 1, nullptr, 100000000ull);
+  }
+}
+
+// 3-D map over [Bsz][L][H] (H contiguous), box {32 channels, rows steps, 1}, no swizzle.
+inline bool bt_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int esize, int64_t Bsz, int64_t L,
+                   int64_t H, uint32_t rows) {
+  auto fn = tmap_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)H, (cuuint64_t)L, (cuuint64_t)Bsz};
+  cuuint64_t strides[2] = {(cuuint64_t)(H * esize), (cuuint64_t)(L * H * esize)};
+  cuuint32_t box[3] = {32, rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Launches the TMA-staged backward when the tensors are TMA-addressable; returns
+// TSSM_ERR_UNSUPPORTED (nothing launched) otherwise.
+template <typename T>
+int launch_ssm_backward_tma(const void* u, const void* A, const void* B, const void* C, const void* h, const void* dY,
+                            void* du, void* dA, void* dB, void* dC, int64_t Bsz, int64_t L, int64_t H,
+                            cudaStream_t st) {
+  constexpr int es = (int)sizeof(T);
+  if (!aligned16(u) || !aligned16(A) || !aligned16(B) || !aligned16(C) || !aligned16(h) || !aligned16(dY) ||
+      (H * es) % 16 != 0 || L >= (int64_t(1) << 31) - BT_CH || H >= (int64_t(1) << 31))
+    return TSSM_ERR_UNSUPPORTED;
+  const CUtensorMapDataType dt = es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap mA, mU, mB, mC, mY, mH;
+  if (!bt_map(&mA, A, dt, es, Bsz, L, H, BT_CH) || !bt_map(&mU, u, dt, es, Bsz, L, H, BT_CH) ||
+      !bt_map(&mB, B, dt, es, Bsz, L, H, BT_CH) || !bt_map(&mC, C, dt, es, Bsz, L, H, BT_CH) ||
+      !bt_map(&mY, dY, dt, es, Bsz, L, H, BT_CH) || !bt_map(&mH, h, dt, es, Bsz, L, H, BT_CH + 1))
+    return TSSM_ERR_UNSUPPORTED;
+  int* status = device_status_ptr();
+  if (!status) return TSSM_ERR_UNSUPPORTED;
+  constexpr int bytes = BtLayout<T>::BYTES;
+  auto kern = ssm_backward_tma_kernel<T>;
+  // The dynamic shared-memory opt-in is per device; it is cheap, so set it on every launch.
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return check_launch("ssm_backward_tma: set smem attribute");
+  dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
+  kern<<<grid, (BT_NW + 1) * 32, bytes, st>>>(mA, mU, mB, mC, mY, mH, (T*)du, (T*)dA, (T*)dB, (T*)dC, (int)L,
+                                              (int)H, status);
+  return check_launch("ssm_backward_tma");
 }
 
 constexpr int DBWD_THREADS = 256;
@@ -239,6 +458,12 @@ extern "C" int tssm_ssm_backward(const void* u, const void* A, const void* B, co
   TSSM_REQUIRE(Bsz <= 65535, "ssm_backward: batch %lld exceeds 65535", (long long)Bsz);
   TSSM_REQUIRE(L * H < (int64_t(1) << 31), "ssm_backward: L*H must be < 2^31 per batch row");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == TSSM_F32 || dtype == TSSM_BF16) {
+    const int r = dtype == TSSM_F32
+                      ? launch_ssm_backward_tma<float>(u, A, B, C, h, dY, du, dA, dB, dC, Bsz, L, H, st)
+                      : launch_ssm_backward_tma<__nv_bfloat16>(u, A, B, C, h, dY, du, dA, dB, dC, Bsz, L, H, st);
+    if (r != TSSM_ERR_UNSUPPORTED) return r;   // launched (or failed): otherwise the register-staged kernel
+  }
   // runs of 4 steps, 32 warps: the six inputs of a run are loaded before its replay
   constexpr int S = 4, NW = 32;
   dim3 grid((unsigned)cdiv(H, 32), (unsigned)Bsz);
