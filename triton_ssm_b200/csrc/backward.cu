@@ -352,12 +352,16 @@ __global__ void __launch_bounds__(DBWD_THREADS) zoh_discretize_bwd_kernel(
   for (int64_t hc = 0; hc < H; hc += DBWD_THREADS * PER) {
     const int64_t h0 = hc + (int64_t)tid * PER;
     const bool act = h0 < H;   // VEC: H % 4 == 0, so all PER channels exist
-    float a[PER], na[PER], acc[PER];
+    // per channel: a, and the reciprocals 1/(a^2+1e-18), 1/(a+1e-12) that replace a
+    // division per element (within an ulp of the quotients)
+    float a[PER], na[PER], acc[PER], r2[PER], r1[PER];
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       na[k] = act ? expf(A_log[h0 + k]) : 1.f;
       a[k] = -na[k];
       acc[k] = 0.f;
+      r2[k] = 1.0f / (a[k] * a[k] + 1e-18f);
+      r1[k] = 1.0f / (a[k] + 1e-12f);
     }
     // four rows per step: their loads go out together, then four independent reductions
     for (int r4 = 0; r4 < nrows; r4 += 4) {
@@ -406,10 +410,10 @@ __global__ void __launch_bounds__(DBWD_THREADS) zoh_discretize_bwd_kernel(
           const float e = expf(x);
           const float em1 = expm1_guard_bf16(x, e);
           part[j] += vda[j][k] * a[k] * vab[j][k] + vdb[j][k] * e * vb[j][k];
-          const float num = (e * dtv[j] * a[k] - em1) / (a[k] * a[k] + 1e-18f);
+          const float num = (e * dtv[j] * a[k] - em1) * r2[k];
           const float da = vda[j][k] * dtv[j] * vab[j][k] + vdb[j][k] * num * vb[j][k];
           if (use) acc[k] += da * (-na[k]);
-          out[k] = vdb[j][k] * em1 / (a[k] + 1e-12f);
+          out[k] = vdb[j][k] * em1 * r1[k];
         }
         if (!use) part[j] = 0.f;
         if (use) {
