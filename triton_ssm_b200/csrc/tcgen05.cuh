@@ -43,22 +43,35 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+// try_wait with a suspend-time hint: the waiting thread sleeps (instead of
+// re-polling shared memory) until the phase completes or ~hint_ns pass.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 1000000u) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait on an mbarrier phase: gives up after `timeout_ns` of wall time
 // (or as soon as *abort becomes non-zero) and returns false so the caller can
 // report a timeout instead of hanging the GPU.  The polling loop is kept out of
 // line: kernels with many wait sites stay small enough for the instruction cache.
-// It polls with the non-blocking test_wait: try_wait (with or without a suspend
-// hint) was measured to park the waiting thread for ~900 cycles after the phase
-// had completed, which lands directly on the chunk pipeline's critical path.
+// Waiting threads sleep in try_wait: a resumed thread was traced to continue a few
+// hundred cycles after the phase completed, but spinning on test_wait instead was
+// measured 1-2 % slower on the N=128 scan under the power cap (the spinning warps
+// draw power and the clock drops) and no faster on N=64.
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, const volatile int* abort,
                                             uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (abort && *abort) return false;
-      if (globaltimer_ns() - t0 > timeout_ns) return false;
-    }
+  const uint32_t hint = timeout_ns < 1000000ull ? (uint32_t)timeout_ns : 1000000u;
+  for (;;) {
+    if (mbar_try_wait(bar, parity, hint)) return true;
+    if (abort && *abort) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
   }
 }
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort = nullptr,
