@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(NW * 32) selective_scan_kernel(
   const bool valid = d < Dm && n < N;
   const int64_t b = blockIdx.y;
   const float a = valid ? -expf(A_log[d * N + n]) : -1.f;
+  const float ra = 1.0f / (a + 1e-12f);   // ZOH coefficient as a product (within an ulp of the quotient)
   const float dsk = (d < Dm) ? Dskip[d] : 0.f;
   const float* xb = x + b * L * Dm;
   const float* dtb = dt + b * L;
@@ -140,7 +141,9 @@ __global__ void __launch_bounds__(NW * 32) selective_scan_kernel(
   float carry = 0.f;
   for (int64_t t0 = 0; t0 < L; t0 += NW * S) {
     const int64_t ts = t0 + (int64_t)warp * S;
-    float ab[S], bu[S], xv[S];
+    // every load of the run (C included) goes out before the first use: the replay
+    // below has no global load between its dependent readout reductions
+    float ab[S], bu[S], xv[S], cv[S];
 #pragma unroll
     for (int i = 0; i < S; ++i) {
       const int64_t t = ts + i;
@@ -149,11 +152,13 @@ __global__ void __launch_bounds__(NW * 32) selective_scan_kernel(
         const float e = expf(xx);
         ab[i] = e;
         xv[i] = xb[t * Dm + d];
-        bu[i] = (expm1_guard_f32(xx, e) / (a + 1e-12f) * Bb[t * N + n]) * xv[i];
+        bu[i] = (expm1_guard_f32(xx, e) * ra * Bb[t * N + n]) * xv[i];
+        cv[i] = Cb[t * N + n];
       } else {
         ab[i] = 1.f;
         bu[i] = 0.f;
         xv[i] = (d < Dm && t < L) ? xb[t * Dm + d] : 0.f;
+        cv[i] = 0.f;
       }
     }
     float ag_a = 1.f, ag_x = 0.f;
@@ -171,7 +176,7 @@ __global__ void __launch_bounds__(NW * 32) selective_scan_kernel(
     for (int i = 0; i < S; ++i) {
       hs = ab[i] * hs + bu[i];
       const int64_t t = ts + i;
-      float part = (valid && t < L) ? Cb[t * N + n] * hs : 0.f;
+      float part = cv[i] * hs;
       for (int off = NP >> 1; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
       if (n == 0 && d < Dm && t < L) y[(b * L + t) * Dm + d] = part + dsk * xv[i];
     }
