@@ -604,7 +604,7 @@ extern "C" int tssm_selective_scan(const void* x, const void* dt, const void* A_
   TSSM_REQUIRE(Bsz <= 65535, "selective_scan: batch %lld exceeds 65535", (long long)Bsz);
   int NP = 1;
   while (NP < N) NP <<= 1;
-  constexpr int S = 16, NW = 16;
+  constexpr int S = 8, NW = 32;
   dim3 grid((unsigned)cdiv(Dm, 32 / NP), (unsigned)Bsz);
   selective_scan_kernel<S, NW><<<grid, NW * 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       (const float*)x, (const float*)dt, (const float*)A_log, (const float*)B, (const float*)C,
