@@ -7,6 +7,12 @@ chunked scan, B=16 H=8 P=64 N=64 L=8192, bf16 inputs, f32 state), one step =
 one full pass over one batch.  Under torchrun each rank runs its own batch
 (weak scaling, no collective on the data path); the time is the max over ranks.
 Prints ONE JSON line on rank 0.
+
+The same line carries the other configs under "configs" (--configs): config 4,
+the sequence-parallel scan of L = 1,048,576 tokens sharded over all N ranks
+with one NCCL all-gather of slice carries (strong scaling; its scan and its
+exchange + fix-up times are also reported apart), and, on one GPU, configs 1,
+3 and 5 (config 5 with steps/s and per-step latency percentiles).
 """
 import argparse
 import json
@@ -477,8 +483,8 @@ def run_ours_dtproj(args, rank, world, local):
 def run_ours_c4(args, rank, world, local):
     """Config 4: B4 H32 P64 N128 L=1,048,576 bf16, sequence sharded over the ranks
     (strong scaling): local scan from a zero state, one all-gather of
-    (state, decay) per rank, carry fix-up."""
-    import triton_ssm_b200 as ts
+    (state, decay) per rank, carry fix-up.  The exchange + fix-up time is
+    measured on its own from events recorded inside the timed steps."""
     from triton_ssm_b200 import parallel, workloads
     dev = torch.device("cuda", local)
     c = workloads.C4
@@ -488,22 +494,51 @@ def run_ours_c4(args, rank, world, local):
     L0, Ls = a * (1 << 14), (b - a) * (1 << 14)
     inp = workloads.ssd_inputs_slice(Bt, L0, Ls, H, P, N, dev, seed=4)
     y = torch.empty_like(inp["x"])
-    group = None
-    step = lambda: parallel.ssd_sequence_parallel(inp["x"], inp["dt"], inp["A_log"], inp["B"], inp["C"], inp["D"],
-                                                  group=group, y=y)
+    step = lambda marks=None: parallel.ssd_sequence_parallel(inp["x"], inp["dt"], inp["A_log"], inp["B"], inp["C"],
+                                                              inp["D"], y=y, marks=marks)
+    stream = torch.cuda.current_stream(dev)
     t_step, clocks = _timed(args, world, dev, step)
+    # a separate pass with events around each step splits scan / exchange + fix-up
+    n_split = max(3, min(args.steps, 10))
+    starts, ends, marks = [], [], []
+    torch.cuda.synchronize()
+    barrier(world)
+    for _ in range(n_split):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        step(marks)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record(stream)
+        starts.append(e0)
+        ends.append(e1)
+    torch.cuda.synchronize()
+    scan_ms = statistics.median(s.elapsed_time(m) for s, m in zip(starts, marks))
+    xfix_ms = statistics.median(m.elapsed_time(e) for m, e in zip(marks, ends))
+    scan_ms = max_over_ranks(scan_ms, world)
+    xfix_ms = max_over_ranks(xfix_ms, world)
     upd = Bt * L * H * P * N
     alg = workloads.ssd_bytes(Bt, L, H, P, N)
+    K = parallel.ssd_local_pieces(Bt, H, Ls, torch.cuda.get_device_properties(dev).multi_processor_count)
     cfg = {"workload": "config4: sequence-parallel multi-head scan B%d H%d P%d N%d L=%d bf16, A_h=-(1+h%%16), "
                        "L sharded over %d rank(s) with one all-gather of slice carries" % (Bt, H, P, N, L, world),
            "global_batch": Bt, "seq_len": L, "parallelism": "sequence (L) x %d" % world,
-           "nvlink_bytes_per_rank": Bt * H * P * N * 4 + Bt * H * 4}
+           "slice_tokens_per_rank": Ls, "in_device_pieces": K,
+           "nvlink_bytes_per_rank": Bt * H * P * N * 4 + Bt * H * 4,
+           "l2": "%d GB of inputs and outputs per rank per step (> the 126 MB L2)" % (alg // world // 10**9)}
     out = _line(args, world, METRIC, upd / t_step, t_step, "bf16", cfg, alg // world,
                 "ssd_chunk_scan_kernel<128,false> + ssd_carry_fixup_kernel<128>",
-                "ssd_chunk_scan_c4.md" if world == 1 and L == c["L"] else None, clocks,
-                launches=(2 if world > 1 else 1) * args.steps)
+                "ssd_chunk_scan_c4.md" if L == c["L"] else None, clocks,
+                launches=(3 if K > 1 else 1) * args.steps + (1 if world > 1 else 0) * args.steps)
+    if out["roofline"]["traffic"] is not None and world > 1:
+        out["roofline"]["traffic"] //= world
+        out["roofline"]["traffic_note"] = "full-size 1-GPU capture divided by the rank count"
     out["scaling"] = "strong"
     out["roofline"]["note"] = "algorithmic bytes per rank (1/world of the whole sequence)"
+    out["split_ms"] = {"local_scan": scan_ms, "exchange_and_fixup": xfix_ms,
+                       "exchange_and_fixup_frac": xfix_ms / max(1e-9, scan_ms + xfix_ms),
+                       "how": "median over %d steps of CUDA events before the step, after the local scan, after "
+                              "the fix-up; max over ranks" % n_split}
+    del inp, y
     return out
 
 
@@ -569,6 +604,36 @@ def run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd):
             "path": "triton_ssm_b200.host.SSDHostPipeline (pinned host buffers, 8 batch slices)"}
 
 
+SUB_KEYS = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "scaling", "dtype", "config", "roofline",
+            "gpu_launches", "clocks", "steps_per_sec", "p50_step_ms", "p99_step_ms", "split_ms", "n_gpus")
+
+
+def run_sub_configs(args, rank, world, local):
+    """The other benchmark configs, each timed like the headline (warm-up, a
+    second of load, exactly `steps` CUDA-event-timed steps, clocks sampled),
+    reported as sub-records of the one JSON line.  Config 4 is the sequence-
+    sharded scan over all ranks (its one collective); configs 1, 3 and 5 run on
+    a single GPU (only when world == 1)."""
+    import copy
+    out = {}
+    names = [c.strip() for c in args.configs.split(",") if c.strip()]
+    runners = {"c1": run_ours_c1, "c3": run_ours_c3, "c4": run_ours_c4, "c5": run_ours_c5}
+    for name in names:
+        if name not in runners:
+            raise SystemExit("unknown sub-config %r" % name)
+        if name != "c4" and world > 1:
+            continue
+        a = copy.copy(args)
+        a.batch = None
+        a.graph = name == "c1" and not args.no_graph
+        torch.cuda.empty_cache()
+        rec = runners[name](a, rank, world, local)
+        out[name] = {k: rec[k] for k in SUB_KEYS if k in rec}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -587,6 +652,10 @@ def main():
     ap.add_argument("--no-graph", action="store_true",
                     help="config 1: time the eager per-op launches instead of graph replays")
     ap.add_argument("--seq-len", type=int, default=None, help="config 4: override L (multiple of 16384)")
+    ap.add_argument("--configs", default="c4,c1,c3,c5",
+                    help="with the default config 2 line: the other configs timed in the same process and reported "
+                         "under 'configs' (c4 on every rank, sequence-sharded; c1/c3/c5 on one GPU only); "
+                         "'none' to skip")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     # Config 1 (forward and backward) is two ~10-30 us kernels: eager Python dispatch of the two operators
@@ -613,6 +682,8 @@ def main():
                   "c5": run_ours_c5, "c1bwd": run_ours_c1bwd, "ring": run_ours_ring,
                   "dtproj": run_ours_dtproj}[args.config]
         out = runner(args, rank, world, local)
+        if args.config == "c2" and args.configs != "none":
+            out["configs"] = run_sub_configs(args, rank, world, local)
         if rank == 0:
             print(json.dumps(out), flush=True)
     finally:

@@ -265,7 +265,10 @@ int tssm_interp_ssm_step(const void* V, const void* M, const void* tau, const vo
                          int64_t stride_hib, int64_t stride_hob, int64_t t_cur, int64_t K,
                          int64_t FTILE, int m_dtype, tssm_stream_t stream);
 
-/* Bytes of device workspace tssm_interp_ssm needs (tile flags + neighbour table). */
+/* Bytes of device workspace tssm_interp_ssm needs (tile flags + neighbour
+ * table): 0 for an empty problem, -1 for sizes outside what tssm_interp_ssm
+ * accepts (Bsz <= 65535, T <= 8192, Lq and Dm < 2^30, and a workspace below
+ * 2^56 bytes). */
 int64_t tssm_interp_ssm_workspace_size(int64_t Bsz, int64_t T, int64_t Dm, int64_t Lq, int64_t FTILE);
 
 /*
@@ -346,6 +349,34 @@ int tssm_ssd_carry_fixup_pieces(const void* S, const void* decay_log2, int64_t p
                                 int64_t P, int64_t N, tssm_stream_t stream);
 
 /*
+ * tssm_ssd_carry_fixup reading every rank's slice carry from the one packed
+ * buffer that a single all-gather of each rank's [state | decay] produces
+ * (the exchange step of the reference's carry scan, ssm_scan.py:53-65, done
+ * across ranks):
+ *   packed [nranks, Bsz*H*P*N + Bsz*H] f32: rank j's final state [Bsz,H,P,N]
+ *   starts at packed + j*(Bsz*H*P*N + Bsz*H) and its decay_log2 [Bsz,H]
+ *   follows it.
+ * Otherwise as tssm_ssd_carry_fixup.  No-op on rank 0.
+ */
+int tssm_ssd_carry_fixup_packed(const void* packed, int64_t rank, int64_t nranks, const void* C,
+                                const void* dt, const void* A_log, void* y, int64_t Bsz, int64_t L,
+                                int64_t H, int64_t P, int64_t N, tssm_stream_t stream);
+
+/*
+ * Final state and decay of sequences scanned as `pieces` in-device pieces
+ * (the carry scan of ssm_scan.py:53-65 over the pieces): with S, decay_log2
+ * as in tssm_ssd_carry_fixup_pieces,
+ *   state_out [Bsz,H,P,N] f32 = the pieces' states chained in order,
+ *     c <- 2^{d_k} c + S_k for k = 0 .. pieces-1;
+ *   decay_out [Bsz,H] f32 = sum_k d_k.
+ * Either output may be NULL.  P*N a multiple of 4; S and state_out 16-byte
+ * aligned.
+ */
+int tssm_ssd_pieces_final_state(const void* S, const void* decay_log2, int64_t pieces, void* state_out,
+                                void* decay_out, int64_t Bsz, int64_t H, int64_t P, int64_t N,
+                                tssm_stream_t stream);
+
+/*
  * Multi-head scan with the reference's own diagonal state h[b,head,p].
  * Replaces multihead_ssm_fwd_local_kernel / multihead_ssm_carry_scan_kernel /
  * multihead_ssm_output_kernel (multihead_ssm_kernel.py:19-187, with the
@@ -362,6 +393,64 @@ int tssm_ssd_carry_fixup_pieces(const void* S, const void* decay_log2, int64_t p
 int tssm_multihead_diag(const void* u, const void* A_log, const void* B, const void* C, const void* dt,
                         const void* Dskip, void* y, int64_t Bsz, int64_t L, int64_t n_heads,
                         int64_t head_dim, int bdisc, int dtype, tssm_stream_t stream);
+
+/*
+ * The reference's blocked scans launch for launch, for callers that drive its
+ * kernels individually (the fused entry points above are the fast path).
+ * Intermediates keep the reference's layouts: loc_a, loc_x [Bsz,L,H] and
+ * carry [2, rows, NBLK] (a-part first, then x-part; rows = Bsz*H), with
+ * NBLK*BLK >= L; blocks past L hold the identity (1, 0).  f32, contiguous.
+ *
+ * tssm_ssm_fwd_local: ssm_fwd_local_kernel (ssm_scan.py:17-50).
+ * tssm_ssm_bwd_local: ssm_bwd_local_kernel (ssm_scan.py:135-170), A_{t+1}
+ *   and C*dY walked from the end of each block.
+ * tssm_blocked_carry_scan: ssm_carry_scan_kernel (ssm_scan.py:53-65),
+ *   multihead_ssm_carry_scan_kernel (multihead_ssm_kernel.py:105-117) with
+ *   reverse = 0, ssm_bwd_carry_scan_kernel (ssm_scan.py:173-185) with
+ *   reverse = 1: inclusive scan of each row's block carries in place.
+ * tssm_ssm_fwd_apply: ssm_fwd_apply_kernel (ssm_scan.py:68-98).
+ * tssm_ssm_output: ssm_output_kernel (ssm_scan.py:101-124), y = C*h + D*u.
+ * tssm_ssm_bwd_apply: ssm_bwd_apply_kernel (ssm_scan.py:188-231).
+ */
+int tssm_ssm_fwd_local(const void* u, const void* A, const void* B, void* loc_a, void* loc_x, void* carry,
+                       int64_t Bsz, int64_t L, int64_t H, int64_t BLK, int64_t NBLK, tssm_stream_t stream);
+int tssm_ssm_bwd_local(const void* A, const void* C, const void* dY, void* loc_a, void* loc_dh, void* carry,
+                       int64_t Bsz, int64_t L, int64_t H, int64_t BLK, int64_t NBLK, tssm_stream_t stream);
+int tssm_blocked_carry_scan(void* carry, int64_t rows, int64_t NBLK, int reverse, tssm_stream_t stream);
+int tssm_ssm_fwd_apply(const void* loc_a, const void* loc_x, const void* carry, void* h, int64_t Bsz,
+                       int64_t L, int64_t H, int64_t BLK, int64_t NBLK, tssm_stream_t stream);
+int tssm_ssm_output(const void* h, const void* C, const void* D, const void* u, void* y, int64_t Bsz,
+                    int64_t L, int64_t H, tssm_stream_t stream);
+int tssm_ssm_bwd_apply(const void* loc_a, const void* loc_dh, const void* carry, const void* u,
+                       const void* A, const void* B, const void* h, const void* dY, void* du, void* dA,
+                       void* dB, void* dC, int64_t Bsz, int64_t L, int64_t H, int64_t BLK, int64_t NBLK,
+                       tssm_stream_t stream);
+
+/*
+ * The multi-head scan's own launches (multihead_ssm_kernel.py:19-187), read
+ * with the intent of its scalar-index lines, for callers that drive them one
+ * at a time:
+ * tssm_mh_fwd_local: multihead_ssm_fwd_local_kernel (:19-102).  u
+ *   [Bsz,L,n_heads*head_dim], B [Bsz,L,n_heads,head_dim] (dtype f32 or bf16,
+ *   element strides as the reference passes them); A_log [n_heads,head_dim]
+ *   f32 (row stride stride_alh); dt [Bsz,L,n_heads] f32.  Per row
+ *   (b, head, p) and block: Abar = exp(dt*a), a = -exp(A_log), bx = (dt*B)*u;
+ *   loc_a, loc_x [Bsz,L,n_heads,head_dim] f32; carry [2, Bsz*n_heads*head_dim,
+ *   NBLK] f32.
+ * tssm_mh_output: multihead_ssm_output_kernel (:120-187).  h = loc_a * x
+ *   prefix + loc_x; y_head = sum_p C*h + sum_p D*u written to every position
+ *   of the head's slice of y [Bsz,L,n_heads*head_dim] (dtype); D f32.
+ * The carry scan between them is tssm_blocked_carry_scan (reverse = 0).
+ */
+int tssm_mh_fwd_local(const void* u, const void* A_log, const void* B, const void* dt, void* loc_a,
+                      void* loc_x, void* carry, int64_t Bsz, int64_t L, int64_t n_heads, int64_t head_dim,
+                      int64_t stride_ub, int64_t stride_ul, int64_t stride_alh, int64_t stride_Bb,
+                      int64_t stride_Bl, int64_t stride_Bh, int64_t stride_db, int64_t stride_dl,
+                      int64_t stride_dh, int64_t BLK, int64_t NBLK, int dtype, tssm_stream_t stream);
+int tssm_mh_output(const void* loc_a, const void* loc_x, const void* carry, const void* C, const void* D,
+                   const void* u, void* y, int64_t Bsz, int64_t L, int64_t n_heads, int64_t head_dim,
+                   int64_t stride_ub, int64_t stride_ul, int64_t stride_Cb, int64_t stride_Cl,
+                   int64_t stride_Ch, int64_t BLK, int64_t NBLK, int dtype, tssm_stream_t stream);
 
 /*
  * Synchronise `stream` and report (then clear) this device's status word:

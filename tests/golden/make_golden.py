@@ -2,7 +2,9 @@
 
 Run once, in a container that holds the reference source tree:
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [/path/to/reference]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/reference
+
+(or set TSSM_REFERENCE_DIR to that path instead of passing it).
 
 Every fixture is produced by the reference's Triton kernels executed on the CPU
 under the Triton interpreter (``TRITON_INTERPRET=1``) at tiny shapes, and saved
@@ -20,7 +22,10 @@ import os
 import sys
 
 os.environ.setdefault("TRITON_INTERPRET", "1")
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TSSM_REFERENCE_DIR")
+if not REF or not os.path.isfile(os.path.join(REF, "ssm_scan.py")):
+    sys.exit("usage: make_golden.py /path/to/reference  (the directory holding ssm_scan.py; "
+             "or set TSSM_REFERENCE_DIR)")
 sys.path.insert(0, REF)
 
 import numpy as np  # noqa: E402

@@ -4,7 +4,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import TOL_BF16, rel_err
+from conftest import TOL_BF16, parity, rel_err
 from test_gpu_ssd import make_inputs
 
 pytestmark = pytest.mark.gpu
@@ -65,3 +65,61 @@ def test_in_device_pieces_rejects_bad_split(cuda_ops):
     x, dt, A_log, B, C, D = make_inputs(1, 1000, 2, 64, 64, seed=3)
     with pytest.raises(ValueError):
         cuda_ops.multihead_ssm(*(t.to(dev) for t in (x, A_log, B, C, dt, D)), pieces=4)
+
+
+@pytest.mark.parametrize("R,K,L", [(8, 8, 131072), (2, 8, 262144)])
+def test_config4_sharded_length(cuda_ops, R, K, L):
+    """Config 4's chain at the lengths the bench shards: B1 H4 P64 N128 bf16,
+    A_h = -(1 + h mod 16), a sequence of L tokens as R rank slices (emulated on
+    one GPU), each scanned as K in-device pieces.  Each slice writes its final
+    state and decay straight into its row of one packed buffer, as the bench's
+    all-gather lays them out; ssd_carry_fixup_packed then chains the slices.
+    (8 x 8 over 131,072 tokens; 2 x 8 over 262,144 = the 131,072-token slice
+    each of 8 ranks holds in the bench, chained to the slice before it.)
+    Reference semantics: the carry scan of ssm_scan.py:53-98 lifted to slices."""
+    from triton_ssm_b200 import workloads
+    Bt, H, P, N = 1, 4, 64, 128
+    inp = workloads.ssd_inputs_slice(Bt, 0, L, H, P, N, "cpu", seed=4)
+    A, D = inp["A_log"].to(dev), inp["D"].to(dev)
+    n, m = Bt * H * P * N, Bt * H
+    packed = torch.empty(R, n + m, device=dev)
+    Ls = L // R
+    slices = []
+    for r in range(R):
+        sl = slice(r * Ls, (r + 1) * Ls)
+        x, dt, Bm, Cm = (inp[k][:, sl].contiguous().to(dev) for k in ("x", "dt", "B", "C"))
+        y, _, _ = cuda_ops.multihead_ssm(x, A, Bm, Cm, dt, D, return_state=True, return_decay=True, pieces=K,
+                                         state_out=packed[r, :n].view(Bt, H, P, N),
+                                         decay_out=packed[r, n:].view(Bt, H))
+        slices.append((y, Cm, dt))
+    for r, (y, Cm, dt) in enumerate(slices):
+        cuda_ops.ssd_carry_fixup_packed(packed, r, Cm, dt, A, y)
+    cuda_ops.check_device_status()
+    y = torch.cat([t[0] for t in slices], dim=1)
+    ref, href = oracle.ssd_scan_chunked(inp["x"], inp["dt"], inp["A_log"], inp["B"], inp["C"], inp["D"], chunk=256)
+    parity("config 4 y, %d slices x %d pieces, L=%d (B1 H4 N128, bf16)" % (R, K, L), y, ref, TOL_BF16)
+    # the last slice's packed state chained over all slices is the whole sequence's final state
+    carry = torch.zeros(Bt, H, P, N, device=dev)
+    for r in range(R):
+        carry = torch.exp2(packed[r, n:].view(Bt, H))[..., None, None] * carry + packed[r, :n].view(Bt, H, P, N)
+    parity("config 4 final state chained over the %d slices" % R, carry, href, TOL_BF16)
+
+
+def test_pieces_final_state_kernel(cuda_ops):
+    """tssm_ssd_pieces_final_state chains the pieces' states in order and sums
+    their log2 decays (checked against the same chain in torch)."""
+    g = torch.Generator().manual_seed(2)
+    Bt, K, H, P, N = 3, 4, 5, 8, 12
+    S = torch.randn(Bt * K, H, P, N, generator=g).to(dev)
+    d = (-torch.rand(Bt * K, H, generator=g) * 3).to(dev)
+    from triton_ssm_b200 import _lib
+    hl = torch.empty(Bt, H, P, N, device=dev)
+    dl = torch.empty(Bt, H, device=dev)
+    _lib.call("tssm_ssd_pieces_final_state", _lib.ptr(S), _lib.ptr(d), K, _lib.ptr(hl), _lib.ptr(dl), Bt, H, P, N,
+              _lib.stream_of(S))
+    Sv, dv = S.view(Bt, K, H, P, N), d.view(Bt, K, H)
+    ref = Sv[:, 0].clone()
+    for k in range(1, K):
+        ref = torch.exp2(dv[:, k])[..., None, None] * ref + Sv[:, k]
+    assert rel_err(hl, ref) < 1e-6
+    assert rel_err(dl, dv.sum(1)) < 1e-6

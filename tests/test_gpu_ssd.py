@@ -4,7 +4,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import TOL_BF16, rel_err
+from conftest import TOL_BF16, parity, rel_err
 
 pytestmark = pytest.mark.gpu
 dev = "cuda"
@@ -65,8 +65,8 @@ def test_ssd_config2_full_size(cuda_ops):
     x, dt, A_log, B, C, D = make_inputs(16, 8192, 8, 64, 64, seed=2)
     y, hl = run(cuda_ops, x, dt, A_log, B, C, D, return_state=True)
     ry, rh = oracle.ssd_scan_chunked(x, dt, A_log, B, C, D, chunk=256)
-    assert rel_err(y, ry) < TOL_BF16
-    assert rel_err(hl, rh) < TOL_BF16
+    parity("config 2 y  (B16 H8 P64 N64 L8192, bf16)", y, ry, TOL_BF16)
+    parity("config 2 h_last (f32 state)", hl, rh, TOL_BF16)
 
 
 def test_ssd_linearity_and_determinism(cuda_ops):

@@ -44,6 +44,16 @@ SIGNATURES = {
     "tssm_multihead_diag": ([P] * 7 + [I64] * 4 + [I32, I32, P], I32),
     "tssm_ssd_carry_fixup": ([P, P, I64, I64, P, P, P, P] + [I64] * 5 + [P], I32),
     "tssm_ssd_carry_fixup_pieces": ([P, P, I64, P, P, P, P] + [I64] * 5 + [P], I32),
+    "tssm_ssd_carry_fixup_packed": ([P, I64, I64, P, P, P, P] + [I64] * 5 + [P], I32),
+    "tssm_ssd_pieces_final_state": ([P, P, I64, P, P] + [I64] * 4 + [P], I32),
+    "tssm_ssm_fwd_local": ([P] * 6 + [I64] * 5 + [P], I32),
+    "tssm_ssm_bwd_local": ([P] * 6 + [I64] * 5 + [P], I32),
+    "tssm_blocked_carry_scan": ([P, I64, I64, I32, P], I32),
+    "tssm_ssm_fwd_apply": ([P] * 4 + [I64] * 5 + [P], I32),
+    "tssm_ssm_output": ([P] * 5 + [I64] * 3 + [P], I32),
+    "tssm_ssm_bwd_apply": ([P] * 12 + [I64] * 5 + [P], I32),
+    "tssm_mh_fwd_local": ([P] * 7 + [I64] * 4 + [I64] * 9 + [I64] * 2 + [I32, P], I32),
+    "tssm_mh_output": ([P] * 7 + [I64] * 4 + [I64] * 5 + [I64] * 2 + [I32, P], I32),
     "tssm_check_device_status": ([P], I32),
     "tssm_selftest_wait_timeout": ([I64, P], I32),
     "tssm_time_aware_interp": ([P] * 4 + [I64] * 3 + [I64] * 7 + [I64] * 2 + [I32, I32, P], I32),

@@ -31,15 +31,11 @@ int check_launch(const char* what) {
 // device: a __device__ variable lives in each device's copy of the module).
 __device__ int g_device_status;
 
+// Looked up on every call rather than cached per device number: a cached
+// address could belong to another context than the caller's current one.
 int* device_status_ptr() {
-  static std::atomic<int*> cache[64];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  int* p = cache[dev].load();
-  if (!p) {
-    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_device_status) != cudaSuccess) return nullptr;
-    cache[dev].store(p);
-  }
+  int* p = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_device_status) != cudaSuccess) return nullptr;
   return p;
 }
 

@@ -1107,7 +1107,14 @@ extern "C" int tssm_interp_ssm_step(const void* V, const void* Mk, const void* t
 
 extern "C" int64_t tssm_interp_ssm_workspace_size(int64_t Bsz, int64_t T, int64_t Dm, int64_t Lq, int64_t FTILE) {
   if (Bsz <= 0 || T <= 0 || Dm <= 0 || Lq <= 0 || FTILE <= 0) return 0;
+  if (Bsz > 65535 || T > 8192 || Lq >= (int64_t(1) << 30) || Dm >= (int64_t(1) << 30)) return -1;
   const int64_t nt = cdiv(Dm, FTILE);
+  // Bsz*nt*Lq*16 can exceed 64 bits at the extremes of the accepted ranges:
+  // sizes beyond 2^56 bytes are reported as -1 (no workspace can satisfy them)
+  const unsigned __int128 rows = (unsigned __int128)Bsz * (unsigned __int128)nt;
+  const unsigned __int128 big = rows * (unsigned __int128)(Lq + WQB) * (unsigned __int128)(2 * sizeof(int4)) +
+                                rows * (unsigned __int128)T;
+  if (big >= ((unsigned __int128)1 << 56)) return -1;
   return (int64_t)(ws_flags_bytes(Bsz, T, nt) + ws_table_bytes(Bsz, Lq, nt));
 }
 
@@ -1126,6 +1133,7 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
   TSSM_REQUIRE(T <= 8192, "interp_ssm: T=%lld exceeds 8192 observations per row", (long long)T);
   TSSM_REQUIRE(Bsz <= 65535 && Lq < (1 << 30) && Dm < (1 << 30), "interp_ssm: size out of range");
   const int64_t need = tssm_interp_ssm_workspace_size(Bsz, T, Dm, Lq, FTILE);
+  TSSM_REQUIRE(need >= 0, "interp_ssm: size out of range");
   TSSM_REQUIRE(workspace && workspace_bytes >= need, "interp_ssm: workspace of %lld bytes needed",
                (long long)need);
   TSSM_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "interp_ssm: workspace must be 256-byte aligned");
@@ -1242,21 +1250,15 @@ namespace {
 constexpr int64_t kStaticScratchBytes = int64_t(8) << 20;   // 8 MiB, held by every device that loads the library
 static __device__ __align__(256) unsigned char g_interp_static_scratch[kStaticScratchBytes];
 
-// Device address of the array for the current device.  In host code the
-// array's name is only a host-side stand-in, so the address is looked up once
-// per device, with that device current, and cached.
+// Device address of the array in the current context.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up with
+// the device current, on every call: a cached address could belong to another
+// context (after cudaDeviceReset, or when the caller runs in a context of its
+// own) and the lookup costs far less than the launches that follow.
 int static_scratch_ptr(void** out) {
-  static std::atomic<void*> cache[64];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_interp_static_scratch);
   if (e != cudaSuccess) return (int)e;
-  if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-  void* p = cache[dev].load();
-  if (!p) {
-    e = cudaGetSymbolAddress(&p, g_interp_static_scratch);
-    if (e != cudaSuccess) return (int)e;
-    cache[dev].store(p);
-  }
   *out = p;
   return 0;
 }
@@ -1269,6 +1271,7 @@ extern "C" int tssm_interp_ssm_static_scratch(const void* V, const void* Mk, con
                                               int64_t Lq, int64_t K, int64_t FTILE, int m_dtype,
                                               tssm_stream_t stream) {
   const int64_t need = tssm_interp_ssm_workspace_size(Bsz, T, Dm, Lq, FTILE);
+  TSSM_REQUIRE(need >= 0, "interp_ssm_static_scratch: size out of range");
   TSSM_REQUIRE(need <= kStaticScratchBytes,
                "interp_ssm_static_scratch: this problem needs %lld bytes of scratch; the library's static "
                "scratch holds %lld bytes (use tssm_interp_ssm with a caller-provided workspace)",

@@ -169,3 +169,69 @@ extern "C" int tssm_ssd_carry_fixup_pieces(const void* S, const void* decay_log2
                       dim3((unsigned)H, (unsigned)Bsz, (unsigned)(pieces - 1)), L / pieces, H, N,
                       reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Final state of sequences scanned as in-device pieces: the pieces' states
+// chained in order, c <- 2^{d_k} c + S_k, and the summed log2 decay.  One
+// thread per four consecutive state elements of one (sequence, head).
+namespace tssm {
+namespace {
+__global__ void __launch_bounds__(256) ssd_pieces_final_state_kernel(
+    const float4* __restrict__ S, const float* __restrict__ d, int pieces, float4* __restrict__ state_out,
+    float* __restrict__ decay_out, int64_t n4, int64_t hpn4, int pn4, int H) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= n4) return;
+  const int64_t b = e / hpn4, rem = e - b * hpn4;
+  const int h = (int)(rem / pn4);
+  float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+  float dsum = 0.f;
+  for (int k = 0; k < pieces; ++k) {
+    const int64_t seq = b * pieces + k;
+    const float dk = d[seq * H + h];
+    const float f = exp2f(dk);
+    const float4 s = S[seq * hpn4 + rem];
+    c.x = fmaf(f, c.x, s.x);
+    c.y = fmaf(f, c.y, s.y);
+    c.z = fmaf(f, c.z, s.z);
+    c.w = fmaf(f, c.w, s.w);
+    dsum += dk;
+  }
+  if (state_out) state_out[e] = c;
+  if (decay_out && rem % pn4 == 0) decay_out[b * H + h] = dsum;
+}
+}  // namespace
+}  // namespace tssm
+
+extern "C" int tssm_ssd_carry_fixup_packed(const void* packed, int64_t rank, int64_t nranks, const void* C,
+                                           const void* dt, const void* A_log, void* y, int64_t Bsz, int64_t L,
+                                           int64_t H, int64_t P, int64_t N, tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(rank >= 0 && rank < nranks, "ssd_carry_fixup_packed: rank out of range");
+  TSSM_REQUIRE(P == 64 && (N == 64 || N == 128), "ssd_carry_fixup_packed: P must be 64 and N 64 or 128");
+  TSSM_REQUIRE(Bsz >= 0 && L >= 0 && H >= 0, "ssd_carry_fixup_packed: bad size");
+  if (rank == 0 || Bsz * L * H == 0) return TSSM_OK;
+  TSSM_REQUIRE(packed && C && dt && A_log && y, "ssd_carry_fixup_packed: null pointer");
+  TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31), "ssd_carry_fixup_packed: size out of range");
+  const int64_t n = Bsz * H * P * N, per_rank = n + Bsz * H;
+  const float* base = static_cast<const float*>(packed);
+  return launch_fixup(base, base + n, (int)rank, 0, per_rank, H * P * N, per_rank, H, C, dt, A_log, y,
+                      dim3((unsigned)H, (unsigned)Bsz), L, H, N, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int tssm_ssd_pieces_final_state(const void* S, const void* decay_log2, int64_t pieces, void* state_out,
+                                           void* decay_out, int64_t Bsz, int64_t H, int64_t P, int64_t N,
+                                           tssm_stream_t stream) {
+  using namespace tssm;
+  TSSM_REQUIRE(pieces >= 1 && pieces <= 65535, "ssd_pieces_final_state: pieces in [1, 65535]");
+  TSSM_REQUIRE(Bsz >= 0 && H >= 0 && P >= 1 && N >= 1 && (P * N) % 4 == 0,
+               "ssd_pieces_final_state: bad size (P*N must be a multiple of 4)");
+  if (Bsz * H == 0 || (!state_out && !decay_out)) return TSSM_OK;
+  TSSM_REQUIRE(S && decay_log2, "ssd_pieces_final_state: null pointer");
+  TSSM_REQUIRE(aligned16(S) && (!state_out || aligned16(state_out)), "ssd_pieces_final_state: states must be 16-byte aligned");
+  TSSM_REQUIRE(P * N / 4 < (int64_t(1) << 31) && H < (int64_t(1) << 31), "ssd_pieces_final_state: size out of range");
+  const int64_t pn4 = P * N / 4, hpn4 = H * pn4, n4 = Bsz * hpn4;
+  ssd_pieces_final_state_kernel<<<(unsigned)cdiv(n4, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const float4*>(S), static_cast<const float*>(decay_log2), (int)pieces,
+      static_cast<float4*>(state_out), static_cast<float*>(decay_out), n4, hpn4, (int)pn4, (int)H);
+  return check_launch("ssd_pieces_final_state");
+}

@@ -14,7 +14,7 @@ from ._lib import call, dtype_code, ptr, stream_of
 __all__ = ["zoh_discretize", "ssm_forward", "selective_scan", "streaming_ssm_inplace",
            "streaming_step", "multihead_ssm", "check_device_status", "fused_time_aware_interp",
            "fused_interp_ssm_step", "fused_interp_ssm", "linspace_queries", "interp_ssm_workspace_bytes",
-           "ssd_carry_fixup", "ssm_backward", "zoh_discretize_bwd", "streaming_interp_then_ssm",
+           "ssd_carry_fixup", "ssd_carry_fixup_packed", "ssm_backward", "zoh_discretize_bwd", "streaming_interp_then_ssm",
            "dt_project_softplus", "zoh_discretize_dtproj", "mean_pool_logit"]
 
 
@@ -353,7 +353,7 @@ def streaming_interp_then_ssm(ring_V, ring_M, ring_tau, ring_head, v_new, m_new,
 
 
 def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h0=None,
-                  return_state=False, y=None, return_decay=False, pieces=1):
+                  return_state=False, y=None, return_decay=False, pieces=1, state_out=None, decay_out=None):
     """Multi-head chunked scan (``multihead_ssm_kernel.py:19-187``).
 
     mode="diag": the reference's own diagonal state h[b,h,p]
@@ -373,11 +373,14 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
     the pieces are chained by ``tssm_ssd_carry_fixup_pieces`` (the bf16
     outputs of a piece's leading tokens are rounded twice).  For few long
     sequences this spreads the work over more SMs.
+    ``state_out`` [Bt,H,P,N] f32 / ``decay_out`` [Bt,H] f32 (mode "ssd"):
+    contiguous tensors that receive the returned state / decay (for example
+    views into a collective's send buffer), so no copy follows.
     """
     del BLK_L
     if pieces != 1:
         return _multihead_ssd_pieces(u, A_log, B, C, dt, D, int(pieces), bdisc, h0, return_state, y,
-                                     return_decay)
+                                     return_decay, state_out, decay_out)
     if bdisc not in _BDISC:
         raise ValueError("multihead_ssm: bdisc must be 'euler' or 'zoh'")
     if mode == "diag":
@@ -407,8 +410,8 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
     h0 = h0.float().contiguous() if h0 is not None else None
     if y is None:
         y = torch.empty_like(u)
-    hl = torch.empty(Bt, H, P, N, device=u.device, dtype=torch.float32) if return_state else None
-    dl = torch.empty(Bt, H, device=u.device, dtype=torch.float32) if return_decay else None
+    hl = _out_tensor(state_out, (Bt, H, P, N), u.device, "state_out") if return_state else None
+    dl = _out_tensor(decay_out, (Bt, H), u.device, "decay_out") if return_decay else None
     call("tssm_multihead_ssd", ptr(u), ptr(dt), ptr(A_log), ptr(B), ptr(C), ptr(D), ptr(y), ptr(h0),
          ptr(hl), ptr(dl), Bt, L, H, P, N, _BDISC[bdisc], stream_of(u))
     out = [y]
@@ -419,7 +422,17 @@ def multihead_ssm(u, A_log, B, C, dt, D, BLK_L=256, mode="ssd", bdisc="euler", h
     return out[0] if len(out) == 1 else tuple(out)
 
 
-def _multihead_ssd_pieces(u, A_log, B, C, dt, D, K, bdisc, h0, return_state, y, return_decay):
+def _out_tensor(t, shape, device, name):
+    """A caller-given f32 output (checked) or a new one."""
+    if t is None:
+        return torch.empty(shape, device=device, dtype=torch.float32)
+    if tuple(t.shape) != tuple(shape) or t.dtype != torch.float32 or not t.is_contiguous() or t.device != device:
+        raise ValueError("%s must be a contiguous f32 tensor of shape %s on %s" % (name, tuple(shape), device))
+    return t
+
+
+def _multihead_ssd_pieces(u, A_log, B, C, dt, D, K, bdisc, h0, return_state, y, return_decay, state_out=None,
+                          decay_out=None):
     if K < 1 or h0 is not None:
         raise ValueError("multihead_ssm: pieces must be >= 1 and h0 None when pieces > 1")
     _cuda(u, A_log, B, C, dt, D)
@@ -440,14 +453,14 @@ def _multihead_ssd_pieces(u, A_log, B, C, dt, D, K, bdisc, h0, return_state, y, 
     call("tssm_ssd_carry_fixup_pieces", ptr(S), ptr(d), K, ptr(C), ptr(dt), ptr(A_log), ptr(y), Bt, L, H, P,
          N, stream_of(y))
     out = [y]
-    if return_state:   # the pieces' states chained in order, as the fix-up chains them
-        Sv, dv = S.view(Bt, K, H, P, N), d.view(Bt, K, H)
-        hl = Sv[:, 0].clone()
-        for k in range(1, K):
-            hl = torch.exp2(dv[:, k])[..., None, None] * hl + Sv[:, k]
+    hl = _out_tensor(state_out, (Bt, H, P, N), u.device, "state_out") if return_state else None
+    dl = _out_tensor(decay_out, (Bt, H), u.device, "decay_out") if return_decay else None
+    if return_state or return_decay:   # the pieces chained in order, as the fix-up chains them
+        call("tssm_ssd_pieces_final_state", ptr(S), ptr(d), K, ptr(hl), ptr(dl), Bt, H, P, N, stream_of(y))
+    if return_state:
         out.append(hl)
     if return_decay:
-        out.append(d.view(Bt, K, H).sum(1))
+        out.append(dl)
     return out[0] if len(out) == 1 else tuple(out)
 
 
@@ -470,6 +483,25 @@ def ssd_carry_fixup(S_all, decay_log2_all, rank, C, dt, A_log, y):
             dt.is_contiguous() and y.is_contiguous()):
         raise ValueError("ssd_carry_fixup: tensors must be contiguous")
     call("tssm_ssd_carry_fixup", ptr(S_all), ptr(decay_log2_all), int(rank), R, ptr(C), ptr(dt),
+         ptr(A_log.float().contiguous()), ptr(y), Bt, L, H, P, N, stream_of(y))
+    return y
+
+
+def ssd_carry_fixup_packed(packed, rank, C, dt, A_log, y, P=64):
+    """``ssd_carry_fixup`` reading the slices' carries from one packed buffer
+    [R, Bt*H*P*N + Bt*H] f32, as one all-gather of every rank's
+    [final state | log2 decay] lays them out (``tssm_ssd_carry_fixup_packed``).
+    C [Bt,L,H,N] bf16, dt [Bt,L,H] f32 and y [Bt,L,H*P] bf16 are this rank's
+    slice; y is fixed in place."""
+    _cuda(packed, C, dt, A_log, y)
+    Bt, L, H, N = C.shape
+    R = packed.shape[0]
+    if packed.dim() != 2 or packed.shape[1] != Bt * H * P * N + Bt * H or packed.dtype != torch.float32 or \
+            tuple(dt.shape) != (Bt, L, H) or tuple(y.shape) != (Bt, L, H * P):
+        raise ValueError("ssd_carry_fixup_packed: shape mismatch")
+    if not (packed.is_contiguous() and C.is_contiguous() and dt.is_contiguous() and y.is_contiguous()):
+        raise ValueError("ssd_carry_fixup_packed: tensors must be contiguous")
+    call("tssm_ssd_carry_fixup_packed", ptr(packed), int(rank), R, ptr(C), ptr(dt),
          ptr(A_log.float().contiguous()), ptr(y), Bt, L, H, P, N, stream_of(y))
     return y
 
@@ -554,7 +586,7 @@ def interp_ssm_workspace_bytes(Bt, T, D, L_q, FTILE=128):
 
 
 def fused_interp_ssm(V, M, tau, A_log, B, C, L_q=None, q=None, dt=None, D=None, K=10, FTILE=128,
-                     return_state=False, return_vhat=False, workspace=None):
+                     return_state=False, return_vhat=False, workspace=None, static_scratch=False):
     """Interpolation of irregular observations onto query times fused with an
     N-state diagonal scan (config 3): the composition of
     ``fused_time_aware_interp_kernel`` and the step of
@@ -567,6 +599,10 @@ def fused_interp_ssm(V, M, tau, A_log, B, C, L_q=None, q=None, dt=None, D=None, 
     observations, the reference's own semantics).
     dt [Bt] f32: discretisation step per row; defaults to the regular query spacing.
     Returns y [Bt,L_q,D] f32 (+ h_last [Bt,D,N], + vhat [Bt,L_q,D]).
+    ``static_scratch``: take the scratch from the library's fixed 8 MiB array
+    (``tssm_interp_ssm_static_scratch``) instead of a workspace tensor, for
+    callers that must not allocate device scratch per call; the outputs are
+    still allocated here.  Calls that overlap on the GPU share that array.
     """
     _cuda(V, M, tau, A_log, B, C, q, dt, D)
     _need(V, (torch.float32,), "V")
@@ -596,14 +632,21 @@ def fused_interp_ssm(V, M, tau, A_log, B, C, L_q=None, q=None, dt=None, D=None, 
     D = D.float().contiguous() if D is not None else None
     dt = dt.float().contiguous()
     need = int(_lib.load_library().tssm_interp_ssm_workspace_size(Bt, T, Dm, Lq, int(FTILE)))
-    if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=V.device)
+    if need < 0:
+        raise ValueError("fused_interp_ssm: sizes out of range")
     y = torch.empty(Bt, Lq, Dm, device=V.device, dtype=torch.float32)
     hl = torch.empty(Bt, Dm, N, device=V.device, dtype=torch.float32) if return_state else None
     vh = torch.empty(Bt, Lq, Dm, device=V.device, dtype=torch.float32) if return_vhat else None
-    call("tssm_interp_ssm", ptr(V), ptr(M), ptr(tau), ptr(q), ptr(A_log), ptr(B), ptr(C), ptr(D), ptr(dt),
-         ptr(y), ptr(hl), ptr(vh), ptr(workspace), workspace.numel(), Bt, T, Dm, N, Lq, int(K), int(FTILE),
-         _mask_code(M), stream_of(V))
+    if static_scratch:
+        call("tssm_interp_ssm_static_scratch", ptr(V), ptr(M), ptr(tau), ptr(q), ptr(A_log), ptr(B), ptr(C),
+             ptr(D), ptr(dt), ptr(y), ptr(hl), ptr(vh), Bt, T, Dm, N, Lq, int(K), int(FTILE), _mask_code(M),
+             stream_of(V))
+    else:
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=V.device)
+        call("tssm_interp_ssm", ptr(V), ptr(M), ptr(tau), ptr(q), ptr(A_log), ptr(B), ptr(C), ptr(D), ptr(dt),
+             ptr(y), ptr(hl), ptr(vh), ptr(workspace), workspace.numel(), Bt, T, Dm, N, Lq, int(K), int(FTILE),
+             _mask_code(M), stream_of(V))
     out = [y]
     if return_state:
         out.append(hl)

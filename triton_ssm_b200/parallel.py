@@ -25,16 +25,31 @@ def shard_range(n, rank, world):
     return start, start + base + (1 if rank < rem else 0)
 
 
-def _all_gather_packed(S, d, group):
-    """One all-gather of every rank's (S, d), packed into a single f32 buffer."""
-    world = dist.get_world_size(group)
-    flat = torch.cat([S.reshape(-1), d.reshape(-1)])
-    bufs = [torch.empty_like(flat) for _ in range(world)]
-    dist.all_gather(bufs, flat, group=group)
-    n = S.numel()
-    S_all = torch.stack([b[:n].view_as(S) for b in bufs]).contiguous()
-    d_all = torch.stack([b[n:].view_as(d) for b in bufs]).contiguous()
-    return S_all, d_all
+class _ExchangeBuffers:
+    """Preallocated send and receive buffers of the carry exchange, kept per
+    (device, shape, world): send = this rank's [final state | log2 decay],
+    recv = every rank's, [world, n + m] f32, filled by one all-gather."""
+
+    _cache = {}
+
+    @classmethod
+    def get(cls, device, Bt, H, P, N, world):
+        key = (str(device), Bt, H, P, N, world)
+        buf = cls._cache.get(key)
+        if buf is None:
+            n, m = Bt * H * P * N, Bt * H
+            send = torch.empty(n + m, device=device, dtype=torch.float32)
+            recv = torch.empty(world * (n + m), device=device, dtype=torch.float32)
+            buf = (send, recv, n)
+            cls._cache[key] = buf
+        return buf
+
+
+def exchange_carries(send, recv, group=None):
+    """One all-gather of every rank's packed [state | decay] into ``recv``
+    (flat [world * len(send)] f32); returns the [world, len(send)] view."""
+    dist.all_gather_into_tensor(recv, send, group=group)
+    return recv.view(-1, send.numel())
 
 
 def ssd_local_pieces(Bt, H, L, sms):
@@ -55,7 +70,7 @@ def ssd_local_pieces(Bt, H, L, sms):
 
 
 def ssd_sequence_parallel(x, dt, A_log, B, C, D, group=None, bdisc="euler", y=None,
-                          local_scan=None, fixup=None):
+                          local_scan=None, fixup=None, marks=None):
     """Multi-head scan of a sequence sharded over the ranks of `group`.
 
     x [Bt,Ls,H*P], dt [Bt,Ls,H], B, C [Bt,Ls,H,N] are this rank's slice of the
@@ -63,24 +78,56 @@ def ssd_sequence_parallel(x, dt, A_log, B, C, D, group=None, bdisc="euler", y=No
     Returns this rank's outputs y [Bt,Ls,H*P] — the same values as a scan of
     the whole sequence on one device.
 
+    Steps: the local scan writes the slice's final state and log2 decay
+    straight into a preallocated send buffer; one all-gather
+    (``all_gather_into_tensor``) fills a preallocated [world, n + m] receive
+    buffer; ``ssd_carry_fixup_packed`` reads the carries from it in place.
+
     ``local_scan(x, dt, A_log, B, C, D) -> (y, S, d)`` and
     ``fixup(S_all, d_all, rank, C, dt, A_log, y)`` default to the CUDA
     operators; the multi-process CPU tests substitute the CPU oracle for both
-    to exercise this orchestration over gloo.
+    to exercise this orchestration over gloo.  ``marks``: a list to which a
+    CUDA event recorded after the local scan is appended (the caller times
+    the exchange and fix-up from it).
     """
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     world = dist.get_world_size(group) if dist.is_initialized() else 1
-    if local_scan is None:
-        def local_scan(x, dt, A_log, B, C, D):
-            sms = torch.cuda.get_device_properties(x.device).multi_processor_count
-            K = ssd_local_pieces(x.shape[0], B.shape[2], x.shape[1], sms)
-            return ops.multihead_ssm(x, A_log, B, C, dt, D, bdisc=bdisc, y=y, return_state=True,
-                                     return_decay=True, pieces=K)
-    if fixup is None:
-        fixup = ops.ssd_carry_fixup
+    Bt, Ls, HP = x.shape
+    H, N = B.shape[2], B.shape[3]
+    P = HP // H
+    if local_scan is None and fixup is None:
+        sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+        K = ssd_local_pieces(Bt, H, Ls, sms)
+        if world == 1:
+            yl = ops.multihead_ssm(x, A_log, B, C, dt, D, bdisc=bdisc, y=y, pieces=K)
+            if marks is not None:
+                marks.append(_event())
+            return yl
+        send, recv, n = _ExchangeBuffers.get(x.device, Bt, H, P, N, world)
+        yl, _, _ = ops.multihead_ssm(x, A_log, B, C, dt, D, bdisc=bdisc, y=y, return_state=True,
+                                     return_decay=True, pieces=K, state_out=send[:n].view(Bt, H, P, N),
+                                     decay_out=send[n:].view(Bt, H))
+        if marks is not None:
+            marks.append(_event())
+        packed = exchange_carries(send, recv, group)
+        ops.ssd_carry_fixup_packed(packed, rank, C, dt, A_log, yl, P=P)
+        return yl
+    if local_scan is None or fixup is None:
+        raise ValueError("ssd_sequence_parallel: give both local_scan and fixup, or neither")
     yl, S, d = local_scan(x, dt, A_log, B, C, D)
     if world == 1:
         return yl
-    S_all, d_all = _all_gather_packed(S, d, group)
+    n = S.numel()
+    send = torch.cat([S.reshape(-1), d.reshape(-1)]).float()
+    recv = torch.empty(world * send.numel(), dtype=send.dtype, device=send.device)
+    packed = exchange_carries(send, recv, group)
+    S_all = packed[:, :n].reshape((world,) + tuple(S.shape))
+    d_all = packed[:, n:].reshape((world,) + tuple(d.shape))
     fixup(S_all, d_all, rank, C, dt, A_log, yl)
     return yl
+
+
+def _event():
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record()
+    return ev
