@@ -480,6 +480,16 @@ def run_ours_dtproj(args, rank, world, local):
                  "dt_project_discretize.md", clocks)
 
 
+def _c4_launches(K, world):
+    """Kernels of one config-4 step: the scan; with in-device pieces their
+    fix-up; with more than one rank the pieces' final state (when K > 1) and
+    the slice fix-up (the all-gather is NCCL's)."""
+    n = 1 + (1 if K > 1 else 0)
+    if world > 1:
+        n += (1 if K > 1 else 0) + 1
+    return n
+
+
 def run_ours_c4(args, rank, world, local):
     """Config 4: B4 H32 P64 N128 L=1,048,576 bf16, sequence sharded over the ranks
     (strong scaling): local scan from a zero state, one all-gather of
@@ -528,7 +538,7 @@ def run_ours_c4(args, rank, world, local):
     out = _line(args, world, METRIC, upd / t_step, t_step, "bf16", cfg, alg // world,
                 "ssd_chunk_scan_kernel<128,false> + ssd_carry_fixup_kernel<128>",
                 "ssd_chunk_scan_c4.md" if L == c["L"] else None, clocks,
-                launches=(3 if K > 1 else 1) * args.steps + (1 if world > 1 else 0) * args.steps)
+                launches=_c4_launches(K, world) * args.steps)
     if out["roofline"]["traffic"] is not None and world > 1:
         out["roofline"]["traffic"] //= world
         out["roofline"]["traffic_note"] = "full-size 1-GPU capture divided by the rank count"
