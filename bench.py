@@ -416,6 +416,44 @@ def run_ours_c1bwd(args, rank, world, local):
                  launches=2 * args.steps)
 
 
+def run_ours_disc(args, rank, world, local):
+    """The standalone ZOH discretisation streams at config 1's H' = D*N = 1024
+    (B4 T1024, f32): zoh_discretize (read B, write Abar and Bbar: 12 B per
+    element) and zoh_discretize_bwd (read B, Abar, dAbar, dBbar, write dB: 20 B
+    per element, plus ddt and dA_log), each timed alone as CUDA-graph replays."""
+    import copy
+    import triton_ssm_b200 as ts
+    dev = torch.device("cuda", local)
+    Bt, T, H = args.batch or 4, 1024, 1024
+    g = torch.Generator(device=dev)
+    g.manual_seed(41 + rank)
+    A_log = torch.log(torch.arange(1, 17, device=dev, dtype=torch.float32)).repeat(H // 16)
+    Bc = torch.randn(Bt, T, H, device=dev, generator=g)
+    dt = torch.empty(Bt, T, device=dev).exponential_(1.0, generator=g).clamp_(1e-3, 10.0)
+    Ab, Bb = ts.zoh_discretize(A_log, Bc, dt)
+    dAb = torch.randn(Bt, T, H, device=dev, generator=g)
+    dBb = torch.randn(Bt, T, H, device=dev, generator=g)
+    a = copy.copy(args)
+    a.graph = not args.no_graph
+    t_f, clk_f = _timed(a, world, dev, lambda: ts.zoh_discretize(A_log, Bc, dt, out=(Ab, Bb)))
+    t_b, clk_b = _timed(a, world, dev, lambda: ts.zoh_discretize_bwd(A_log, Bc, dt, Ab, dAb, dBb))
+    n = Bt * T * H
+    alg_f = n * 12 + Bt * T * 4 + H * 4
+    alg_b = n * 20 + Bt * T * 8 + H * 8
+    cfg = {"workload": "zoh_discretize, B%d T%d H%d f32 (config 1's drop-in discretisation)" % (Bt, T, H),
+           "global_batch": Bt * world, "seq_len": T, "parallelism": "batch, %d rank(s)" % world,
+           "timing": "CUDA-graph replays" if a.graph else "eager launches",
+           "l2": "%d MB per step; no flush" % (alg_f // 10**6)}
+    out = _line(a, world, METRIC, world * n / t_f, t_f, "f32", cfg, alg_f, "zoh_discretize_kernel<float,1>", None,
+                clk_f)
+    peak, _ = peaks()
+    out["backward"] = {"ms_per_step": t_b * 1e3, "value": world * n / t_b, "unit": UNIT,
+                       "kernel": "zoh_discretize_bwd_kernel<1> (+ the dA_log clear)",
+                       "algorithmic_bytes_per_launch": alg_b, "achieved_gbs": alg_b / t_b / 1e9,
+                       "frac": alg_b / t_b / 1e9 / peak, "clocks": clk_b}
+    return out
+
+
 def run_ours_ring(args, rank, world, local):
     """Streaming ring-buffer ingest + forward fill + step (race-free
     streaming_interp_then_ssm): S=4096 streams, H=1024 features, K=10 (the
@@ -655,7 +693,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s pre-timing load")
     ap.add_argument("--batch", type=int, default=None, help="override the batch (profiling runs)")
-    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c1bwd", "ring", "dtproj"], default="c2",
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5", "c1bwd", "ring", "dtproj", "disc"], default="c2",
                     help="workload (default c2, the headline; the others are for measurement notes)")
     ap.add_argument("--c1-mode", choices=["pair", "fused", "pool"], default="pair")
     ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays of the step")
@@ -690,7 +728,7 @@ def main():
     try:
         runner = {"c1": run_ours_c1, "c2": run_ours_c2, "c3": run_ours_c3, "c4": run_ours_c4,
                   "c5": run_ours_c5, "c1bwd": run_ours_c1bwd, "ring": run_ours_ring,
-                  "dtproj": run_ours_dtproj}[args.config]
+                  "dtproj": run_ours_dtproj, "disc": run_ours_disc}[args.config]
         out = runner(args, rank, world, local)
         if args.config == "c2" and args.configs != "none":
             out["configs"] = run_sub_configs(args, rank, world, local)

@@ -331,7 +331,7 @@ int launch_ssm_backward_tma(const void* u, const void* A, const void* B, const v
 }
 
 constexpr int DBWD_THREADS = 256;
-constexpr int DBWD_ROWS = 16;   // (b, t) rows per CTA
+constexpr int DBWD_ROWS = 64;   // at most this many (b, t) rows per CTA
 
 // VEC: H % 4 == 0 and 16-byte aligned rows, four channels per thread per pass.
 template <bool VEC>
@@ -343,8 +343,10 @@ __global__ void __launch_bounds__(DBWD_THREADS) zoh_discretize_bwd_kernel(
   constexpr int PER = VEC ? 4 : 1;
   __shared__ float s_ddt[DBWD_ROWS][NWARP];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t r0 = (int64_t)blockIdx.x * DBWD_ROWS;
-  const int nrows = R - r0 < DBWD_ROWS ? (int)(R - r0) : DBWD_ROWS;
+  // an even split of the rows over the grid (a whole number of CTAs per SM, so
+  // every SM streams the same bytes)
+  const int64_t r0 = R * blockIdx.x / gridDim.x;
+  const int nrows = (int)(R * (blockIdx.x + 1) / gridDim.x - r0);
   for (int i = tid; i < DBWD_ROWS * NWARP; i += DBWD_THREADS) (&s_ddt[0][0])[i] = 0.f;
   __syncthreads();
   // Chunks of DBWD_THREADS*PER channels; every thread runs every chunk (the ddt
@@ -505,8 +507,10 @@ extern "C" int tssm_zoh_discretize_bwd(const void* A_log, const void* B, const v
                          : check_launch("zoh_discretize_bwd: clear ddt");
   const bool vec = (H % 4 == 0) && aligned16(B) && aligned16(Abar) && aligned16(dAbar) && aligned16(dBbar) &&
                    aligned16(dB);
-  const unsigned grid = (unsigned)cdiv(R, DBWD_ROWS);
-  TSSM_REQUIRE(cdiv(R, DBWD_ROWS) < (int64_t(1) << 31), "zoh_discretize_bwd: too many rows");
+  // two CTAs per SM, or more when that would put over DBWD_ROWS rows in one CTA
+  const int64_t nct = std::min<int64_t>(R, std::max<int64_t>(2 * num_sms(), cdiv(R, DBWD_ROWS)));
+  TSSM_REQUIRE(nct < (int64_t(1) << 31), "zoh_discretize_bwd: too many rows");
+  const unsigned grid = (unsigned)nct;
   if (vec)
     zoh_discretize_bwd_kernel<true><<<grid, DBWD_THREADS, 0, st>>>(
         (const float*)A_log, (const float*)B, (const float*)dt, (const float*)Abar, (const float*)dAbar,

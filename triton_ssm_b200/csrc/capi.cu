@@ -39,6 +39,14 @@ int* device_status_ptr() {
   return p;
 }
 
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      n < 1)
+    return 1;
+  return n;
+}
+
 // Self-test of the bounded-wait path: one thread waits on an mbarrier phase
 // that nothing completes, with the same helper the pipelined kernels use; the
 // wait gives up after `timeout_ns` and the code is stored in the status word.

@@ -23,6 +23,8 @@ int check_launch(const char* what);
 // Device address of this device's status word (0 = fine); kernels with bounded
 // waits store a non-zero code there when a wait gives up.
 int* device_status_ptr();
+// Streaming multiprocessors of the current device (148 on B200; 1 if the query fails).
+int num_sms();
 
 #define TSSM_REQUIRE(cond, ...)                 \
   do {                                          \

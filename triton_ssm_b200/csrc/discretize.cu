@@ -42,34 +42,17 @@ __device__ __forceinline__ void zoh_one(float a, float ra, float dtv, float bc, 
   bbar = em1 * ra * bc;
 }
 
-// CTA = (ZR consecutive (b, t) rows, 256*W channels): each thread owns W
-// channels (W = 4: one 128-bit / 64-bit vector) and walks the CTA's rows, so
-// the per-channel a = -exp(A_log) is computed once per thread and (b, t) is
-// stepped rather than divided out.
-constexpr int ZR = 8;
+constexpr int ZR = 8;   // rows whose loads one thread has in flight
 
+// ZR rows (nr of them valid) starting at row r0, channels h0 .. h0+W-1 with
+// their a = -exp(A_log) and ra = 1/(a + 1e-12).
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(256) zoh_discretize_kernel(
-    const float* __restrict__ A_log, const T* __restrict__ B, const float* __restrict__ dt,
-    T* __restrict__ Abar, T* __restrict__ Bbar, int64_t Bsz, int64_t Tn, int64_t H,
-    int64_t sBb, int64_t sBt, int64_t sdb, int64_t sdt, int64_t sab, int64_t sat,
-    int64_t sbb, int64_t sbt) {
-  constexpr int W = VEC ? 4 : 1;
-  const int64_t h0 = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * W;
-  const int64_t rows = Bsz * Tn;
-  const int64_t r0 = (int64_t)blockIdx.x * ZR;
-  if (h0 >= H || r0 >= rows) return;
-  float a[W], ra[W];
-  if constexpr (VEC) {
-    const float4 al = __ldg(reinterpret_cast<const float4*>(A_log + h0));
-    a[0] = -expf(al.x); a[1] = -expf(al.y); a[2] = -expf(al.z); a[3] = -expf(al.w);
-  } else {
-    a[0] = -expf(__ldg(A_log + h0));
-  }
-#pragma unroll
-  for (int k = 0; k < W; ++k) ra[k] = 1.0f / (a[k] + 1e-12f);
+__device__ __forceinline__ void zoh_rows(const float (&a)[VEC ? 4 : 1], const float (&ra)[VEC ? 4 : 1],
+                                         const T* __restrict__ B, const float* __restrict__ dt,
+                                         T* __restrict__ Abar, T* __restrict__ Bbar, int64_t Tn, int64_t h0,
+                                         int64_t r0, int nr, int64_t sBb, int64_t sBt, int64_t sdb, int64_t sdt,
+                                         int64_t sab, int64_t sat, int64_t sbb, int64_t sbt) {
   const int64_t b0 = r0 / Tn, t0 = r0 - b0 * Tn;
-  const int nr = (int)min((int64_t)ZR, rows - r0);
   // every row's loads go out first (ZR of them in flight per thread), then the math and stores
   int64_t bs[ZR], ts[ZR];
   {
@@ -123,6 +106,38 @@ __global__ void __launch_bounds__(256) zoh_discretize_kernel(
   }
 }
 
+// CTA = (a contiguous range of (b, t) rows, 256*W channels): each thread owns
+// W channels (W = 4: one 128-bit / 64-bit vector) and walks the range ZR rows
+// at a time, so the per-channel a = -exp(A_log) is computed once per thread and
+// (b, t) is stepped rather than divided out.  The rows are split evenly over a
+// grid of a whole number of CTAs per SM (every SM moves the same bytes: a short
+// stream has no tail of half-empty waves).
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) zoh_discretize_kernel(
+    const float* __restrict__ A_log, const T* __restrict__ B, const float* __restrict__ dt,
+    T* __restrict__ Abar, T* __restrict__ Bbar, int64_t Bsz, int64_t Tn, int64_t H,
+    int64_t sBb, int64_t sBt, int64_t sdb, int64_t sdt, int64_t sab, int64_t sat,
+    int64_t sbb, int64_t sbt) {
+  constexpr int W = VEC ? 4 : 1;
+  const int64_t h0 = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * W;
+  const int64_t rows = Bsz * Tn;
+  const int64_t ra0 = rows * blockIdx.x / gridDim.x, ra1 = rows * (blockIdx.x + 1) / gridDim.x;
+  if (h0 >= H || ra0 >= ra1) return;
+  float a[W], ra[W];
+  if constexpr (VEC) {
+    const float4 al = __ldg(reinterpret_cast<const float4*>(A_log + h0));
+    a[0] = -expf(al.x); a[1] = -expf(al.y); a[2] = -expf(al.z); a[3] = -expf(al.w);
+  } else {
+    a[0] = -expf(__ldg(A_log + h0));
+  }
+#pragma unroll
+  for (int k = 0; k < W; ++k) ra[k] = 1.0f / (a[k] + 1e-12f);
+  for (int64_t r0 = ra0; r0 < ra1; r0 += ZR)
+    zoh_rows<T, VEC>(a, ra, B, dt, Abar, Bbar, Tn, h0, r0, (int)min((int64_t)ZR, ra1 - r0), sBb, sBt, sdb, sdt, sab,
+                     sat, sbb, sbt);
+}
+
 template <typename T>
 int launch(const float* A_log, const T* B, const float* dt, T* Abar, T* Bbar, int64_t Bsz,
            int64_t Tn, int64_t H, int64_t sBb, int64_t sBt, int64_t sdb, int64_t sdt, int64_t sab,
@@ -132,8 +147,10 @@ int launch(const float* A_log, const T* B, const float* dt, T* Abar, T* Bbar, in
   const bool vec = (H % 4 == 0) && sBb % 4 == 0 && sBt % 4 == 0 && sab % 4 == 0 && sat % 4 == 0 &&
                    sbb % 4 == 0 && sbt % 4 == 0 && al(B) && al(Abar) && al(Bbar) && aligned16(A_log);
   if (Bsz * Tn * H == 0) return TSSM_OK;
-  const int64_t gcol = cdiv(vec ? H / 4 : H, 256), grow = cdiv(Bsz * Tn, ZR);
-  TSSM_REQUIRE(gcol <= 65535 && grow <= 0x7fffffff, "zoh_discretize: size exceeds the grid");
+  const int64_t gcol = cdiv(vec ? H / 4 : H, 256);
+  // two 256-thread CTAs per SM per column block, rows split evenly over them
+  const int64_t grow = std::min<int64_t>(cdiv(Bsz * Tn, ZR), std::max<int64_t>(1, 2 * num_sms() / gcol));
+  TSSM_REQUIRE(gcol <= 65535, "zoh_discretize: size exceeds the grid");
   const dim3 grid((unsigned)grow, (unsigned)gcol);
   if (vec)
     zoh_discretize_kernel<T, true><<<grid, 256, 0, st>>>(A_log, B, dt, Abar, Bbar, Bsz, Tn, H, sBb, sBt, sdb, sdt,

@@ -270,13 +270,11 @@ __device__ __forceinline__ void blocked_entry(int p, int n, int c, float w, int 
 }
 
 // Kernel 2: per (tile, b, query slice): last/next flagged index scans in shared
-// memory, then the table.  Per-query form (BLOCKED = false, read by kernel 3):
-// each thread walks a contiguous run of sorted queries with two monotone
-// pointers (lo = #{tau < q}, hi = #{tau <= q}).  Blocked form (read by kernel
-// 3b): one warp per block of WQB queries, one query per lane, binary searches
-// inside the row range that the block's first and last queries bracket.
+// memory, then the per-query table read by kernel 3: each thread walks a
+// contiguous run of sorted queries with two monotone pointers (lo = #{tau < q},
+// hi = #{tau <= q}).  (The blocked table of kernel 3b comes from kernel 2f.)
 constexpr int NB_THREADS = 256;
-template <bool BLOCKED, int NT>
+template <int NT>
 __global__ void __launch_bounds__(NT) interp_neighbors_kernel(const uint8_t* __restrict__ flags,
                                                               const float* __restrict__ tau,
                                                               const float* __restrict__ q, Nbr* __restrict__ tab,
@@ -328,77 +326,6 @@ __global__ void __launch_bounds__(NT) interp_neighbors_kernel(const uint8_t* __r
   __syncthreads();
 
   const float* qb = q ? q + (int64_t)b * Lq : nullptr;
-  if (BLOCKED) {
-    // one warp per block of WQB queries, one query per lane (binary searches)
-    const int nblk = (Lq + WQB - 1) / WQB;
-    int4* outb = reinterpret_cast<int4*>(tab) + ((int64_t)b * ntiles + tile) * nblk * (WQB + 1);
-    const int per_cta = (nblk + gridDim.z - 1) / gridDim.z;
-    const int jb1 = min(nblk, (int)blockIdx.z * per_cta + per_cta);
-    for (int jb = blockIdx.z * per_cta + warp; jb < jb1; jb += NT / 32) {
-      const int j = jb * WQB + lane;
-      int prev = -1, next = -1, cur = -1;
-      float w = 0.f;
-      // [blo, bhi]: rows holding #{tau < q} .. #{tau <= q} of every query of the block
-      int blo = 0, bhi = T;
-      if (qb) {
-        const int jl = min(Lq - 1, jb * WQB + WQB - 1);
-        const float tf = qb[jb * WQB], tl = qb[jl];
-        int l = 0, h = T;
-        const float key = lane == 0 ? tf : tl;   // lane 0: first query, lane 1: last query
-        if (lane < 2) {
-          while (l < h) {
-            const int m = (l + h) >> 1;
-            if (lane == 0 ? stau[m] < key : stau[m] <= key) l = m + 1; else h = m;
-          }
-        }
-        blo = __shfl_sync(0xffffffffu, l, 0);
-        bhi = __shfl_sync(0xffffffffu, l, 1);
-      }
-      if (j < Lq) {
-        float tq;
-        if (!qb) {
-          cur = j;
-          tq = stau[j];
-          if (j >= 1) {
-            const int p = lastf[j - 1];
-            if (p >= 0 && p >= j - K) prev = p;
-          }
-          if (j + 1 < T) {
-            const int n = nextf[j + 1];
-            if (n < T && n <= j + K) next = n;
-          }
-        } else {
-          tq = qb[j];
-          // the block's queries are sorted: its first and last lanes bracket the
-          // row range, every lane then searches inside it
-          int l = blo, h = bhi;
-          while (l < h) { const int m = (l + h) >> 1; if (stau[m] < tq) l = m + 1; else h = m; }
-          const int lo = l;
-          h = bhi;
-          while (l < h) { const int m = (l + h) >> 1; if (stau[m] <= tq) l = m + 1; else h = m; }
-          const int hiq = l;
-          if (hiq > lo) cur = hiq - 1;
-          if (lo >= 1) {
-            const int p = lastf[lo - 1];
-            if (p >= 0 && p >= lo - K) prev = p;
-          }
-          if (hiq < T) {
-            const int n = nextf[hiq];
-            if (n < T && n <= hiq + K - 1) next = n;
-          }
-        }
-        const float tp = prev >= 0 ? stau[prev] : 0.f;
-        const float tn = next >= 0 ? stau[next] : 0.f;
-        w = weight_ref(tq, tp, tn);
-      }
-      // lanes past Lq hold (-1, -1, -1): no operand (a partial block never takes the pair-only path)
-      int4 e, hdr;
-      blocked_entry(prev, next, cur, w, Dm, e, hdr);
-      outb[(int64_t)jb * (WQB + 1) + lane] = e;
-      if (lane == 0) outb[(int64_t)jb * (WQB + 1) + WQB] = hdr;
-    }
-    return;
-  }
   Nbr* out = tab + ((int64_t)b * ntiles + tile) * Lq;
   const int per_cta = (Lq + gridDim.z - 1) / gridDim.z;
   const int qa = blockIdx.z * per_cta, qe = min(Lq, qa + per_cta);
@@ -446,6 +373,202 @@ __global__ void __launch_bounds__(NT) interp_neighbors_kernel(const uint8_t* __r
     const float tp = prev >= 0 ? stau[prev] : 0.f;
     const float tn = next >= 0 ? stau[next] : 0.f;
     out[j] = Nbr{prev, next, cur, weight_ref(tq, tp, tn)};
+  }
+}
+
+// Kernel 2f, the blocked table with the tile flags fused in: CTA = (tile, b, a
+// run of bpc query blocks).  The CTA's queries can reach only the observation
+// rows [lo(first query) - K, hi(last query) + K); it sums the tile's mask over
+// exactly those rows itself (no flags pass over the whole mask, no flags buffer),
+// turns the flags into last / next flagged indices over that window, and writes
+// the blocked entries of its blocks.  U8V: byte mask with 16-byte rows words
+// (FTILE/16 words per tile row, a power of two <= 32), summed with dp4a.
+template <typename M, bool U8V, int NT>
+__global__ void __launch_bounds__(NT) interp_table_kernel(const M* __restrict__ Mk, const float* __restrict__ tau,
+                                                          const float* __restrict__ q, int4* __restrict__ tab, int T,
+                                                          int Lq, int K, int ntiles, int Dm, int FTILE, int bpc) {
+  constexpr int NWARP = NT / 32;
+  extern __shared__ int shi[];
+  float* stau = reinterpret_cast<float*>(shi);   // [T]
+  int* lastf = shi + T;                          // [W] largest flagged row <= w0+i in the window, else -1
+  int* nextf = lastf + T;                        // [W] smallest flagged row >= w0+i in the window, else T
+  __shared__ int s_win[2];
+  __shared__ int agg_l[NWARP], agg_n[NWARP];
+  const int tile = blockIdx.x, b = blockIdx.y;
+  const int nblk = (Lq + WQB - 1) / WQB;
+  const int jb0 = (int)blockIdx.z * bpc, jb1 = min(nblk, jb0 + bpc);
+  if (jb0 >= jb1) return;   // uniform over the CTA
+  const float* tb = tau + (int64_t)b * T;
+  const float* qb = q ? q + (int64_t)b * Lq : nullptr;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < T; i += NT) stau[i] = tb[i];
+  __syncthreads();
+  if (warp == 0) {
+    const int jf = jb0 * WQB, jl = min(Lq, jb1 * WQB) - 1;
+    int w0, w1;
+    if (qb) {
+      const float key = lane == 0 ? qb[jf] : qb[jl];
+      int l = 0, h = T;
+      if (lane < 2) {
+        while (l < h) {
+          const int m = (l + h) >> 1;
+          if (lane == 0 ? stau[m] < key : stau[m] <= key) l = m + 1; else h = m;
+        }
+      }
+      const int lo_f = __shfl_sync(0xffffffffu, l, 0), hi_l = __shfl_sync(0xffffffffu, l, 1);
+      w0 = max(0, lo_f - K);
+      w1 = min(T, hi_l + K);
+    } else {
+      w0 = max(0, jf - K);
+      w1 = min(T, jl + K + 1);
+    }
+    if (lane == 0) {
+      s_win[0] = w0;
+      s_win[1] = max(w0, w1);
+    }
+  }
+  __syncthreads();
+  const int w0 = s_win[0], W = s_win[1] - s_win[0];
+  const int ft0 = tile * FTILE, fn = min(FTILE, Dm - ft0);
+  const M* mrow0 = Mk + ((int64_t)b * T + w0) * Dm + ft0;
+  auto put = [&](int r, bool f) {
+    lastf[r] = f ? w0 + r : -1;
+    nextf[r] = f ? w0 + r : T;
+  };
+  if constexpr (U8V) {
+    // one group of wpt lanes per row, 32/wpt rows per warp step, four steps' loads in flight
+    const int wpt = FTILE / 16, rpw = 32 / wpt, g = lane / wpt, wl = lane - g * wpt;
+    const int step = NWARP * rpw;
+    for (int rb = warp * rpw; rb < W; rb += 4 * step) {
+      uint32_t sum[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = rb + u * step + g;
+        sum[u] = 0;
+        if (r < W) {
+          const uint4 v = __ldcs(reinterpret_cast<const uint4*>(mrow0 + (int64_t)r * Dm) + wl);
+          sum[u] = __dp4a(v.x, 0x01010101u, 0u) + __dp4a(v.y, 0x01010101u, 0u) + __dp4a(v.z, 0x01010101u, 0u) +
+                   __dp4a(v.w, 0x01010101u, 0u);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        for (int o = wpt >> 1; o > 0; o >>= 1) sum[u] += __shfl_xor_sync(0xffffffffu, sum[u], o, wpt);
+        const int r = rb + u * step + g;
+        if (wl == 0 && r < W) put(r, sum[u] > 0);
+      }
+    }
+  } else {
+    for (int rb = warp; rb < W; rb += 4 * NWARP) {
+      float acc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = rb + u * NWARP;
+        acc[u] = 0.f;
+        if (r < W)
+          for (int f = lane; f < fn; f += 32) acc[u] += mval(mrow0 + (int64_t)r * Dm + f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+        const int r = rb + u * NWARP;
+        if (lane == 0 && r < W) put(r, acc[u] > 0.5f);
+      }
+    }
+  }
+  __syncthreads();
+  // prefix max of lastf / suffix min of nextf over the window: per-thread
+  // segments, warp scans of the segment aggregates, per-warp carries
+  const int seg = (W + NT - 1) / NT;
+  const int s0 = min(W, tid * seg), s1 = min(W, s0 + seg);
+  int runl = -1, runn = T;
+  for (int i = s0; i < s1; ++i) runl = max(runl, lastf[i]);
+  for (int i = s1 - 1; i >= s0; --i) runn = min(runn, nextf[i]);
+  int incl_l = runl, incl_n = runn;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int vl = __shfl_up_sync(0xffffffffu, incl_l, o);
+    const int vn = __shfl_down_sync(0xffffffffu, incl_n, o);
+    if (lane >= o) incl_l = max(incl_l, vl);
+    if (lane + o < 32) incl_n = min(incl_n, vn);
+  }
+  if (lane == 31) agg_l[warp] = incl_l;
+  if (lane == 0) agg_n[warp] = incl_n;
+  __syncthreads();
+  int cl = -1, cn = T;
+  for (int w = 0; w < warp; ++w) cl = max(cl, agg_l[w]);
+  for (int w = NWARP - 1; w > warp; --w) cn = min(cn, agg_n[w]);
+  int excl_l = __shfl_up_sync(0xffffffffu, incl_l, 1);
+  int excl_n = __shfl_down_sync(0xffffffffu, incl_n, 1);
+  excl_l = lane == 0 ? cl : max(cl, excl_l);
+  excl_n = lane == 31 ? cn : min(cn, excl_n);
+  runl = excl_l;
+  for (int i = s0; i < s1; ++i) { runl = max(runl, lastf[i]); lastf[i] = runl; }
+  runn = excl_n;
+  for (int i = s1 - 1; i >= s0; --i) { runn = min(runn, nextf[i]); nextf[i] = runn; }
+  __syncthreads();
+
+  // one warp per block of WQB queries, one query per lane; every index that is
+  // looked up below lies inside the window (see the bounds above)
+  int4* outb = tab + ((int64_t)b * ntiles + tile) * nblk * (WQB + 1);
+  for (int jb = jb0 + warp; jb < jb1; jb += NWARP) {
+    const int j = jb * WQB + lane;
+    int prev = -1, next = -1, cur = -1;
+    float w = 0.f;
+    int blo = 0, bhi = T;
+    if (qb) {
+      const int jl = min(Lq - 1, jb * WQB + WQB - 1);
+      const float key = lane == 0 ? qb[jb * WQB] : qb[jl];
+      int l = 0, h = T;
+      if (lane < 2) {
+        while (l < h) {
+          const int m = (l + h) >> 1;
+          if (lane == 0 ? stau[m] < key : stau[m] <= key) l = m + 1; else h = m;
+        }
+      }
+      blo = __shfl_sync(0xffffffffu, l, 0);
+      bhi = __shfl_sync(0xffffffffu, l, 1);
+    }
+    if (j < Lq) {
+      float tq;
+      if (!qb) {
+        cur = j;
+        tq = stau[j];
+        if (j >= 1) {
+          const int p = lastf[j - 1 - w0];
+          if (p >= 0 && p >= j - K) prev = p;
+        }
+        if (j + 1 < T) {
+          const int n = nextf[j + 1 - w0];
+          if (n < T && n <= j + K) next = n;
+        }
+      } else {
+        tq = qb[j];
+        int l = blo, h = bhi;
+        while (l < h) { const int m = (l + h) >> 1; if (stau[m] < tq) l = m + 1; else h = m; }
+        const int lo = l;
+        h = bhi;
+        while (l < h) { const int m = (l + h) >> 1; if (stau[m] <= tq) l = m + 1; else h = m; }
+        const int hiq = l;
+        if (hiq > lo) cur = hiq - 1;
+        if (lo >= 1) {
+          const int p = lastf[lo - 1 - w0];
+          if (p >= 0 && p >= lo - K) prev = p;
+        }
+        if (hiq < T) {
+          const int n = nextf[hiq - w0];
+          if (n < T && n <= hiq + K - 1) next = n;
+        }
+      }
+      const float tp = prev >= 0 ? stau[prev] : 0.f;
+      const float tn = next >= 0 ? stau[next] : 0.f;
+      w = weight_ref(tq, tp, tn);
+    }
+    int4 e, hdr;
+    blocked_entry(prev, next, cur, w, Dm, e, hdr);
+    outb[(int64_t)jb * (WQB + 1) + lane] = e;
+    if (lane == 0) outb[(int64_t)jb * (WQB + 1) + WQB] = hdr;
   }
 }
 
@@ -1147,7 +1270,34 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
   // N <= 16 with whole 32-feature runs per tile: blocked table + chunked scan
   const bool chunked = N <= 16 && Dm % 32 == 0 && FTILE % 32 == 0 && T * Dm < (int64_t(1) << 31) && aligned16(V);
   const size_t nb_shm = (size_t)T * 12;
-  {
+  if (chunked) {
+    // flags and the blocked table in one launch, about four CTAs per SM
+    const int nblk = (int)cdiv(Lq, WQB);
+    const int64_t want = cdiv(4 * (int64_t)num_sms(), Bsz * ntiles);
+    const int qsplit = (int)std::max<int64_t>(1, std::min<int64_t>(nblk, want));
+    const int bpc = (int)cdiv(nblk, qsplit);
+    const int nz = (int)cdiv(nblk, bpc);
+    TSSM_REQUIRE(ntiles <= 65535 && nz <= 65535, "interp_ssm: size exceeds the grid");
+    const dim3 grid((unsigned)ntiles, (unsigned)Bsz, (unsigned)nz);
+#define TABLE_LAUNCH(MT, U8V)                                                                                   \
+  do {                                                                                                          \
+    auto kern = interp_table_kernel<MT, U8V, NB_THREADS>;                                                       \
+    if (nb_shm > 48 * 1024 &&                                                                                   \
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nb_shm) != cudaSuccess)    \
+      return check_launch("interp_ssm: table smem");                                                            \
+    kern<<<grid, NB_THREADS, nb_shm, st>>>((const MT*)Mk, (const float*)tau, (const float*)q,                  \
+                                           reinterpret_cast<int4*>(tab), (int)T, (int)Lq, (int)K, ntiles,       \
+                                           (int)Dm, (int)FTILE, bpc);                                           \
+  } while (0)
+    if (vec) TABLE_LAUNCH(uint8_t, true);
+    else if (m_dtype == TSSM_U8) TABLE_LAUNCH(uint8_t, false);
+    else if (m_dtype == TSSM_F32) TABLE_LAUNCH(float, false);
+    else {
+      set_error("interp_ssm: mask dtype must be u8 or f32");
+      return TSSM_ERR_INVALID;
+    }
+#undef TABLE_LAUNCH
+  } else {
     const int64_t rows = T * ntiles;   // one warp per (t, tile) row, 8 warps per block
     dim3 grid((unsigned)std::max<int64_t>(1, cdiv(rows, 8)), (unsigned)Bsz);
     if (vec) {
@@ -1162,7 +1312,7 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       set_error("interp_ssm: mask dtype must be u8 or f32");
       return TSSM_ERR_INVALID;
     }
-    auto nk = chunked ? interp_neighbors_kernel<true, NB_THREADS> : interp_neighbors_kernel<false, NB_THREADS>;
+    auto nk = interp_neighbors_kernel<NB_THREADS>;
     if (nb_shm > 48 * 1024 &&
         cudaFuncSetAttribute(nk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nb_shm) != cudaSuccess)
       return check_launch("interp_ssm: neighbour smem");
