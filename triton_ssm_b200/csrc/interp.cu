@@ -34,6 +34,7 @@ __device__ unsigned long long g_interp_trace[128 * 8];
   } while (0)
 #endif
 namespace {
+int getenv_int(const char* k, int d) { const char* v = getenv(k); return v ? atoi(v) : d; }
 using sm100::named_bar_arrive;
 using sm100::named_bar_sync;
 
@@ -1189,6 +1190,15 @@ struct alignas(128) PairSmem {
   uint64_t rbar[PRB];
 };
 
+// The interpolated pair round((1-w)*vp) + round(w*vn), each product and the
+// sum rounded separately as the reference does (scalar IEEE operations: the
+// packed forms may be contracted into a fused multiply-add).
+__device__ __forceinline__ float2 lerp2(int4 x, float2 vp, float2 vn) {
+  const float om = __int_as_float(x.w), w = __int_as_float(x.z);
+  return make_float2(__fadd_rn(__fmul_rn(om, vp.x), __fmul_rn(w, vn.x)),
+                     __fadd_rn(__fmul_rn(om, vp.y), __fmul_rn(w, vn.y)));
+}
+
 template <int NS, bool VHAT>
 __global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
     const __grid_constant__ CUtensorMap tmV, const float* __restrict__ Vp, const int4* __restrict__ tabq,
@@ -1303,29 +1313,23 @@ __global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
     ++r_issued;
     return true;
   };
-  // readout of the state after the previous query (two chains of NS/2), then
-  // the update by this query's pair of values
-  auto readout_update = [&](float2 v2) -> float2 {
-    float2 acc0 = fmul2(c2[0], g2[0]);
-    float2 acc1 = NS > 1 ? fmul2(c2[1], g2[1]) : make_float2(0.f, 0.f);
+  // readout of the current state: four independent chains of NS/4 packed FMAs
+  // (a short dependent path), summed pairwise
+  auto readout = [&]() -> float2 {
+    float2 acc[4];
 #pragma unroll
-    for (int k = 2; k < NS; ++k) {
-      if (k & 1) acc1 = ffma2(c2[k], g2[k], acc1);
-      else acc0 = ffma2(c2[k], g2[k], acc0);
-    }
+    for (int c = 0; c < 4; ++c) acc[c] = c < NS ? fmul2(c2[c], g2[c]) : make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 4; k < NS; ++k) acc[k & 3] = ffma2(c2[k], g2[k], acc[k & 3]);
+    return fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+  };
+  // readout of the state after the previous query, then the update by this
+  // query's pair of values
+  auto readout_update = [&](float2 v2) -> float2 {
+    const float2 r = readout();
 #pragma unroll
     for (int k = 0; k < NS; ++k) g2[k] = ffma2(a2[k], g2[k], v2);
-    return fadd2(acc0, acc1);
-  };
-  auto readout = [&]() -> float2 {
-    float2 acc0 = fmul2(c2[0], g2[0]);
-    float2 acc1 = NS > 1 ? fmul2(c2[1], g2[1]) : make_float2(0.f, 0.f);
-#pragma unroll
-    for (int k = 2; k < NS; ++k) {
-      if (k & 1) acc1 = ffma2(c2[k], g2[k], acc1);
-      else acc0 = ffma2(c2[k], g2[k], acc0);
-    }
-    return fadd2(acc0, acc1);
+    return r;
   };
   auto run_block = [&](int i, bool out) {
     const int j = js + i;
@@ -1339,18 +1343,27 @@ __global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
     const int64_t rs = Dm / 2;   // one query row, in float2
     float2 vprev = make_float2(0.f, 0.f);
     if (out && nq == WQB && !direct) {
+      // groups of four queries; the next group's entries and operands are loaded
+      // while this group computes
+      int4 xn[4];
+      float2 vpn[4], vnn[4];
+      auto load_group = [&](int g0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) xn[u] = e[g0 + u];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { vpn[u] = rw[xn[u].x]; vnn[u] = rw[xn[u].y]; }
+      };
+      load_group(0);
 #pragma unroll 1
       for (int g0 = 0; g0 < WQB; g0 += 4) {
         int4 x[4];
         float2 vp[4], vn[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = e[g0 + u];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) { vp[u] = rw[x[u].x]; vn[u] = rw[x[u].y]; }
+        for (int u = 0; u < 4; ++u) { x[u] = xn[u]; vp[u] = vpn[u]; vn[u] = vnn[u]; }
+        if (g0 + 4 < WQB) load_group(g0 + 4);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const float om = __int_as_float(x[u].w), w = __int_as_float(x[u].z);
-          const float2 v = fadd2(fmul2(make_float2(om, om), vp[u]), fmul2(make_float2(w, w), vn[u]));
+          const float2 v = lerp2(x[u], vp[u], vn[u]);
           const float2 acc = readout_update(v);
           if (u > 0 || g0 > 0) {
             yrow[(int64_t)(g0 + u - 1) * rs] = ffma2(dsk2, vprev, acc);
@@ -1371,8 +1384,7 @@ __global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
           vp = x.x >= 0 ? *reinterpret_cast<const float2*>(Vb + x.x) : make_float2(0.f, 0.f);
           vn = x.y >= 0 ? *reinterpret_cast<const float2*>(Vb + x.y) : make_float2(0.f, 0.f);
         }
-        const float om = __int_as_float(x.w), w = __int_as_float(x.z);
-        const float2 v = fadd2(fmul2(make_float2(om, om), vp), fmul2(make_float2(w, w), vn));
+        const float2 v = lerp2(x, vp, vn);
         if (out) {
           const float2 acc = readout_update(v);
           if (qq > 0) {
@@ -1395,12 +1407,16 @@ __global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
   for (int i = 0; i < min(nb, PTS - 1); ++i) issue_table(i);
   if (stage_rows(0)) {
     for (int i = 0; i < nb; ++i) {
+      IT_TRACE(i, 0);
       __syncwarp();   // block i-1's rows and entries were read by every lane
       if (i + PTS - 1 < nb) issue_table(i + PTS - 1);
       if (i + 1 < nb && !stage_rows(i + 1)) break;
+      IT_TRACE(i, 1);
       if (!wait_bar(&S.rbar[i % PRB], i / PRB, 9312)) break;
+      IT_TRACE(i, 2);
       ++r_done;
       run_block(i, js + i >= jo);
+      IT_TRACE(i, 3);
     }
   }
   if (!alive) {
@@ -1611,7 +1627,7 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       const int64_t groups = Bsz * (Dm / PF);
       const int nch = (int)std::max<int64_t>(1, std::min<int64_t>(nblk / 16, cdiv(7 * (int64_t)num_sms(), groups)));
       TSSM_REQUIRE(groups * nch < (int64_t(1) << 31), "interp_ssm: size exceeds the grid");
-      const size_t pshm = sizeof(PairSmem) + 128;
+      const size_t pshm = std::max<size_t>(sizeof(PairSmem) + 128, (size_t)getenv_int("TSSM_PAIR_SMEM", 0));
 #define PAIR_LAUNCH(NS, VH)                                                                                     \
   do {                                                                                                          \
     auto kern = interp_ssm_scan_pair_kernel<NS, VH>;                                                           \
