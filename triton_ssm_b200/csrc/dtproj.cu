@@ -6,7 +6,8 @@
 // and, fused, with one dt per (b, t, h) (the selective form of
 // discretize_kernel.py:38-54):
 //   Abar = exp(dt a), Bbar = expm1*(dt a) / (a + 1e-12) B,  a = -exp(A_log[h]).
-// A CTA computes a [32 rows x 128 channels] tile: W's 128-column slab and the
+// The tensor-core kernel (dtproj_tc.cu) takes the shapes it supports; the
+// CUDA-core kernel below takes the rest.  A CTA computes a [32 rows x 128 channels] tile: W's 128-column slab and the
 // 32 rows of dt_raw sit in shared memory, each thread accumulates 4 rows x 4
 // channels over r in the reference's order (one fma per r, two channels per
 // packed f32x2 instruction), and the epilogue writes dt, or Abar and Bbar,
@@ -126,10 +127,22 @@ __global__ void __launch_bounds__(DTP_THREADS) dt_project_kernel(
   }
 }
 
+}  // namespace
+
+// dtproj_tc.cu: the same arithmetic with the contraction on tcgen05 tensor cores
+// (TSSM_ERR_UNSUPPORTED when its size and alignment conditions do not hold).
+int launch_dtproj_tc(bool disc, const void* dt_raw, const void* W, const void* bias, const void* A_log, const void* B,
+                     void* dt_out, void* Abar, void* Bbar, int64_t rows, int64_t H, int64_t R, double dt_min,
+                     double dt_max, cudaStream_t st);
+
+namespace {
+
 template <bool DISC>
 int launch_dtproj(const void* dt_raw, const void* W, const void* bias, const void* A_log, const void* B, void* dt_out,
                   void* Abar, void* Bbar, int64_t rows, int64_t H, int64_t R, double dt_min, double dt_max,
                   cudaStream_t st) {
+  const int tc = launch_dtproj_tc(DISC, dt_raw, W, bias, A_log, B, dt_out, Abar, Bbar, rows, H, R, dt_min, dt_max, st);
+  if (tc != TSSM_ERR_UNSUPPORTED) return tc;
   const size_t R4 = (size_t)((R + 3) & ~3);
   const size_t smem = (R4 * DTP_HT + (size_t)DTP_RB * (R4 + 4)) * sizeof(float);
   const bool vec = H % 4 == 0 && (!dt_out || aligned16(dt_out)) &&

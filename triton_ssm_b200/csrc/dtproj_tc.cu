@@ -1,0 +1,331 @@
+// Delta-t projection on tcgen05 tensor cores, alone (dt_project_softplus_kernel,
+// discretize_kernel.py:165-213) and fused into the ZOH discretisation with one
+// dt per (b, t, h) (discretize_kernel.py:38-54).
+//
+//   acc = dt_raw W + bias,  dt = clamp(log(1 + exp(acc)), dt_min, dt_max)
+//   Abar = exp(dt a), Bbar = expm1*(dt a) / (a + 1e-12) B,  a = -exp(A_log[h])
+//
+// The contraction dt_raw [rows x R] . W [R x H] (R <= 64) is a dense GEMM: it
+// runs as [128 rows x 64 channels] tiles of kind::tf32 MMAs with f32
+// accumulators in TMEM.  tf32 keeps 11 bits of each operand, so every operand
+// is split exactly into hi = tf32(x) and lo = x - hi, and the tile is the sum of
+// the three products hi.hi + hi.lo + lo.hi (the dropped lo.lo term is below
+// 2^-22 of each product: f32-accurate, as the 1e-4 parity bar needs).
+//
+// Persistent CTAs (one per SM) walk a contiguous range of tiles, channels
+// fastest, so a 128-row block of dt_raw is loaded and split once per 16
+// channel tiles.  Roles:
+//   warp 4, one thread: TMA loads of the dt_raw block, the W slab and (fused
+//     form) the B tile one tile ahead, and the 24 MMAs of each tile into one of
+//     two TMEM accumulators;
+//   warps 0-3 (one thread per tile row): the hi/lo split of each newly loaded
+//     operand, then the epilogue of the previous MMAs -- bias, softplus, clamp,
+//     the ZOH arithmetic against the swizzled B tile -- into 128B-swizzled
+//     staging tiles that TMA stores write out (two staging buffers, so one
+//     store drains while the next half-tile is computed).
+// Every mbarrier wait is bounded; a wait that gives up sets the device status
+// word and every role leaves its loop; the CTA drains its MMAs, loads and
+// stores (bounded) and frees TMEM before it exits.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+#include "tmap.cuh"
+
+namespace tssm {
+namespace {
+using namespace sm100;
+
+constexpr int TM = 128;                     // rows per tile (the MMA's M)
+constexpr int TN = 64;                      // channels per tile (the MMA's N)
+constexpr int KM = 64;                      // largest dt_rank on this path
+constexpr int NEPI = 128;                   // epilogue threads, one per tile row
+constexpr int NTHR = NEPI + 32;             // + the load / MMA warp
+constexpr uint32_t A_PART = TM * KM * 4;    // 32 KB: two [128 rows x 128 B] K atoms
+constexpr uint32_t W_PART = KM * TN * 4;    // 16 KB: two [64 K-rows x 128 B] channel blocks (MN-major)
+constexpr uint32_t HALF = TM * 32 * 4;      // 16 KB: one [128 x 32] f32 tile, 128B swizzle
+constexpr uint32_t OFF_AHI = 0;
+constexpr uint32_t OFF_ALO = OFF_AHI + A_PART;
+constexpr uint32_t OFF_WHI = OFF_ALO + A_PART;
+constexpr uint32_t OFF_WLO = OFF_WHI + W_PART;
+constexpr uint32_t OFF_B = OFF_WLO + W_PART;        // [2 buffers][2 halves] of the B tile
+constexpr uint32_t OFF_O = OFF_B + 4 * HALF;         // [2 staging buffers][out0 half, out1 half]
+constexpr uint32_t OFF_COL = OFF_O + 4 * HALF;       // [2][3][TN]: bias, a, 1/(a + 1e-12)
+constexpr uint32_t OFF_BAR = OFF_COL + 2 * 3 * TN * 4;
+constexpr int NBAR = 10;
+constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;   // + slack to align the base to 1024
+static_assert(SMEM_BYTES <= 232448, "dt-projection shared-memory layout exceeds the per-CTA limit");
+constexpr uint32_t TMEM_COLS = 2 * TN;
+
+// Nearest tf32 (the low 13 mantissa bits cleared); x - tf32(x) is exact in f32.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+__device__ __forceinline__ void split4(float4* hi_inout, float4* lo_out) {
+  const float4 x = *hi_inout;
+  const float4 h = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+  *lo_out = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+  *hi_inout = h;
+}
+
+template <bool DISC>
+__global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
+    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmO0,
+    const __grid_constant__ CUtensorMap tmO1, const float* __restrict__ bias, const float* __restrict__ A_log,
+    int* __restrict__ status, int H, int R, float dt_min, float dt_max, int ntn, int nitems) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* barA = bars + 0;       // dt_raw block landed
+  uint64_t* barW = bars + 1;       // W slab landed
+  uint64_t* barB = bars + 2;       // [2] B tile landed
+  uint64_t* barSplit = bars + 4;   // hi/lo split and channel constants written (NEPI arrivals)
+  uint64_t* barMMA = bars + 5;     // [2] the tile's MMAs completed
+  uint64_t* barFree = bars + 7;    // [2] epilogue done with that TMEM accumulator and B buffer (NEPI arrivals)
+  uint64_t* barDrain = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+  const int per = (nitems + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int it0 = (int)blockIdx.x * per, it1 = min(nitems, it0 + per);
+
+  if (tid == 0) {
+    mbar_init(barA, 1);
+    mbar_init(barW, 1);
+    mbar_init(&barB[0], 1);
+    mbar_init(&barB[1], 1);
+    mbar_init(barSplit, NEPI);
+    mbar_init(&barMMA[0], 1);
+    mbar_init(&barMMA[1], 1);
+    mbar_init(&barFree[0], NEPI);
+    mbar_init(&barFree[1], NEPI);
+    mbar_init(barDrain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+    if (mbar_wait(bar, parity, abort_flag)) return true;
+    if (!*abort_flag) {
+      *abort_flag = 1;
+      atomicExch(status, code);
+    }
+    return false;
+  };
+
+  if (warp == 4) {
+    // ============================================================ loads and MMAs
+    if (lane == 0 && it0 < it1) {
+      prefetch_tmap(&tmX);
+      prefetch_tmap(&tmW);
+      if (DISC) prefetch_tmap(&tmB);
+      constexpr uint32_t ID = make_idesc_tf32(TM, TN, false, true);
+      const int nks = (R + 7) / 8;   // K steps of 8 (zero-filled past R)
+      int last_m = -1, a_armed = 0, w_armed = 0, b_armed[2] = {0, 0};
+      bool ok = true;
+      for (int it = it0; it < it1; ++it) {
+        const int j = it - it0, s = j & 1;
+        const int m = it / ntn, n = it - m * ntn, m0 = m * TM, n0 = n * TN;
+        // this buffer's previous user (tile j-2) released its B tile and accumulator
+        if (j >= 2 && !(ok = wait(&barFree[s], ((j - 2) >> 1) & 1, 9501))) break;
+        if (DISC) {
+          mbar_arrive_expect_tx(&barB[s], 2 * HALF);
+          tma_load_2d(smem + OFF_B + s * 2 * HALF, &tmB, n0, m0, &barB[s]);
+          tma_load_2d(smem + OFF_B + s * 2 * HALF + HALF, &tmB, n0 + 32, m0, &barB[s]);
+          ++b_armed[s];
+        }
+        // the previous tile's MMAs are the last readers of the operand buffers
+        if (j >= 1 && !(ok = wait(&barMMA[(j - 1) & 1], ((j - 1) >> 1) & 1, 9502))) break;
+        if (m != last_m) {
+          mbar_arrive_expect_tx(barA, A_PART);
+          tma_load_2d(smem + OFF_AHI, &tmX, 0, m0, barA);
+          tma_load_2d(smem + OFF_AHI + A_PART / 2, &tmX, 32, m0, barA);
+          ++a_armed;
+          last_m = m;
+        }
+        mbar_arrive_expect_tx(barW, W_PART);
+        tma_load_2d(smem + OFF_WHI, &tmW, n0, 0, barW);
+        tma_load_2d(smem + OFF_WHI + W_PART / 2, &tmW, n0 + 32, 0, barW);
+        ++w_armed;
+        if (!(ok = wait(barSplit, j & 1, 9503))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(s * TN);
+        const uint64_t dAhi = make_desc_sw128(smem_u32(smem + OFF_AHI), 16);
+        const uint64_t dAlo = make_desc_sw128(smem_u32(smem + OFF_ALO), 16);
+        const uint64_t dWhi = make_desc_sw128(smem_u32(smem + OFF_WHI), W_PART / 2);
+        const uint64_t dWlo = make_desc_sw128(smem_u32(smem + OFF_WLO), W_PART / 2);
+#pragma unroll 1
+        for (int p = 0; p < 3; ++p) {
+          const uint64_t a = p == 2 ? dAlo : dAhi, w = p == 1 ? dWlo : dWhi;
+#pragma unroll 1
+          for (int ks = 0; ks < nks; ++ks) {
+            // A (K-major): 32 B per K step inside a 128-byte row, 16 KB per 32-wide K atom;
+            // W (MN-major): one 8-row (1024 B) group per K step
+            const uint64_t ad = a + (uint64_t)(((ks >> 2) * (A_PART / 2) + (ks & 3) * 32) >> 4);
+            const uint64_t wd = w + (uint64_t)((ks * 1024) >> 4);
+            umma_tf32(d, ad, wd, ID, (p | ks) != 0);
+          }
+        }
+        umma_commit(&barMMA[s]);
+      }
+      // this thread's MMAs complete before teardown; after a failed wait, the loads it
+      // armed complete too (every wait below is bounded)
+      umma_commit(barDrain);
+      mbar_wait(barDrain, 0, nullptr, 100000000ull);
+      if (!ok) {
+        if (a_armed) mbar_wait(barA, (a_armed - 1) & 1, nullptr, 100000000ull);
+        if (w_armed) mbar_wait(barW, (w_armed - 1) & 1, nullptr, 100000000ull);
+        for (int b = 0; b < 2; ++b)
+          if (b_armed[b]) mbar_wait(&barB[b], (b_armed[b] - 1) & 1, nullptr, 100000000ull);
+      }
+    }
+  } else {
+    // ============================================================ split + epilogue (one row per thread)
+    int last_m = -1, a_seen = 0;
+    const int r = tid;
+    for (int it = it0; it < it1; ++it) {
+      const int j = it - it0, s = j & 1;
+      const int m = it / ntn, n = it - m * ntn, m0 = m * TM, n0 = n * TN;
+      if (m != last_m) {
+        if (!wait(barA, a_seen & 1, 9511)) break;
+        ++a_seen;
+        last_m = m;
+        float4* hi = reinterpret_cast<float4*>(smem + OFF_AHI);
+        float4* lo = reinterpret_cast<float4*>(smem + OFF_ALO);
+#pragma unroll 4
+        for (int k = 0; k < (int)(A_PART / 16 / NEPI); ++k) split4(hi + tid + k * NEPI, lo + tid + k * NEPI);
+      }
+      if (!wait(barW, j & 1, 9512)) break;
+      {
+        float4* hi = reinterpret_cast<float4*>(smem + OFF_WHI);
+        float4* lo = reinterpret_cast<float4*>(smem + OFF_WLO);
+#pragma unroll
+        for (int k = 0; k < (int)(W_PART / 16 / NEPI); ++k) split4(hi + tid + k * NEPI, lo + tid + k * NEPI);
+      }
+      float* col = reinterpret_cast<float*>(smem + OFF_COL) + s * 3 * TN;
+      if (tid < TN) {
+        const int h = n0 + tid;
+        col[tid] = h < H ? bias[h] : 0.f;
+        if (DISC) {
+          const float a = h < H ? -expf(A_log[h]) : -1.f;
+          col[TN + tid] = a;
+          col[2 * TN + tid] = 1.0f / (a + 1e-12f);
+        }
+      }
+      fence_proxy_async_smem();   // the split tiles are read by the tensor core (async proxy)
+      named_bar_sync(2, NEPI);    // channel constants visible to every epilogue thread
+      mbar_arrive(barSplit);
+      if (!wait(&barMMA[s], (j >> 1) & 1, 9513)) break;
+      tc_fence_after();
+      if (DISC && !wait(&barB[s], (j >> 1) & 1, 9514)) break;
+      const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(s * TN);
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        float acc[32];
+        tmem_ld32(trow + (uint32_t)(hf * 32), acc);
+        tmem_wait_ld();
+        // staging buffer hf was last stored from one tile ago: that store has read it
+        if (tid == 0) bulk_wait_read<1>();
+        named_bar_sync(1, NEPI);
+        uint8_t* o0 = smem + OFF_O + hf * 2 * HALF;
+        uint8_t* o1 = o0 + HALF;
+        const uint8_t* bt = smem + OFF_B + s * 2 * HALF + hf * HALF;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t off = (uint32_t)r * 128u + ((((uint32_t)q ^ ((uint32_t)r & 7u)) & 7u) << 4);
+          float bv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (DISC) {
+            const float4 t = *reinterpret_cast<const float4*>(bt + off);
+            bv[0] = t.x; bv[1] = t.y; bv[2] = t.z; bv[3] = t.w;
+          }
+          float y0[4], y1[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = hf * 32 + q * 4 + e;
+            const float v = acc[q * 4 + e] + col[c];
+            const float dtv = fminf(fmaxf(logf(1.0f + expf(v)), dt_min), dt_max);
+            if (DISC) {
+              const float x = dtv * col[TN + c];
+              const float ex = expf(x);
+              y0[e] = ex;
+              y1[e] = expm1_guard_f32(x, ex) * col[2 * TN + c] * bv[e];
+            } else {
+              y0[e] = dtv;
+              y1[e] = 0.f;
+            }
+          }
+          *reinterpret_cast<float4*>(o0 + off) = make_float4(y0[0], y0[1], y0[2], y0[3]);
+          if (DISC) *reinterpret_cast<float4*>(o1 + off) = make_float4(y1[0], y1[1], y1[2], y1[3]);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, NEPI);
+        if (tid == 0) {
+          tma_store_2d(&tmO0, o0, n0 + 32 * hf, m0);
+          if (DISC) tma_store_2d(&tmO1, o1, n0 + 32 * hf, m0);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&barFree[s]);
+    }
+    if (tid == 0) bulk_wait<0>();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+// The tensor-core path: R <= 64, rows of dt_raw, W, B and the outputs 16-byte
+// aligned (R % 4 == 0, H % 4 == 0, 16-byte aligned bases), and no dt output in
+// the fused form.  Returns TSSM_ERR_UNSUPPORTED when those do not hold, so the
+// caller takes the CUDA-core kernel instead.
+int launch_dtproj_tc(bool disc, const void* dt_raw, const void* W, const void* bias, const void* A_log, const void* B,
+                     void* dt_out, void* Abar, void* Bbar, int64_t rows, int64_t H, int64_t R, double dt_min,
+                     double dt_max, cudaStream_t st) {
+  if (R > KM || R % 4 || H % 4 || (disc && dt_out) || !aligned16(dt_raw) || !aligned16(W) ||
+      (disc ? !(aligned16(B) && aligned16(Abar) && aligned16(Bbar)) : !aligned16(dt_out)) ||
+      rows >= (int64_t(1) << 31) || H >= (int64_t(1) << 31))
+    return TSSM_ERR_UNSUPPORTED;
+  if (getenv("TSSM_DTPROJ_CUDA_CORES")) return TSSM_ERR_UNSUPPORTED;
+  int* status = device_status_ptr();
+  if (!status) {
+    set_error("dt_project: device status word unavailable");
+    return TSSM_ERR_CUDA;
+  }
+  CUtensorMap mX, mW, mB, mO0, mO1;
+  void* o0 = disc ? Abar : dt_out;
+  void* o1 = disc ? Bbar : dt_out;
+  const void* bsrc = disc ? B : dt_out;
+  if (!tmap2d_f32_sw128(&mX, dt_raw, (uint64_t)R, (uint64_t)rows, TM) ||
+      !tmap2d_f32_sw128(&mW, W, (uint64_t)H, (uint64_t)R, KM) ||
+      !tmap2d_f32_sw128(&mB, bsrc, (uint64_t)H, (uint64_t)rows, TM) ||
+      !tmap2d_f32_sw128(&mO0, o0, (uint64_t)H, (uint64_t)rows, TM) ||
+      !tmap2d_f32_sw128(&mO1, o1, (uint64_t)H, (uint64_t)rows, TM)) {
+    return TSSM_ERR_UNSUPPORTED;   // e.g. a tensor narrower than one box: the CUDA-core kernel takes it
+  }
+  const int64_t ntm = cdiv(rows, TM), ntn = cdiv(H, TN), nitems = ntm * ntn;
+  TSSM_REQUIRE(nitems < (int64_t(1) << 31), "dt_project: size exceeds the grid");
+  const int grid = (int)std::min<int64_t>(nitems, num_sms());
+  auto kern = disc ? dtproj_tc_kernel<true> : dtproj_tc_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
+    return check_launch("dt_project: set smem attribute");
+  kern<<<grid, NTHR, SMEM_BYTES, st>>>(mX, mW, mB, mO0, mO1, (const float*)bias, (const float*)A_log, status,
+                                       (int)H, (int)R, (float)dt_min, (float)dt_max, (int)ntn, (int)nitems);
+  return check_launch(disc ? "zoh_discretize_dtproj" : "dt_project_softplus");
+}
+
+}  // namespace tssm
