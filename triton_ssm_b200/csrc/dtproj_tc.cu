@@ -19,7 +19,7 @@
 //     form) the B tile one tile ahead, and the 24 MMAs of each tile into one of
 //     two TMEM accumulators;
 //   warps 0-3 (one thread per tile row): the hi/lo split of each newly loaded
-//     operand, then the epilogue of the previous MMAs -- bias, softplus, clamp,
+//     operand (W transposed to K-major on the way), then the epilogue of the previous MMAs -- bias, softplus, clamp,
 //     the ZOH arithmetic against the swizzled B tile -- into 128B-swizzled
 //     staging tiles that TMA stores write out (two staging buffers, so one
 //     store drains while the next half-tile is computed).
@@ -42,7 +42,7 @@ constexpr int KM = 64;                      // largest dt_rank on this path
 constexpr int NEPI = 128;                   // epilogue threads, one per tile row
 constexpr int NTHR = NEPI + 32;             // + the load / MMA warp
 constexpr uint32_t A_PART = TM * KM * 4;    // 32 KB: two [128 rows x 128 B] K atoms
-constexpr uint32_t W_PART = KM * TN * 4;    // 16 KB: two [64 K-rows x 128 B] channel blocks (MN-major)
+constexpr uint32_t W_PART = KM * TN * 4;    // 16 KB: two [64 rows x 128 B] tiles (as landed: per 32 channels; split: per 32 K)
 constexpr uint32_t HALF = TM * 32 * 4;      // 16 KB: one [128 x 32] f32 tile, 128B swizzle
 constexpr uint32_t OFF_AHI = 0;
 constexpr uint32_t OFF_ALO = OFF_AHI + A_PART;
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
       prefetch_tmap(&tmX);
       prefetch_tmap(&tmW);
       if (DISC) prefetch_tmap(&tmB);
-      constexpr uint32_t ID = make_idesc_tf32(TM, TN, false, true);
+      constexpr uint32_t ID = make_idesc_tf32(TM, TN, false, false);
       const int nks = (R + 7) / 8;   // K steps of 8 (zero-filled past R)
       int last_m = -1, a_armed = 0, w_armed = 0, b_armed[2] = {0, 0};
       bool ok = true;
@@ -162,17 +162,17 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
         const uint32_t d = tmem + (uint32_t)(s * TN);
         const uint64_t dAhi = make_desc_sw128(smem_u32(smem + OFF_AHI), 16);
         const uint64_t dAlo = make_desc_sw128(smem_u32(smem + OFF_ALO), 16);
-        const uint64_t dWhi = make_desc_sw128(smem_u32(smem + OFF_WHI), W_PART / 2);
-        const uint64_t dWlo = make_desc_sw128(smem_u32(smem + OFF_WLO), W_PART / 2);
+        const uint64_t dWhi = make_desc_sw128(smem_u32(smem + OFF_WHI), 16);
+        const uint64_t dWlo = make_desc_sw128(smem_u32(smem + OFF_WLO), 16);
 #pragma unroll 1
         for (int p = 0; p < 3; ++p) {
           const uint64_t a = p == 2 ? dAlo : dAhi, w = p == 1 ? dWlo : dWhi;
 #pragma unroll 1
           for (int ks = 0; ks < nks; ++ks) {
-            // A (K-major): 32 B per K step inside a 128-byte row, 16 KB per 32-wide K atom;
-            // W (MN-major): one 8-row (1024 B) group per K step
+            // A and W (both K-major): 32 B per K step inside a 128-byte row; the second
+            // 32-wide K atom starts 16 KB (A) / 8 KB (W) further on
             const uint64_t ad = a + (uint64_t)(((ks >> 2) * (A_PART / 2) + (ks & 3) * 32) >> 4);
-            const uint64_t wd = w + (uint64_t)((ks * 1024) >> 4);
+            const uint64_t wd = w + (uint64_t)(((ks >> 2) * (W_PART / 2) + (ks & 3) * 32) >> 4);
             umma_tf32(d, ad, wd, ID, (p | ks) != 0);
           }
         }
@@ -207,10 +207,35 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
       }
       if (!wait(barW, j & 1, 9512)) break;
       {
-        float4* hi = reinterpret_cast<float4*>(smem + OFF_WHI);
-        float4* lo = reinterpret_cast<float4*>(smem + OFF_WLO);
+        // W as landed ([k][32 n] 128-byte rows per 32-channel block) -> hi/lo in K-major
+        // tiles ([n][32 k] 128-byte rows per 32-wide K atom), the layout the MMA reads
+        // (an MN-major tf32 operand read back as zeros here); the landed slab is copied
+        // to the lo region first so the hi tile can be written over it
+        const uint8_t* src = smem + OFF_WLO;
+        {
+          const float4* a = reinterpret_cast<const float4*>(smem + OFF_WHI);
+          float4* b = reinterpret_cast<float4*>(smem + OFF_WLO);
+          for (int k = tid; k < (int)(W_PART / 16); k += NEPI) b[k] = a[k];
+        }
+        named_bar_sync(2, NEPI);
+        float wv[32];
 #pragma unroll
-        for (int k = 0; k < (int)(W_PART / 16 / NEPI); ++k) split4(hi + tid + k * NEPI, lo + tid + k * NEPI);
+        for (int e = 0; e < 32; ++e) {
+          const int idx = tid + e * NEPI, k = idx & 63, n = idx >> 6;
+          const uint32_t so = (uint32_t)(n >> 5) * (W_PART / 2) + (uint32_t)k * 128u +
+                              (((((uint32_t)(n & 31) >> 2) ^ ((uint32_t)k & 7u)) & 7u) << 4) + ((uint32_t)n & 3u) * 4u;
+          wv[e] = *reinterpret_cast<const float*>(src + so);
+        }
+        named_bar_sync(2, NEPI);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int idx = tid + e * NEPI, k = idx & 63, n = idx >> 6;
+          const uint32_t d = (uint32_t)(k >> 5) * (W_PART / 2) + (uint32_t)n * 128u +
+                             (((((uint32_t)(k & 31) >> 2) ^ ((uint32_t)n & 7u)) & 7u) << 4) + ((uint32_t)k & 3u) * 4u;
+          const float h = tf32_round(wv[e]);
+          *reinterpret_cast<float*>(smem + OFF_WHI + d) = h;
+          *reinterpret_cast<float*>(smem + OFF_WLO + d) = wv[e] - h;
+        }
       }
       float* col = reinterpret_cast<float*>(smem + OFF_COL) + s * 3 * TN;
       if (tid < TN) {

@@ -21,6 +21,8 @@
 
 namespace tssm {
 #ifdef TSSM_INTERP_TRACE
+// Debug-only per-unit start/end (globaltimer) and SM id of the pair scan.
+__device__ unsigned long long g_unit_trace[4096 * 3];
 // Debug-only per-block phase timestamps (clock64) of CTA (0,0), thread 0.
 __device__ unsigned long long g_interp_trace[128 * 8];
 #define IT_TRACE(blk, ev)                                                                          \
@@ -1208,6 +1210,14 @@ __global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
     int nch) {
   extern __shared__ __align__(16) uint8_t dsm[];
   PairSmem& S = *reinterpret_cast<PairSmem*>(dsm + ((128u - (sm100::smem_u32(dsm) & 127u)) & 127u));
+#ifdef TSSM_INTERP_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 4096) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_unit_trace[blockIdx.x * 3] = sm100::globaltimer_ns();
+    g_unit_trace[blockIdx.x * 3 + 2] = smid;
+  }
+#endif
   constexpr unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x;
   const int gpr = Dm / PF;
@@ -1419,6 +1429,9 @@ __global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
       IT_TRACE(i, 3);
     }
   }
+#ifdef TSSM_INTERP_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 4096) g_unit_trace[blockIdx.x * 3 + 1] = sm100::globaltimer_ns();
+#endif
   if (!alive) {
     for (; t_done < t_issued; ++t_done) mbar_poll(&S.tbar[t_done % PTS], (uint32_t)((t_done / PTS) & 1), 100000000ull);
     for (; r_done < r_issued; ++r_done) mbar_poll(&S.rbar[r_done % PRB], (uint32_t)((r_done / PRB) & 1), 100000000ull);
@@ -1703,6 +1716,10 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
 }
 
 #ifdef TSSM_INTERP_TRACE
+extern "C" int tssm_debug_read_unit_trace(unsigned long long* out, int n) {
+  return cudaMemcpyFromSymbol(out, tssm::g_unit_trace, sizeof(unsigned long long) * (n < 4096 * 3 ? n : 4096 * 3)) ==
+                 cudaSuccess ? 0 : 3;
+}
 extern "C" int tssm_debug_read_interp_trace(unsigned long long* out, int n) {
   return cudaMemcpyFromSymbol(out, tssm::g_interp_trace, sizeof(unsigned long long) * (n < 1024 ? n : 1024)) ==
                  cudaSuccess ? 0 : 3;
