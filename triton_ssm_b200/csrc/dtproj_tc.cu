@@ -15,14 +15,14 @@
 // Persistent CTAs (one per SM) walk a contiguous range of tiles, channels
 // fastest, so a 128-row block of dt_raw is loaded and split once per 16
 // channel tiles.  Roles:
-//   warp 4, one thread: TMA loads of the dt_raw block, the W slab and (fused
+//   warp 8, one thread: TMA loads of the dt_raw block, the W slab and (fused
 //     form) the B tile one tile ahead, and the 24 MMAs of each tile into one of
 //     two TMEM accumulators;
-//   warps 0-3 (one thread per tile row): the hi/lo split of each newly loaded
-//     operand (W transposed to K-major on the way), then the epilogue of the previous MMAs -- bias, softplus, clamp,
-//     the ZOH arithmetic against the swizzled B tile -- into 128B-swizzled
-//     staging tiles that TMA stores write out (two staging buffers, so one
-//     store drains while the next half-tile is computed).
+//   warps 0-7 (one thread per tile row and 32-channel half): the hi/lo split of
+//     each newly loaded operand (W transposed to K-major on the way), then the
+//     epilogue of the tile's MMAs -- bias, softplus, clamp, the ZOH arithmetic
+//     against the swizzled B tile -- into 128B-swizzled staging tiles that TMA
+//     stores write out.
 // Every mbarrier wait is bounded; a wait that gives up sets the device status
 // word and every role leaves its loop; the CTA drains its MMAs, loads and
 // stores (bounded) and frees TMEM before it exits.
@@ -39,7 +39,7 @@ using namespace sm100;
 constexpr int TM = 128;                     // rows per tile (the MMA's M)
 constexpr int TN = 64;                      // channels per tile (the MMA's N)
 constexpr int KM = 64;                      // largest dt_rank on this path
-constexpr int NEPI = 128;                   // epilogue threads, one per tile row
+constexpr int NEPI = 256;                   // epilogue threads: one per (tile row, 32-channel half)
 constexpr int NTHR = NEPI + 32;             // + the load / MMA warp
 constexpr uint32_t A_PART = TM * KM * 4;    // 32 KB: two [128 rows x 128 B] K atoms
 constexpr uint32_t W_PART = KM * TN * 4;    // 16 KB: two [64 rows x 128 B] tiles (as landed: per 32 channels; split: per 32 K)
@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
     return false;
   };
 
-  if (warp == 4) {
+  if (warp == NEPI / 32) {
     // ============================================================ loads and MMAs
     if (lane == 0 && it0 < it1) {
       prefetch_tmap(&tmX);
@@ -190,9 +190,10 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
       }
     }
   } else {
-    // ============================================================ split + epilogue (one row per thread)
+    // ============================================================ split + epilogue
+    // warps w and w+4 share TMEM lanes 32*(w%4) ..: row r of the tile, channel half hf
     int last_m = -1, a_seen = 0;
-    const int r = tid;
+    const int r = tid & (TM - 1), hf = tid / TM;
     for (int it = it0; it < it1; ++it) {
       const int j = it - it0, s = j & 1;
       const int m = it / ntn, n = it - m * ntn, m0 = m * TM, n0 = n * TN;
@@ -218,9 +219,10 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
           for (int k = tid; k < (int)(W_PART / 16); k += NEPI) b[k] = a[k];
         }
         named_bar_sync(2, NEPI);
-        float wv[32];
+        constexpr int WE = KM * TN / NEPI;   // elements of the slab per thread
+        float wv[WE];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < WE; ++e) {
           const int idx = tid + e * NEPI, k = idx & 63, n = idx >> 6;
           const uint32_t so = (uint32_t)(n >> 5) * (W_PART / 2) + (uint32_t)k * 128u +
                               (((((uint32_t)(n & 31) >> 2) ^ ((uint32_t)k & 7u)) & 7u) << 4) + ((uint32_t)n & 3u) * 4u;
@@ -228,7 +230,7 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
         }
         named_bar_sync(2, NEPI);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < WE; ++e) {
           const int idx = tid + e * NEPI, k = idx & 63, n = idx >> 6;
           const uint32_t d = (uint32_t)(k >> 5) * (W_PART / 2) + (uint32_t)n * 128u +
                              (((((uint32_t)(k & 31) >> 2) ^ ((uint32_t)n & 7u)) & 7u) << 4) + ((uint32_t)k & 3u) * 4u;
@@ -253,14 +255,13 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
       if (!wait(&barMMA[s], (j >> 1) & 1, 9513)) break;
       tc_fence_after();
       if (DISC && !wait(&barB[s], (j >> 1) & 1, 9514)) break;
-      const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(s * TN);
-#pragma unroll 1
-      for (int hf = 0; hf < 2; ++hf) {
+      const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(s * TN);
+      {
         float acc[32];
         tmem_ld32(trow + (uint32_t)(hf * 32), acc);
         tmem_wait_ld();
-        // staging buffer hf was last stored from one tile ago: that store has read it
-        if (tid == 0) bulk_wait_read<1>();
+        // the previous tile's stores have finished reading the staging tiles
+        if (tid == 0) bulk_wait_read<0>();
         named_bar_sync(1, NEPI);
         uint8_t* o0 = smem + OFF_O + hf * 2 * HALF;
         uint8_t* o1 = o0 + HALF;
@@ -295,8 +296,12 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
         fence_proxy_async_smem();
         named_bar_sync(1, NEPI);
         if (tid == 0) {
-          tma_store_2d(&tmO0, o0, n0 + 32 * hf, m0);
-          if (DISC) tma_store_2d(&tmO1, o1, n0 + 32 * hf, m0);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint8_t* p0 = smem + OFF_O + h2 * 2 * HALF;
+            tma_store_2d(&tmO0, p0, n0 + 32 * h2, m0);
+            if (DISC) tma_store_2d(&tmO1, p0 + HALF, n0 + 32 * h2, m0);
+          }
           bulk_commit();
         }
       }
