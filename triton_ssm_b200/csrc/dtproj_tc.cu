@@ -15,10 +15,10 @@
 // Persistent CTAs (one per SM) walk a contiguous range of tiles, channels
 // fastest, so a 128-row block of dt_raw is loaded and split once per 16
 // channel tiles.  Roles:
-//   warp 8, one thread: TMA loads of the dt_raw block, the W slab and (fused
+//   warp 16, one thread: TMA loads of the dt_raw block, the W slab and (fused
 //     form) the B tile one tile ahead, and the 24 MMAs of each tile into one of
 //     two TMEM accumulators;
-//   warps 0-7 (one thread per tile row and 32-channel half): the hi/lo split of
+//   warps 0-15 (one thread per tile row and 16-channel quarter): the hi/lo split of
 //     each newly loaded operand (W transposed to K-major on the way), then the
 //     epilogue of the tile's MMAs -- bias, softplus, clamp, the ZOH arithmetic
 //     against the swizzled B tile -- into 128B-swizzled staging tiles that TMA
@@ -33,13 +33,25 @@
 #include "tmap.cuh"
 
 namespace tssm {
+#ifdef TSSM_DTPROJ_TRACE
+// Debug-only phase timestamps (globaltimer, ns) of CTA 0: [tile][event].
+__device__ unsigned long long g_dtp_trace[64 * 16];
+#define DTP_TRACE(tile, ev)                                                                   \
+  do {                                                                                        \
+    if (blockIdx.x == 0 && (tile) < 64) g_dtp_trace[(tile) * 16 + (ev)] = globaltimer_ns();   \
+  } while (0)
+#else
+#define DTP_TRACE(tile, ev) \
+  do {                      \
+  } while (0)
+#endif
 namespace {
 using namespace sm100;
 
 constexpr int TM = 128;                     // rows per tile (the MMA's M)
 constexpr int TN = 64;                      // channels per tile (the MMA's N)
 constexpr int KM = 64;                      // largest dt_rank on this path
-constexpr int NEPI = 256;                   // epilogue threads: one per (tile row, 32-channel half)
+constexpr int NEPI = 512;                   // epilogue threads: one per (tile row, 16-channel quarter)
 constexpr int NTHR = NEPI + 32;             // + the load / MMA warp
 constexpr uint32_t A_PART = TM * KM * 4;    // 32 KB: two [128 rows x 128 B] K atoms
 constexpr uint32_t W_PART = KM * TN * 4;    // 16 KB: two [64 rows x 128 B] tiles (as landed: per 32 channels; split: per 32 K)
@@ -130,14 +142,16 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
       prefetch_tmap(&tmW);
       if (DISC) prefetch_tmap(&tmB);
       constexpr uint32_t ID = make_idesc_tf32(TM, TN, false, false);
-      const int nks = (R + 7) / 8;   // K steps of 8 (zero-filled past R)
+      const int natom = (R + 31) / 32;   // 32-wide K atoms (zero-filled past R)
       int last_m = -1, a_armed = 0, w_armed = 0, b_armed[2] = {0, 0};
       bool ok = true;
       for (int it = it0; it < it1; ++it) {
         const int j = it - it0, s = j & 1;
         const int m = it / ntn, n = it - m * ntn, m0 = m * TM, n0 = n * TN;
         // this buffer's previous user (tile j-2) released its B tile and accumulator
+        DTP_TRACE(j, 0);
         if (j >= 2 && !(ok = wait(&barFree[s], ((j - 2) >> 1) & 1, 9501))) break;
+        DTP_TRACE(j, 1);
         if (DISC) {
           mbar_arrive_expect_tx(&barB[s], 2 * HALF);
           tma_load_2d(smem + OFF_B + s * 2 * HALF, &tmB, n0, m0, &barB[s]);
@@ -146,6 +160,7 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
         }
         // the previous tile's MMAs are the last readers of the operand buffers
         if (j >= 1 && !(ok = wait(&barMMA[(j - 1) & 1], ((j - 1) >> 1) & 1, 9502))) break;
+        DTP_TRACE(j, 2);
         if (m != last_m) {
           mbar_arrive_expect_tx(barA, A_PART);
           tma_load_2d(smem + OFF_AHI, &tmX, 0, m0, barA);
@@ -158,25 +173,26 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
         tma_load_2d(smem + OFF_WHI + W_PART / 2, &tmW, n0 + 32, 0, barW);
         ++w_armed;
         if (!(ok = wait(barSplit, j & 1, 9503))) break;
+        DTP_TRACE(j, 3);
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(s * TN);
         const uint64_t dAhi = make_desc_sw128(smem_u32(smem + OFF_AHI), 16);
         const uint64_t dAlo = make_desc_sw128(smem_u32(smem + OFF_ALO), 16);
         const uint64_t dWhi = make_desc_sw128(smem_u32(smem + OFF_WHI), 16);
         const uint64_t dWlo = make_desc_sw128(smem_u32(smem + OFF_WLO), 16);
+        // A and W (both K-major): 32 B per K step inside a 128-byte row (four per asm
+        // block); the second 32-wide K atom starts 16 KB (A) / 8 KB (W) further on.
+        // K past R reads zeros, so whole atoms are issued.
 #pragma unroll 1
         for (int p = 0; p < 3; ++p) {
           const uint64_t a = p == 2 ? dAlo : dAhi, w = p == 1 ? dWlo : dWhi;
 #pragma unroll 1
-          for (int ks = 0; ks < nks; ++ks) {
-            // A and W (both K-major): 32 B per K step inside a 128-byte row; the second
-            // 32-wide K atom starts 16 KB (A) / 8 KB (W) further on
-            const uint64_t ad = a + (uint64_t)(((ks >> 2) * (A_PART / 2) + (ks & 3) * 32) >> 4);
-            const uint64_t wd = w + (uint64_t)(((ks >> 2) * (W_PART / 2) + (ks & 3) * 32) >> 4);
-            umma_tf32(d, ad, wd, ID, (p | ks) != 0);
-          }
+          for (int at = 0; at < natom; ++at)
+            umma_tf32_x4(d, a + (uint64_t)((at * (A_PART / 2)) >> 4), w + (uint64_t)((at * (W_PART / 2)) >> 4), ID,
+                         (p | at) != 0);
         }
         umma_commit(&barMMA[s]);
+        DTP_TRACE(j, 4);
       }
       // this thread's MMAs complete before teardown; after a failed wait, the loads it
       // armed complete too (every wait below is bounded)
@@ -191,49 +207,47 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
     }
   } else {
     // ============================================================ split + epilogue
-    // warps w and w+4 share TMEM lanes 32*(w%4) ..: row r of the tile, channel half hf
+    // Warps w, w+4, w+8, w+12 share TMEM lanes 32*(w%4) ..: thread = (tile row r,
+    // 16-channel quarter qt).  After the MMAs of tile j complete, the operands of
+    // tile j+1 are split first (so its MMAs run while tile j's epilogue computes).
     int last_m = -1, a_seen = 0;
-    const int r = tid & (TM - 1), hf = tid / TM;
-    for (int it = it0; it < it1; ++it) {
+    const int r = tid & (TM - 1), qt = tid / TM;
+    auto split_tile = [&](int it) -> bool {
       const int j = it - it0, s = j & 1;
-      const int m = it / ntn, n = it - m * ntn, m0 = m * TM, n0 = n * TN;
+      const int m = it / ntn, n = it - m * ntn, n0 = n * TN;
+      if (tid == 0) DTP_TRACE(j, 5);
       if (m != last_m) {
-        if (!wait(barA, a_seen & 1, 9511)) break;
+        if (!wait(barA, a_seen & 1, 9511)) return false;
         ++a_seen;
         last_m = m;
         float4* hi = reinterpret_cast<float4*>(smem + OFF_AHI);
         float4* lo = reinterpret_cast<float4*>(smem + OFF_ALO);
-#pragma unroll 4
+#pragma unroll
         for (int k = 0; k < (int)(A_PART / 16 / NEPI); ++k) split4(hi + tid + k * NEPI, lo + tid + k * NEPI);
       }
-      if (!wait(barW, j & 1, 9512)) break;
+      if (tid == 0) DTP_TRACE(j, 6);
+      if (!wait(barW, j & 1, 9512)) return false;
+      if (tid == 0) DTP_TRACE(j, 7);
       {
         // W as landed ([k][32 n] 128-byte rows per 32-channel block) -> hi/lo in K-major
         // tiles ([n][32 k] 128-byte rows per 32-wide K atom), the layout the MMA reads
-        // (an MN-major tf32 operand read back as zeros here); the landed slab is copied
-        // to the lo region first so the hi tile can be written over it
-        const uint8_t* src = smem + OFF_WLO;
-        {
-          const float4* a = reinterpret_cast<const float4*>(smem + OFF_WHI);
-          float4* b = reinterpret_cast<float4*>(smem + OFF_WLO);
-          for (int k = tid; k < (int)(W_PART / 16); k += NEPI) b[k] = a[k];
-        }
-        named_bar_sync(2, NEPI);
+        // (an MN-major tf32 operand read back as zeros here); the slab is read into
+        // registers first so the hi/lo tiles can be written over it
         constexpr int WE = KM * TN / NEPI;   // elements of the slab per thread
         float wv[WE];
 #pragma unroll
         for (int e = 0; e < WE; ++e) {
-          const int idx = tid + e * NEPI, k = idx & 63, n = idx >> 6;
-          const uint32_t so = (uint32_t)(n >> 5) * (W_PART / 2) + (uint32_t)k * 128u +
-                              (((((uint32_t)(n & 31) >> 2) ^ ((uint32_t)k & 7u)) & 7u) << 4) + ((uint32_t)n & 3u) * 4u;
-          wv[e] = *reinterpret_cast<const float*>(src + so);
+          const int idx = tid + e * NEPI, k = idx & 63, nn = idx >> 6;
+          const uint32_t so = (uint32_t)(nn >> 5) * (W_PART / 2) + (uint32_t)k * 128u +
+                              (((((uint32_t)(nn & 31) >> 2) ^ ((uint32_t)k & 7u)) & 7u) << 4) + ((uint32_t)nn & 3u) * 4u;
+          wv[e] = *reinterpret_cast<const float*>(smem + OFF_WHI + so);
         }
         named_bar_sync(2, NEPI);
 #pragma unroll
         for (int e = 0; e < WE; ++e) {
-          const int idx = tid + e * NEPI, k = idx & 63, n = idx >> 6;
-          const uint32_t d = (uint32_t)(k >> 5) * (W_PART / 2) + (uint32_t)n * 128u +
-                             (((((uint32_t)(k & 31) >> 2) ^ ((uint32_t)n & 7u)) & 7u) << 4) + ((uint32_t)k & 3u) * 4u;
+          const int idx = tid + e * NEPI, k = idx & 63, nn = idx >> 6;
+          const uint32_t d = (uint32_t)(k >> 5) * (W_PART / 2) + (uint32_t)nn * 128u +
+                             (((((uint32_t)(k & 31) >> 2) ^ ((uint32_t)nn & 7u)) & 7u) << 4) + ((uint32_t)k & 3u) * 4u;
           const float h = tf32_round(wv[e]);
           *reinterpret_cast<float*>(smem + OFF_WHI + d) = h;
           *reinterpret_cast<float*>(smem + OFF_WLO + d) = wv[e] - h;
@@ -252,61 +266,78 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
       fence_proxy_async_smem();   // the split tiles are read by the tensor core (async proxy)
       named_bar_sync(2, NEPI);    // channel constants visible to every epilogue thread
       mbar_arrive(barSplit);
-      if (!wait(&barMMA[s], (j >> 1) & 1, 9513)) break;
-      tc_fence_after();
-      if (DISC && !wait(&barB[s], (j >> 1) & 1, 9514)) break;
-      const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(s * TN);
-      {
-        float acc[32];
-        tmem_ld32(trow + (uint32_t)(hf * 32), acc);
-        tmem_wait_ld();
-        // the previous tile's stores have finished reading the staging tiles
-        if (tid == 0) bulk_wait_read<0>();
-        named_bar_sync(1, NEPI);
-        uint8_t* o0 = smem + OFF_O + hf * 2 * HALF;
-        uint8_t* o1 = o0 + HALF;
-        const uint8_t* bt = smem + OFF_B + s * 2 * HALF + hf * HALF;
+      if (tid == 0) DTP_TRACE(j, 8);
+      return true;
+    };
+    auto epilogue_tile = [&](int it) -> bool {
+      const int j = it - it0, s = j & 1;
+      const int m = it / ntn, n = it - m * ntn, m0 = m * TM, n0 = n * TN;
+      if (DISC && !wait(&barB[s], (j >> 1) & 1, 9514)) return false;
+      if (tid == 0) DTP_TRACE(j, 10);
+      const float* col = reinterpret_cast<const float*>(smem + OFF_COL) + s * 3 * TN;
+      float acc[16];
+      tmem_ld16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(s * TN + qt * 16), acc);
+      tmem_wait_ld();
+      // the previous tile's stores have finished reading the staging tiles
+      if (tid == 0) bulk_wait_read<0>();
+      named_bar_sync(1, NEPI);
+      if (tid == 0) DTP_TRACE(j, 11);
+      const int hf = qt >> 1;               // 32-channel half (one swizzled [128 x 128 B] tile)
+      uint8_t* o0 = smem + OFF_O + hf * 2 * HALF;
+      uint8_t* o1 = o0 + HALF;
+      const uint8_t* bt = smem + OFF_B + s * 2 * HALF + hf * HALF;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint32_t off = (uint32_t)r * 128u + ((((uint32_t)q ^ ((uint32_t)r & 7u)) & 7u) << 4);
-          float bv[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const uint32_t q = (uint32_t)((qt & 1) * 4 + q4);   // 16-byte chunk of the 128-byte row
+        const uint32_t off = (uint32_t)r * 128u + (((q ^ ((uint32_t)r & 7u)) & 7u) << 4);
+        float bv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (DISC) {
+          const float4 t = *reinterpret_cast<const float4*>(bt + off);
+          bv[0] = t.x; bv[1] = t.y; bv[2] = t.z; bv[3] = t.w;
+        }
+        float y0[4], y1[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = qt * 16 + q4 * 4 + e;
+          const float v = acc[q4 * 4 + e] + col[c];
+          const float dtv = fminf(fmaxf(logf(1.0f + expf(v)), dt_min), dt_max);
           if (DISC) {
-            const float4 t = *reinterpret_cast<const float4*>(bt + off);
-            bv[0] = t.x; bv[1] = t.y; bv[2] = t.z; bv[3] = t.w;
+            const float x = dtv * col[TN + c];
+            const float ex = expf(x);
+            y0[e] = ex;
+            y1[e] = expm1_guard_f32(x, ex) * col[2 * TN + c] * bv[e];
+          } else {
+            y0[e] = dtv;
+            y1[e] = 0.f;
           }
-          float y0[4], y1[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = hf * 32 + q * 4 + e;
-            const float v = acc[q * 4 + e] + col[c];
-            const float dtv = fminf(fmaxf(logf(1.0f + expf(v)), dt_min), dt_max);
-            if (DISC) {
-              const float x = dtv * col[TN + c];
-              const float ex = expf(x);
-              y0[e] = ex;
-              y1[e] = expm1_guard_f32(x, ex) * col[2 * TN + c] * bv[e];
-            } else {
-              y0[e] = dtv;
-              y1[e] = 0.f;
-            }
-          }
-          *reinterpret_cast<float4*>(o0 + off) = make_float4(y0[0], y0[1], y0[2], y0[3]);
-          if (DISC) *reinterpret_cast<float4*>(o1 + off) = make_float4(y1[0], y1[1], y1[2], y1[3]);
         }
-        fence_proxy_async_smem();
-        named_bar_sync(1, NEPI);
-        if (tid == 0) {
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint8_t* p0 = smem + OFF_O + h2 * 2 * HALF;
-            tma_store_2d(&tmO0, p0, n0 + 32 * h2, m0);
-            if (DISC) tma_store_2d(&tmO1, p0 + HALF, n0 + 32 * h2, m0);
-          }
-          bulk_commit();
-        }
+        *reinterpret_cast<float4*>(o0 + off) = make_float4(y0[0], y0[1], y0[2], y0[3]);
+        if (DISC) *reinterpret_cast<float4*>(o1 + off) = make_float4(y1[0], y1[1], y1[2], y1[3]);
       }
       tc_fence_before();
-      mbar_arrive(&barFree[s]);
+      mbar_arrive(&barFree[s]);   // this thread is done with the accumulator and the B tile
+      fence_proxy_async_smem();
+      named_bar_sync(1, NEPI);
+      if (tid == 0) DTP_TRACE(j, 12);
+      if (tid == 0) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint8_t* p0 = smem + OFF_O + h2 * 2 * HALF;
+          tma_store_2d(&tmO0, p0, n0 + 32 * h2, m0);
+          if (DISC) tma_store_2d(&tmO1, p0 + HALF, n0 + 32 * h2, m0);
+        }
+        bulk_commit();
+      }
+      return true;
+    };
+    bool ok = it0 >= it1 || split_tile(it0);
+    for (int it = it0; ok && it < it1; ++it) {
+      const int j = it - it0, s = j & 1;
+      if (!(ok = wait(&barMMA[s], (j >> 1) & 1, 9513))) break;
+      if (tid == 0) DTP_TRACE(j, 9);
+      tc_fence_after();
+      if (it + 1 < it1 && !(ok = split_tile(it + 1))) break;
+      ok = epilogue_tile(it);
     }
     if (tid == 0) bulk_wait<0>();
   }
@@ -318,6 +349,12 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
 }
 
 }  // namespace
+
+#ifdef TSSM_DTPROJ_TRACE
+extern "C" int tssm_debug_read_dtp_trace(unsigned long long* out, int n) {
+  return cudaMemcpyFromSymbol(out, g_dtp_trace, sizeof(unsigned long long) * (n < 1024 ? n : 1024)) == cudaSuccess ? 0 : 3;
+}
+#endif
 
 // The tensor-core path: R <= 64, rows of dt_raw, W, B and the outputs 16-byte
 // aligned (R % 4 == 0, H % 4 == 0, 16-byte aligned bases), and no dt output in
