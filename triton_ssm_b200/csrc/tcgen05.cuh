@@ -277,6 +277,36 @@ __device__ __forceinline__ void umma_tf32_x4(uint32_t d_tmem, uint64_t a0, uint6
       "l"(a0), "l"(b0), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Four kind::tf32 MMAs with A read from TMEM (row m in lane m, 8 K columns per
+// step) and B from a K-major shared-memory descriptor (32 bytes per step).
+__device__ __forceinline__ void umma_tf32_tmemA_x4(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
+                                                   uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      ".reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %3, %3;\n\t"
+      "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+      "add.s64 b1, %2, 2;\n\tadd.s64 b2, %2, 4;\n\tadd.s64 b3, %2, 6;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [a1], b1, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [a2], b2, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [a3], b3, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns from registers: thread t of the warp
+// writes the 16 columns of TMEM lane (lane_base + t).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&r)[16]) {
+  const uint32_t* u = reinterpret_cast<const uint32_t*>(r);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]),
+      "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // 32 lanes x 16 consecutive 32-bit columns: thread t of the warp receives the
 // 16 columns of TMEM lane (lane_base + t).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&r)[16]) {
