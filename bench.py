@@ -286,8 +286,8 @@ def run_ours_c3(args, rank, world, local):
                        (Bt, T, Lq, Dm, N),
            "global_batch": Bt * world, "seq_len": Lq, "parallelism": "batch, %d rank(s)" % world}
     return _line(args, world, METRIC, world * upd / t_step, t_step, "f32", cfg, alg,
-                 "interp_flags + interp_neighbors + interp_ssm_scan", "interp_ssm_c3.md", clocks,
-                 launches=3 * args.steps)
+                 "interp_table + interp_ssm_scan_chunk", "interp_ssm_c3.md", clocks,
+                 launches=2 * args.steps)
 
 
 def run_ours_c5(args, rank, world, local):
@@ -514,7 +514,7 @@ def run_ours_dtproj(args, rank, world, local):
                        "ZOH discretisation, B%d T%d H%d f32" % (R, Bt, T, H),
            "global_batch": Bt * world, "seq_len": T, "parallelism": "batch, %d rank(s)" % world,
            "l2": "B in + Abar, Bbar out: %d MB per step, larger than the 126 MB L2" % (n * 12 // 1000000)}
-    return _line(args, world, METRIC, world * n / t_step, t_step, "f32", cfg, alg, "dt_project_kernel<disc>",
+    return _line(args, world, METRIC, world * n / t_step, t_step, "f32", cfg, alg, "dtproj_tc_kernel<true> (tcgen05)",
                  "dt_project_discretize.md", clocks)
 
 

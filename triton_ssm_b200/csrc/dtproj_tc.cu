@@ -397,7 +397,6 @@ int launch_dtproj_tc(bool disc, const void* dt_raw, const void* W, const void* b
       (disc ? !(aligned16(B) && aligned16(Abar) && aligned16(Bbar)) : !aligned16(dt_out)) ||
       rows >= (int64_t(1) << 31) || H >= (int64_t(1) << 31))
     return TSSM_ERR_UNSUPPORTED;
-  if (getenv("TSSM_DTPROJ_CUDA_CORES")) return TSSM_ERR_UNSUPPORTED;
   int* status = device_status_ptr();
   if (!status) {
     set_error("dt_project: device status word unavailable");

@@ -21,8 +21,6 @@
 
 namespace tssm {
 #ifdef TSSM_INTERP_TRACE
-// Debug-only per-unit start/end (globaltimer) and SM id of the pair scan.
-__device__ unsigned long long g_unit_trace[4096 * 3];
 // Debug-only per-block phase timestamps (clock64) of CTA (0,0), thread 0.
 __device__ unsigned long long g_interp_trace[128 * 8];
 #define IT_TRACE(blk, ev)                                                                          \
@@ -36,7 +34,6 @@ __device__ unsigned long long g_interp_trace[128 * 8];
   } while (0)
 #endif
 namespace {
-int getenv_int(const char* k, int d) { const char* v = getenv(k); return v ? atoi(v) : d; }
 using sm100::named_bar_arrive;
 using sm100::named_bar_sync;
 
@@ -1169,288 +1166,6 @@ __global__ void __launch_bounds__(CH_WARPS * 32, 2) interp_ssm_scan_chunk_kernel
   }
 }
 
-// ---------------------------------------------------------------------------
-// Kernel 3c, for N <= 16 with runs of 64 features inside one tile (Dm % 64 == 0,
-// FTILE % 64 == 0), reading the blocked table.  One warp per CTA and per unit
-// (b, 64 features, chunk of the queries): lane l owns features d0+2l and
-// d0+2l+1, and every f32x2 instruction advances the SAME state of those two
-// features, so the interpolated pair, the state update, the readout and the
-// output all go through packed instructions with nothing to broadcast (the
-// one-feature-per-lane kernel 3b duplicates v into both halves and reduces the
-// two half-sums per output).  Units are one-warp CTAs so the grid fills every
-// SM evenly.  Chunks start W queries early from a zero state exactly as in
-// kernel 3b; when W exceeds a chunk (slow decay), chunk 0 walks the whole row
-// and the other chunks of the row exit.
-constexpr int PF = 64;        // features per unit
-constexpr int PTS = 3;        // table slots
-constexpr int PRB = 2;        // row buffers
-
-struct alignas(128) PairSmem {
-  float rows[PRB][WRB + 1][PF];   // staged observation rows; row WRB stays zero
-  int4 tab[PTS][WQB + 1];
-  uint64_t tbar[PTS];
-  uint64_t rbar[PRB];
-};
-
-// The interpolated pair round((1-w)*vp) + round(w*vn), each product and the
-// sum rounded separately as the reference does (scalar IEEE operations: the
-// packed forms may be contracted into a fused multiply-add).
-__device__ __forceinline__ float2 lerp2(int4 x, float2 vp, float2 vn) {
-  const float om = __int_as_float(x.w), w = __int_as_float(x.z);
-  return make_float2(__fadd_rn(__fmul_rn(om, vp.x), __fmul_rn(w, vn.x)),
-                     __fadd_rn(__fmul_rn(om, vp.y), __fmul_rn(w, vn.y)));
-}
-
-template <int NS, bool VHAT>
-__global__ void __launch_bounds__(32) interp_ssm_scan_pair_kernel(
-    const __grid_constant__ CUtensorMap tmV, const float* __restrict__ Vp, const int4* __restrict__ tabq,
-    const float* __restrict__ A_log, const float* __restrict__ Bp, const float* __restrict__ Cp,
-    const float* __restrict__ Dskip, const float* __restrict__ dt, float* __restrict__ y, float* __restrict__ h_last,
-    float* __restrict__ vhat_out, int* __restrict__ status, int T, int Dm, int N, int Lq, int FTILE, int ntiles,
-    int nch) {
-  extern __shared__ __align__(16) uint8_t dsm[];
-  PairSmem& S = *reinterpret_cast<PairSmem*>(dsm + ((128u - (sm100::smem_u32(dsm) & 127u)) & 127u));
-#ifdef TSSM_INTERP_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < 4096) {
-    unsigned smid;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    g_unit_trace[blockIdx.x * 3] = sm100::globaltimer_ns();
-    g_unit_trace[blockIdx.x * 3 + 2] = smid;
-  }
-#endif
-  constexpr unsigned FULL = 0xffffffffu;
-  const int lane = threadIdx.x;
-  const int gpr = Dm / PF;
-  const int unit = blockIdx.x;
-  const int chunk = unit % nch, grp = (unit / nch) % gpr, b = unit / (nch * gpr);
-  const int d0 = grp * PF, d = d0 + 2 * lane;
-  const int nblk = (Lq + WQB - 1) / WQB;
-  const int4* tq = tabq + ((int64_t)b * ntiles + d0 / FTILE) * nblk * (WQB + 1);
-  const float* Vb = Vp + (int64_t)b * T * Dm + d;   // this lane's two features; + row * Dm
-
-  if (lane == 0) {
-    for (int i = 0; i < PTS; ++i) sm100::mbar_init(&S.tbar[i], 1);
-    for (int i = 0; i < PRB; ++i) sm100::mbar_init(&S.rbar[i], 1);
-    sm100::fence_mbar_init();
-    sm100::prefetch_tmap(&tmV);
-  }
-#pragma unroll
-  for (int i = 0; i < PRB; ++i) reinterpret_cast<float2*>(S.rows[i][WRB])[lane] = make_float2(0.f, 0.f);
-  __syncwarp();
-
-  // per state: Abar and C*Bbar of the two features, packed
-  const float dtb = dt[b];
-  auto coeffs = [&](int dd, int n, float& ab, float& bb) {
-    const float a = -expf(A_log[(int64_t)dd * N + n]);
-    const float x = dtb * a;
-    const float e = expf(x);
-    ab = e;
-    bb = zoh_coeff(x, e, a) * Bp[(int64_t)dd * N + n];
-  };
-  float2 a2[NS], c2[NS], g2[NS];
-  float amax = 0.f;
-  bool bad = false;
-#pragma unroll
-  for (int k = 0; k < NS; ++k) {
-    float ab0 = 0.f, bb0 = 0.f, ab1 = 0.f, bb1 = 0.f, cb0 = 0.f, cb1 = 0.f;
-    if (k < N) {
-      coeffs(d, k, ab0, bb0);
-      coeffs(d + 1, k, ab1, bb1);
-      cb0 = Cp[(int64_t)d * N + k] * bb0;
-      cb1 = Cp[(int64_t)(d + 1) * N + k] * bb1;
-      amax = fmaxf(amax, fmaxf(fabsf(ab0), fabsf(ab1)));
-      bad |= ab0 != ab0 || ab1 != ab1;
-    }
-    a2[k] = make_float2(ab0, ab1);
-    c2[k] = make_float2(cb0, cb1);
-    g2[k] = make_float2(0.f, 0.f);
-  }
-  const float2 dsk2 = Dskip ? make_float2(Dskip[d], Dskip[d + 1]) : make_float2(0.f, 0.f);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(FULL, amax, o));
-  if (__any_sync(FULL, bad)) amax = 1.0f;
-  // warm-up length in blocks (the same value in every chunk of this (b, group))
-  const int chb = (nblk + nch - 1) / nch;
-  int wb = 0x7fffffff;
-  if (amax < 1.0f) {
-    const float steps = amax > 0.f ? ceilf(40.0f / -log2f(amax)) : 0.f;
-    if (steps < (float)(1 << 30)) wb = ((int)steps + WQB - 1) / WQB;
-  }
-  const bool whole_row = wb >= chb && nblk > chb;
-  int jc0 = min(nblk, chunk * chb), jc1 = min(nblk, jc0 + chb);
-  if (whole_row) {
-    if (chunk != 0) return;   // chunk 0 of the row walks every block from the row's start
-    jc0 = 0;
-    jc1 = nblk;
-  }
-  if (jc0 >= jc1) return;
-
-  bool alive = true;
-  int t_issued = 0, t_done = 0, r_issued = 0, r_done = 0;
-  auto wait_bar = [&](uint64_t* bar, int use, int code) {
-    const bool ok = __all_sync(FULL, mbar_poll(bar, (uint32_t)(use & 1)));
-    if (!ok) {
-      if (lane == 0) atomicExch(status, code);
-      alive = false;
-    }
-    return ok;
-  };
-  const int js = whole_row ? 0 : max(0, jc0 - wb), jo = jc0, je = jc1;
-  const int nb = je - js;
-  auto issue_table = [&](int i) {
-    if (lane == 0) {
-      constexpr uint32_t bytes = (WQB + 1) * sizeof(int4);
-      sm100::fence_proxy_async_smem();
-      sm100::mbar_arrive_expect_tx(&S.tbar[i % PTS], bytes);
-      bulk_g2s(S.tab[i % PTS], tq + (int64_t)(js + i) * (WQB + 1), bytes, &S.tbar[i % PTS]);
-    }
-    ++t_issued;
-  };
-  auto stage_rows = [&](int i) -> bool {
-    if (!wait_bar(&S.tbar[i % PTS], i / PTS, 9311)) return false;
-    ++t_done;
-    if (lane == 0) {
-      const int4 h = S.tab[i % PTS][WQB];
-      uint64_t* rb = &S.rbar[i % PRB];
-      if (h.y > 0) {
-        sm100::fence_proxy_async_smem();
-        sm100::mbar_arrive_expect_tx(rb, (uint32_t)(WRB * PF * sizeof(float)));
-        sm100::tma_load_3d(S.rows[i % PRB], &tmV, d0, h.x, b, rb);
-      } else {
-        sm100::mbar_arrive(rb);
-      }
-    }
-    ++r_issued;
-    return true;
-  };
-  // readout of the current state: four independent chains of NS/4 packed FMAs
-  // (a short dependent path), summed pairwise
-  auto readout = [&]() -> float2 {
-    float2 acc[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) acc[c] = c < NS ? fmul2(c2[c], g2[c]) : make_float2(0.f, 0.f);
-#pragma unroll
-    for (int k = 4; k < NS; ++k) acc[k & 3] = ffma2(c2[k], g2[k], acc[k & 3]);
-    return fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
-  };
-  // readout of the state after the previous query, then the update by this
-  // query's pair of values
-  auto readout_update = [&](float2 v2) -> float2 {
-    const float2 r = readout();
-#pragma unroll
-    for (int k = 0; k < NS; ++k) g2[k] = ffma2(a2[k], g2[k], v2);
-    return r;
-  };
-  auto run_block = [&](int i, bool out) {
-    const int j = js + i;
-    const int nq = min(WQB, Lq - j * WQB);
-    const int4* e = S.tab[i % PTS];
-    const bool direct = e[WQB].y < 0;
-    const float2* rw = reinterpret_cast<const float2*>(&S.rows[i % PRB][0][0]) + lane;
-    float2* yrow = reinterpret_cast<float2*>(y + ((int64_t)b * Lq + (int64_t)j * WQB) * Dm + d);
-    float2* vrow = VHAT ? reinterpret_cast<float2*>(vhat_out + ((int64_t)b * Lq + (int64_t)j * WQB) * Dm + d)
-                        : nullptr;
-    const int64_t rs = Dm / 2;   // one query row, in float2
-    float2 vprev = make_float2(0.f, 0.f);
-    if (out && nq == WQB && !direct) {
-      // groups of four queries; the next group's entries and operands are loaded
-      // while this group computes
-      int4 xn[4];
-      float2 vpn[4], vnn[4];
-      auto load_group = [&](int g0) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) xn[u] = e[g0 + u];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) { vpn[u] = rw[xn[u].x]; vnn[u] = rw[xn[u].y]; }
-      };
-      load_group(0);
-#pragma unroll 1
-      for (int g0 = 0; g0 < WQB; g0 += 4) {
-        int4 x[4];
-        float2 vp[4], vn[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) { x[u] = xn[u]; vp[u] = vpn[u]; vn[u] = vnn[u]; }
-        if (g0 + 4 < WQB) load_group(g0 + 4);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 v = lerp2(x[u], vp[u], vn[u]);
-          const float2 acc = readout_update(v);
-          if (u > 0 || g0 > 0) {
-            yrow[(int64_t)(g0 + u - 1) * rs] = ffma2(dsk2, vprev, acc);
-            if (VHAT) vrow[(int64_t)(g0 + u - 1) * rs] = vprev;
-          }
-          vprev = v;
-        }
-      }
-    } else {
-#pragma unroll 1
-      for (int qq = 0; qq < nq; ++qq) {
-        const int4 x = e[qq];
-        float2 vp, vn;
-        if (!direct) {
-          vp = rw[x.x];
-          vn = rw[x.y];
-        } else {
-          vp = x.x >= 0 ? *reinterpret_cast<const float2*>(Vb + x.x) : make_float2(0.f, 0.f);
-          vn = x.y >= 0 ? *reinterpret_cast<const float2*>(Vb + x.y) : make_float2(0.f, 0.f);
-        }
-        const float2 v = lerp2(x, vp, vn);
-        if (out) {
-          const float2 acc = readout_update(v);
-          if (qq > 0) {
-            yrow[(int64_t)(qq - 1) * rs] = ffma2(dsk2, vprev, acc);
-            if (VHAT) vrow[(int64_t)(qq - 1) * rs] = vprev;
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < NS; ++k) g2[k] = ffma2(a2[k], g2[k], v);
-        }
-        vprev = v;
-      }
-    }
-    if (out && nq > 0) {   // the block's last readout
-      yrow[(int64_t)(nq - 1) * rs] = ffma2(dsk2, vprev, readout());
-      if (VHAT) vrow[(int64_t)(nq - 1) * rs] = vprev;
-    }
-  };
-
-  for (int i = 0; i < min(nb, PTS - 1); ++i) issue_table(i);
-  if (stage_rows(0)) {
-    for (int i = 0; i < nb; ++i) {
-      IT_TRACE(i, 0);
-      __syncwarp();   // block i-1's rows and entries were read by every lane
-      if (i + PTS - 1 < nb) issue_table(i + PTS - 1);
-      if (i + 1 < nb && !stage_rows(i + 1)) break;
-      IT_TRACE(i, 1);
-      if (!wait_bar(&S.rbar[i % PRB], i / PRB, 9312)) break;
-      IT_TRACE(i, 2);
-      ++r_done;
-      run_block(i, js + i >= jo);
-      IT_TRACE(i, 3);
-    }
-  }
-#ifdef TSSM_INTERP_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < 4096) g_unit_trace[blockIdx.x * 3 + 1] = sm100::globaltimer_ns();
-#endif
-  if (!alive) {
-    for (; t_done < t_issued; ++t_done) mbar_poll(&S.tbar[t_done % PTS], (uint32_t)((t_done / PTS) & 1), 100000000ull);
-    for (; r_done < r_issued; ++r_done) mbar_poll(&S.rbar[r_done % PRB], (uint32_t)((r_done / PRB) & 1), 100000000ull);
-    return;
-  }
-  if (h_last && jc1 == nblk) {
-#pragma unroll
-    for (int k = 0; k < NS; ++k) {
-      if (k < N) {
-        float ab, bb0, bb1;
-        coeffs(d, k, ab, bb0);
-        coeffs(d + 1, k, ab, bb1);
-        h_last[((int64_t)b * Dm + d) * N + k] = bb0 * g2[k].x;
-        h_last[((int64_t)b * Dm + d + 1) * N + k] = bb1 * g2[k].y;
-      }
-    }
-  }
-}
-
 size_t ws_flags_bytes(int64_t Bsz, int64_t T, int64_t ntiles) { return (size_t)((Bsz * ntiles * T + 255) / 256 * 256); }
 // the per-query table, or its blocked form (WQB entries + a header per block), whichever is larger
 size_t ws_table_bytes(int64_t Bsz, int64_t Lq, int64_t ntiles) {
@@ -1628,41 +1343,6 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       return TSSM_ERR_CUDA;
     }
     TSSM_REQUIRE(Bsz * (Dm / 32) < (int64_t(1) << 31), "interp_ssm: size exceeds the grid");
-    if (Dm % PF == 0 && FTILE % PF == 0) {
-      // two features per lane, one-warp units: about seven units per SM, chunks
-      // of at least 16 query blocks
-      CUtensorMap tmP;
-      if (!tmap3d_f32(&tmP, V, (uint64_t)Dm, (uint64_t)T, (uint64_t)Bsz, PF, WRB)) {
-        set_error("interp_ssm: cuTensorMapEncodeTiled failed");
-        return TSSM_ERR_CUDA;
-      }
-      const int nblk = (int)cdiv(Lq, WQB);
-      const int64_t groups = Bsz * (Dm / PF);
-      const int nch = (int)std::max<int64_t>(1, std::min<int64_t>(nblk / 16, cdiv(7 * (int64_t)num_sms(), groups)));
-      TSSM_REQUIRE(groups * nch < (int64_t(1) << 31), "interp_ssm: size exceeds the grid");
-      const size_t pshm = std::max<size_t>(sizeof(PairSmem) + 128, (size_t)getenv_int("TSSM_PAIR_SMEM", 0));
-#define PAIR_LAUNCH(NS, VH)                                                                                     \
-  do {                                                                                                          \
-    auto kern = interp_ssm_scan_pair_kernel<NS, VH>;                                                           \
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pshm) != cudaSuccess)      \
-      return check_launch("interp_ssm: pair scan smem");                                                        \
-    kern<<<(unsigned)(groups * nch), 32, pshm, st>>>(                                                           \
-        tmP, Vf, reinterpret_cast<const int4*>(tab), (const float*)A_log, (const float*)B, (const float*)C,     \
-        (const float*)Dskip, (const float*)dt, (float*)y, (float*)h_last, (float*)vhat, status, (int)T,         \
-        (int)Dm, (int)N, (int)Lq, (int)FTILE, ntiles, nch);                                                     \
-  } while (0)
-      if (vhat) {
-        if (N <= 4) PAIR_LAUNCH(4, true);
-        else if (N <= 8) PAIR_LAUNCH(8, true);
-        else PAIR_LAUNCH(16, true);
-      } else {
-        if (N <= 4) PAIR_LAUNCH(4, false);
-        else if (N <= 8) PAIR_LAUNCH(8, false);
-        else PAIR_LAUNCH(16, false);
-      }
-#undef PAIR_LAUNCH
-      return check_launch("interp_ssm");
-    }
     CUtensorMap tmV;
     if (!tmap3d_f32(&tmV, V, (uint64_t)Dm, (uint64_t)T, (uint64_t)Bsz, 32, WRB)) {
       set_error("interp_ssm: cuTensorMapEncodeTiled failed");
@@ -1716,10 +1396,6 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
 }
 
 #ifdef TSSM_INTERP_TRACE
-extern "C" int tssm_debug_read_unit_trace(unsigned long long* out, int n) {
-  return cudaMemcpyFromSymbol(out, tssm::g_unit_trace, sizeof(unsigned long long) * (n < 4096 * 3 ? n : 4096 * 3)) ==
-                 cudaSuccess ? 0 : 3;
-}
 extern "C" int tssm_debug_read_interp_trace(unsigned long long* out, int n) {
   return cudaMemcpyFromSymbol(out, tssm::g_interp_trace, sizeof(unsigned long long) * (n < 1024 ? n : 1024)) ==
                  cudaSuccess ? 0 : 3;
