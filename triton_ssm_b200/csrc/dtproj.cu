@@ -6,8 +6,9 @@
 // and, fused, with one dt per (b, t, h) (the selective form of
 // discretize_kernel.py:38-54):
 //   Abar = exp(dt a), Bbar = expm1*(dt a) / (a + 1e-12) B,  a = -exp(A_log[h]).
-// The tensor-core kernel (dtproj_tc.cu) takes the shapes it supports; the
-// CUDA-core kernel below takes the rest.  A CTA computes a [32 rows x 128 channels] tile: W's 128-column slab and the
+// The tensor-core kernel (dtproj_tc.cu) takes dt_rank <= 64 with dt_rank % 4 == 0
+// and a 16-byte aligned dt_raw; the CUDA-core kernel below takes the rest.  A
+// CTA computes a [32 rows x 128 channels] tile: W's 128-column slab and the
 // 32 rows of dt_raw sit in shared memory, each thread accumulates 4 rows x 4
 // channels over r in the reference's order (one fma per r, two channels per
 // packed f32x2 instruction), and the epilogue writes dt, or Abar and Bbar,

@@ -5,28 +5,35 @@
 //   acc = dt_raw W + bias,  dt = clamp(log(1 + exp(acc)), dt_min, dt_max)
 //   Abar = exp(dt a), Bbar = expm1*(dt a) / (a + 1e-12) B,  a = -exp(A_log[h])
 //
-// The contraction dt_raw [rows x R] . W [R x H] (R <= 64) is a dense GEMM: it
-// runs as [128 rows x 64 channels] tiles of kind::tf32 MMAs with f32
-// accumulators in TMEM, the dt_raw operand read from TMEM.  tf32 keeps 11 bits of each operand, so every operand
-// is split exactly into hi = tf32(x) and lo = x - hi, and the tile is the sum of
-// the three products hi.hi + hi.lo + lo.hi (the dropped lo.lo term is below
-// 2^-22 of each product: f32-accurate, as the 1e-4 parity bar needs).
+// The contraction dt_raw [rows x R] . W [R x H] (R <= 64) is a dense GEMM,
+// computed transposed: a tile is [128 channels x 128 rows] of kind::tf32 MMAs
+// with the channel block of W (the A operand, M = channels) held in TMEM for the
+// CTA's whole run and the dt_raw rows (the B operand, N = rows, K-major as it
+// lies in memory) staged by TMA.  The f32 accumulator then has one channel per
+// TMEM lane, so an epilogue thread owns one channel and walks rows: each of its
+// warp's loads of B and stores of Abar / Bbar covers 32 consecutive channels of
+// one row (128 contiguous bytes), issued straight from registers with no
+// staging copy, and the next tile's B values are loaded while this tile's are
+// used.  tf32 keeps 11 bits of each operand, so both operands are split exactly
+// into hi = tf32(x) and lo = x - hi and the tile is the sum of the three
+// products hi.hi + hi.lo + lo.hi (the dropped lo.lo term is below 2^-22 of each
+// product: f32-accurate, as the 1e-4 parity bar needs).
 //
-// Persistent CTAs (one per SM) walk a contiguous range of tiles, channels
-// fastest, so a 128-row block of dt_raw is loaded and split once per 16
-// channel tiles.  Roles:
-//   warp 16, one thread: TMA loads of the dt_raw block, the W slab and (fused
-//     form) the B tile two tiles ahead (three buffers), and the 24 MMAs of each
-//     tile into one of two TMEM accumulators;
-//   warps 0-15 (one thread per tile row and 16-channel quarter): the hi/lo split of
-//     each newly loaded operand (dt_raw into TMEM columns, W transposed to
-//     K-major shared-memory tiles), then the
-//     epilogue of the tile's MMAs -- bias, softplus, clamp, the ZOH arithmetic
-//     against the swizzled B tile -- into 128B-swizzled staging tiles that TMA
-//     stores write out.
+// exp and log are the hardware approximations (ex2 / lg2 with a scale: relative
+// error near 2^-22), which is also how the reference's tl.exp / tl.log compile.
+//
+// Persistent CTAs (about one per SM) take a contiguous range of tiles, rows
+// fastest within a channel block, so a CTA meets at most two channel blocks:
+// both are split into TMEM before the first tile.  Roles:
+//   warp 16, one thread: TMA loads of the dt_raw rows (two stages) and the 24
+//     MMAs of each tile into one of two TMEM accumulators;
+//   warps 0-15, thread = (channel lane, 32-row quarter of the tile): W into TMEM,
+//     the in-place hi/lo split of each landed dt_raw stage (the next tile's,
+//     before this tile's epilogue, so its MMAs overlap the epilogue), and the
+//     epilogue.
 // Every mbarrier wait is bounded; a wait that gives up sets the device status
-// word and every role leaves its loop; the CTA drains its MMAs, loads and
-// stores (bounded) and frees TMEM before it exits.
+// word and every role leaves its loop; the CTA drains its MMAs and loads
+// (bounded) and frees TMEM before it exits.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -34,44 +41,28 @@
 #include "tmap.cuh"
 
 namespace tssm {
-#ifdef TSSM_DTPROJ_TRACE
-// Debug-only phase timestamps (globaltimer, ns) of CTA 0: [tile][event].
-__device__ unsigned long long g_dtp_trace[64 * 16];
-#define DTP_TRACE(tile, ev)                                                                   \
-  do {                                                                                        \
-    if (blockIdx.x == 0 && (tile) < 64) g_dtp_trace[(tile) * 16 + (ev)] = globaltimer_ns();   \
-  } while (0)
-#else
-#define DTP_TRACE(tile, ev) \
-  do {                      \
-  } while (0)
-#endif
 namespace {
 using namespace sm100;
 
-constexpr int TM = 128;                     // rows per tile (the MMA's M)
-constexpr int TN = 64;                      // channels per tile (the MMA's N)
-constexpr int KM = 64;                      // largest dt_rank on this path
-constexpr int NEPI = 512;                   // epilogue threads: one per (tile row, 16-channel quarter)
-constexpr int NTHR = NEPI + 32;             // + the load / MMA warp
-constexpr int NBB = 3;                      // B-tile buffers (loads run two tiles ahead)
-constexpr uint32_t A_RAW = TM * KM * 4;     // 32 KB: the dt_raw block as landed, two [128 x 128 B] K atoms
-constexpr uint32_t W_PART = KM * TN * 4;    // 16 KB: two [64 rows x 128 B] tiles (landed: per 32 channels; split: per 32 K)
-constexpr uint32_t HALF = TM * 32 * 4;      // 16 KB: one [128 x 32] f32 tile, 128B swizzle
-constexpr uint32_t OFF_A = 0;
-constexpr uint32_t OFF_WHI = OFF_A + A_RAW;
-constexpr uint32_t OFF_WLO = OFF_WHI + W_PART;
-constexpr uint32_t OFF_B = OFF_WLO + W_PART;         // [NBB buffers][2 halves] of the B tile
-constexpr uint32_t OFF_O = OFF_B + NBB * 2 * HALF;   // staging: [2 halves][out0, out1]
-constexpr uint32_t OFF_COL = OFF_O + 4 * HALF;       // [2][3][TN]: bias, a, 1/(a + 1e-12)
-constexpr uint32_t OFF_BAR = OFF_COL + 2 * 3 * TN * 4;
-constexpr int NBAR = 14;
+constexpr int CM = 128;                      // channels per tile (the MMA's M, one per TMEM lane)
+constexpr int RN = 128;                      // rows per tile (the MMA's N)
+constexpr int KM = 64;                       // largest dt_rank on this path
+constexpr int NEPI = 512;                    // epilogue threads: (channel lane, 32-row quarter)
+constexpr int NTHR = NEPI + 32;              // + the load / MMA warp
+constexpr int NX = 2;                        // dt_raw stages
+constexpr uint32_t X_ATOM = RN * 128;        // 16 KB: 128 rows x 32 f32 of K, 128B swizzle
+constexpr uint32_t X_PART = 2 * X_ATOM;      // both K atoms
+constexpr uint32_t X_STAGE = 2 * X_PART;     // hi (the landed rows, split in place), then lo
+constexpr uint32_t OFF_X = 0;
+constexpr uint32_t OFF_BAR = OFF_X + NX * X_STAGE;
+constexpr int NBAR = 2 * NX + 5;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;   // + slack to align the base to 1024
 static_assert(SMEM_BYTES <= 232448, "dt-projection shared-memory layout exceeds the per-CTA limit");
-// TMEM columns: two f32 accumulators, then the dt_raw block's hi and lo parts (A operand)
-constexpr uint32_t TM_D = 0, TM_AHI = 2 * TN, TM_ALO = TM_AHI + KM;
-constexpr uint32_t TMEM_COLS = 256;
+// TMEM columns: two f32 accumulators [128 channels x 128 rows], then two W slots
+// (hi: 64 K columns, lo: 64 K columns) for the CTA's first and second channel block
+constexpr uint32_t TM_D = 0, TM_W = 2 * RN;
+constexpr uint32_t TMEM_COLS = 512;
 
 // Nearest tf32 (the low 13 mantissa bits cleared); x - tf32(x) is exact in f32.
 __device__ __forceinline__ float tf32_round(float x) {
@@ -82,35 +73,30 @@ __device__ __forceinline__ float tf32_round(float x) {
 
 template <bool DISC>
 __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
-    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmO0,
-    const __grid_constant__ CUtensorMap tmO1, const float* __restrict__ bias, const float* __restrict__ A_log,
-    int* __restrict__ status, int H, int R, float dt_min, float dt_max, int ntn, int nitems) {
+    const __grid_constant__ CUtensorMap tmX, const float* __restrict__ W, const float* __restrict__ bias,
+    const float* __restrict__ A_log, const float* __restrict__ B, float* __restrict__ out0,
+    float* __restrict__ out1, float* __restrict__ dt_out, int* __restrict__ status, int rows, int H, int R,
+    float dt_min, float dt_max, int nrb, int nitems, int per) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* barA = bars + 0;        // dt_raw block landed
-  uint64_t* barW = bars + 1;        // W slab landed
-  uint64_t* barB = bars + 2;        // [NBB] B tile landed
-  uint64_t* barSplit = bars + 5;    // operands split, channel constants written (NEPI arrivals)
-  uint64_t* barMMA = bars + 6;      // [2] the tile's MMAs completed
-  uint64_t* barBfree = bars + 8;    // [NBB] epilogue done with that B buffer (NEPI arrivals)
-  uint64_t* barTfree = bars + 11;   // [2] epilogue done with that accumulator (NEPI arrivals)
-  uint64_t* barDrain = bars + 13;
+  uint64_t* barX = bars + 0;            // [NX] dt_raw stage landed
+  uint64_t* barSplit = bars + NX;       // [NX] stage split (and, first time, W in TMEM) (NEPI arrivals)
+  uint64_t* barMMA = bars + 2 * NX;     // [2] the tile's MMAs completed
+  uint64_t* barTfree = barMMA + 2;      // [2] epilogue done with that accumulator (NEPI arrivals)
+  uint64_t* barDrain = barTfree + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
-  const int per = (nitems + (int)gridDim.x - 1) / (int)gridDim.x;
   const int it0 = (int)blockIdx.x * per, it1 = min(nitems, it0 + per);
+  const int ntile = it1 - it0;
+  const int cb0 = it0 / nrb;   // the CTA's first channel block (its W slot 0)
 
   if (tid == 0) {
-    mbar_init(barA, 1);
-    mbar_init(barW, 1);
-    for (int i = 0; i < NBB; ++i) {
-      mbar_init(&barB[i], 1);
-      mbar_init(&barBfree[i], NEPI);
+    for (int i = 0; i < NX; ++i) {
+      mbar_init(&barX[i], 1);
+      mbar_init(&barSplit[i], NEPI);
     }
-    mbar_init(barSplit, NEPI);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&barMMA[i], 1);
       mbar_init(&barTfree[i], NEPI);
@@ -134,242 +120,173 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
     }
     return false;
   };
-  auto tile_mn = [&](int it, int& m0, int& n0) {
-    const int m = it / ntn;
-    m0 = m * TM;
-    n0 = (it - m * ntn) * TN;
-    return m;
-  };
+  const int natom = (R + 31) / 32;   // 32-wide K atoms (zero-filled past R)
 
   if (warp == NEPI / 32) {
     // ============================================================ loads and MMAs
-    if (lane == 0 && it0 < it1) {
+    if (lane == 0 && ntile > 0) {
       prefetch_tmap(&tmX);
-      prefetch_tmap(&tmW);
-      if (DISC) prefetch_tmap(&tmB);
-      constexpr uint32_t ID = make_idesc_tf32(TM, TN, false, false);
-      const int natom = (R + 31) / 32;   // 32-wide K atoms (zero-filled past R)
-      int last_m = -1, a_armed = 0, w_armed = 0, b_armed[NBB] = {0, 0, 0};
+      constexpr uint32_t ID = make_idesc_tf32(CM, RN, false, false);
+      int x_armed[NX] = {0, 0};
       bool ok = true;
-      auto issue_b = [&](int it) -> bool {   // B tile of tile it -> buffer (it - it0) % NBB
-        const int jb = it - it0, bb = jb % NBB;
-        if (jb >= NBB && !wait(&barBfree[bb], ((jb - NBB) / NBB) & 1, 9501)) return false;
-        int m0, n0;
-        tile_mn(it, m0, n0);
-        mbar_arrive_expect_tx(&barB[bb], 2 * HALF);
-        tma_load_2d(smem + OFF_B + bb * 2 * HALF, &tmB, n0, m0, &barB[bb]);
-        tma_load_2d(smem + OFF_B + bb * 2 * HALF + HALF, &tmB, n0 + 32, m0, &barB[bb]);
-        ++b_armed[bb];
-        return true;
+      auto issue_x = [&](int j) {   // dt_raw rows of tile j -> stage j % NX
+        const int st = j % NX, it = it0 + j;
+        const int m0 = (it % nrb) * RN;
+        uint8_t* dst = smem + OFF_X + st * X_STAGE;
+        mbar_arrive_expect_tx(&barX[st], (uint32_t)natom * X_ATOM);
+        for (int at = 0; at < natom; ++at) tma_load_2d(dst + at * X_ATOM, &tmX, 32 * at, m0, &barX[st]);
+        ++x_armed[st];
       };
-      if (DISC) ok = issue_b(it0);
-      for (int it = it0; ok && it < it1; ++it) {
-        const int j = it - it0, s = j & 1;
-        int m0, n0;
-        const int m = tile_mn(it, m0, n0);
-        DTP_TRACE(j, 0);
-        if (DISC && it + 1 < it1 && !(ok = issue_b(it + 1))) break;   // two tiles ahead of its epilogue
-        DTP_TRACE(j, 1);
-        // the previous tile's MMAs (and the split before them) are done with W and the dt_raw block
-        if (j >= 1 && !(ok = wait(&barMMA[(j - 1) & 1], ((j - 1) >> 1) & 1, 9502))) break;
-        DTP_TRACE(j, 2);
-        if (m != last_m) {
-          mbar_arrive_expect_tx(barA, A_RAW);
-          tma_load_2d(smem + OFF_A, &tmX, 0, m0, barA);
-          tma_load_2d(smem + OFF_A + A_RAW / 2, &tmX, 32, m0, barA);
-          ++a_armed;
-          last_m = m;
-        }
-        mbar_arrive_expect_tx(barW, W_PART);
-        tma_load_2d(smem + OFF_WHI, &tmW, n0, 0, barW);
-        tma_load_2d(smem + OFF_WHI + W_PART / 2, &tmW, n0 + 32, 0, barW);
-        ++w_armed;
-        if (!(ok = wait(barSplit, j & 1, 9503))) break;
-        if (j >= 2 && !(ok = wait(&barTfree[s], ((j - 2) >> 1) & 1, 9504))) break;
-        DTP_TRACE(j, 3);
+      issue_x(0);
+      if (ntile > 1) issue_x(1);
+      for (int j = 0; ok && j < ntile; ++j) {
+        const int s = j & 1, st = j % NX;
+        if (!(ok = wait(&barSplit[st], (j / NX) & 1, 9501))) break;
+        // the split of tile j followed the completion of tile j-1's MMAs: its stage is free
+        if (j >= 1 && j + 1 < ntile) issue_x(j + 1);
+        if (j >= 2 && !(ok = wait(&barTfree[s], ((j - 2) >> 1) & 1, 9502))) break;
         tc_fence_after();
-        const uint32_t d = tmem + TM_D + (uint32_t)(s * TN);
-        const uint64_t dWhi = make_desc_sw128(smem_u32(smem + OFF_WHI), 16);
-        const uint64_t dWlo = make_desc_sw128(smem_u32(smem + OFF_WLO), 16);
-        // hi.hi + hi.lo + lo.hi; A from TMEM (8 columns per K step), W K-major (32 B per
-        // K step, second 32-wide K atom 8 KB further on)
+        const int slot = (it0 + j) / nrb - cb0;
+        const uint32_t d = tmem + TM_D + (uint32_t)(s * RN);
+        const uint32_t whi = tmem + TM_W + (uint32_t)(slot * 2 * KM), wlo = whi + KM;
+        const uint32_t xs = smem_u32(smem + OFF_X + st * X_STAGE);
+        const uint64_t dXhi = make_desc_sw128(xs, 16), dXlo = make_desc_sw128(xs + X_PART, 16);
+        // W_hi.x_hi + W_hi.x_lo + W_lo.x_hi; A from TMEM (8 K columns per step), x K-major
+        // (32 B per step, the second K atom 16 KB further on)
 #pragma unroll 1
         for (int p = 0; p < 3; ++p) {
-          const uint32_t acol = tmem + (p == 2 ? TM_ALO : TM_AHI);
-          const uint64_t w = p == 1 ? dWlo : dWhi;
+          const uint32_t a = p == 2 ? wlo : whi;
+          const uint64_t x = p == 1 ? dXlo : dXhi;
 #pragma unroll 1
           for (int at = 0; at < natom; ++at)
-            umma_tf32_tmemA_x4(d, acol + (uint32_t)(32 * at), w + (uint64_t)((at * (W_PART / 2)) >> 4), ID,
+            umma_tf32_tmemA_x4(d, a + (uint32_t)(32 * at), x + (uint64_t)((at * X_ATOM) >> 4), ID,
                                (p | at) != 0);
         }
         umma_commit(&barMMA[s]);
-        DTP_TRACE(j, 4);
       }
       // this thread's MMAs complete before teardown; after a failed wait, the loads it
       // armed complete too (every wait below is bounded)
       umma_commit(barDrain);
       mbar_wait(barDrain, 0, nullptr, 100000000ull);
-      if (!ok) {
-        if (a_armed) mbar_wait(barA, (a_armed - 1) & 1, nullptr, 100000000ull);
-        if (w_armed) mbar_wait(barW, (w_armed - 1) & 1, nullptr, 100000000ull);
-        for (int b = 0; b < NBB; ++b)
-          if (b_armed[b]) mbar_wait(&barB[b], (b_armed[b] - 1) & 1, nullptr, 100000000ull);
-      }
+      if (!ok)
+        for (int st = 0; st < NX; ++st)
+          if (x_armed[st]) mbar_wait(&barX[st], (x_armed[st] - 1) & 1, nullptr, 100000000ull);
     }
-  } else {
-    // ============================================================ split + epilogue
-    // Warps w, w+4, w+8, w+12 share TMEM lanes 32*(w%4) ..: thread = (tile row r,
-    // quarter qt: 16 channels of the epilogue, 16 K columns of the A split).  After
-    // the MMAs of tile j complete, the operands of tile j+1 are split first, so its
-    // MMAs run while tile j's epilogue computes.
-    int last_m = -1, a_seen = 0;
-    const int r = tid & (TM - 1), qt = tid / TM;
-    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
-    auto split_tile = [&](int it) -> bool {
-      const int j = it - it0, s = j & 1;
-      int m0, n0;
-      const int m = tile_mn(it, m0, n0);
-      if (tid == 0) DTP_TRACE(j, 5);
-      if (m != last_m) {
-        // this thread's 16 K columns of row r: hi and lo into the A columns of TMEM
-        if (!wait(barA, a_seen & 1, 9511)) return false;
-        ++a_seen;
-        last_m = m;
-        const uint8_t* row = smem + OFF_A + (qt >> 1) * (A_RAW / 2) + r * 128;
-        float hi[16], lo[16];
+  } else if (ntile > 0) {
+    // ============================================================ W, split, epilogue
+    const int wq = warp & 3, qt = warp >> 2;   // TMEM lane quarter (channels), row quarter
+    const int co = 32 * wq + lane;             // this thread's channel within a block
+    const uint32_t tlane = (uint32_t)(32 * wq) << 16;
+    const int nslot = (it1 - 1) / nrb - cb0 + 1;   // 1 or 2 (the host checks)
+    // W of the CTA's channel blocks, split, into TMEM: lane = channel, column = k;
+    // this thread writes its channel's 16 K columns [16 qt, 16 qt + 16)
+    float cbias[2], ca[2], cra[2];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t q = (uint32_t)((qt & 1) * 4 + c);
-          const float4 x = *reinterpret_cast<const float4*>(row + (((q ^ ((uint32_t)r & 7u)) & 7u) << 4));
-          const float xs[4] = {x.x, x.y, x.z, x.w};
+    for (int sl = 0; sl < 2; ++sl) {
+      const int c = (cb0 + sl) * CM + co;
+      const bool live = sl < nslot && c < H;
+      float hi[16], lo[16];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            hi[c * 4 + e] = tf32_round(xs[e]);
-            lo[c * 4 + e] = xs[e] - hi[c * 4 + e];
-          }
-        }
-        tmem_st16(tmem + tlane + TM_AHI + (uint32_t)(qt * 16), hi);
-        tmem_st16(tmem + tlane + TM_ALO + (uint32_t)(qt * 16), lo);
-        tmem_wait_st();
+      for (int e = 0; e < 16; ++e) {
+        const int k = 16 * qt + e;
+        const float w = (live && k < R) ? __ldg(W + (int64_t)k * H + c) : 0.f;
+        hi[e] = tf32_round(w);
+        lo[e] = w - hi[e];
       }
-      if (tid == 0) DTP_TRACE(j, 6);
-      if (!wait(barW, j & 1, 9512)) return false;
-      if (tid == 0) DTP_TRACE(j, 7);
-      {
-        // W as landed ([k][32 n] 128-byte rows per 32-channel block) -> hi/lo in K-major
-        // tiles ([n][32 k] 128-byte rows per 32-wide K atom), the layout the MMA reads
-        // (an MN-major tf32 operand read back as zeros here); the slab is read into
-        // registers first so the hi tile can be written over it
-        constexpr int WE = KM * TN / NEPI;   // elements of the slab per thread
-        float wv[WE];
-#pragma unroll
-        for (int e = 0; e < WE; ++e) {
-          const int idx = tid + e * NEPI, k = idx & 63, nn = idx >> 6;
-          const uint32_t so = (uint32_t)(nn >> 5) * (W_PART / 2) + (uint32_t)k * 128u +
-                              (((((uint32_t)(nn & 31) >> 2) ^ ((uint32_t)k & 7u)) & 7u) << 4) + ((uint32_t)nn & 3u) * 4u;
-          wv[e] = *reinterpret_cast<const float*>(smem + OFF_WHI + so);
-        }
-        named_bar_sync(2, NEPI);
-#pragma unroll
-        for (int e = 0; e < WE; ++e) {
-          const int idx = tid + e * NEPI, k = idx & 63, nn = idx >> 6;
-          const uint32_t d = (uint32_t)(k >> 5) * (W_PART / 2) + (uint32_t)nn * 128u +
-                             (((((uint32_t)(k & 31) >> 2) ^ ((uint32_t)nn & 7u)) & 7u) << 4) + ((uint32_t)k & 3u) * 4u;
-          const float h = tf32_round(wv[e]);
-          *reinterpret_cast<float*>(smem + OFF_WHI + d) = h;
-          *reinterpret_cast<float*>(smem + OFF_WLO + d) = wv[e] - h;
-        }
+      if (sl < nslot) {
+        tmem_st16(tmem + tlane + TM_W + (uint32_t)(sl * 2 * KM + 16 * qt), hi);
+        tmem_st16(tmem + tlane + TM_W + (uint32_t)(sl * 2 * KM + KM + 16 * qt), lo);
       }
-      float* col = reinterpret_cast<float*>(smem + OFF_COL) + s * 3 * TN;
-      if (tid < TN) {
-        const int h = n0 + tid;
-        col[tid] = h < H ? bias[h] : 0.f;
-        if (DISC) {
-          const float a = h < H ? -expf(A_log[h]) : -1.f;
-          col[TN + tid] = a;
-          col[2 * TN + tid] = 1.0f / (a + 1e-12f);
-        }
+      cbias[sl] = live ? __ldg(bias + c) : 0.f;
+      ca[sl] = (DISC && live) ? -expf(__ldg(A_log + c)) : -1.f;
+      cra[sl] = 1.0f / (ca[sl] + 1e-12f);
+    }
+    tmem_wait_st();
+    // the landed dt_raw rows of tile j, split in place: hi over the rows, lo beside
+    // them (elementwise, so the swizzled layout needs no index arithmetic)
+    auto split_tile = [&](int j) -> bool {
+      const int st = j % NX;
+      if (!wait(&barX[st], (j / NX) & 1, 9511)) return false;
+      float4* xh = reinterpret_cast<float4*>(smem + OFF_X + st * X_STAGE);
+      float4* xl = reinterpret_cast<float4*>(smem + OFF_X + st * X_STAGE + X_PART);
+      const int n4 = natom * (int)(X_ATOM / 16);
+      for (int q = tid; q < n4; q += NEPI) {
+        const float4 x = xh[q];
+        float4 h;
+        h.x = tf32_round(x.x); h.y = tf32_round(x.y); h.z = tf32_round(x.z); h.w = tf32_round(x.w);
+        xh[q] = h;
+        xl[q] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
       }
-      fence_proxy_async_smem();   // the W tiles are read by the tensor core (async proxy)
-      tc_fence_before();          // and so are the A columns written to TMEM
-      named_bar_sync(2, NEPI);    // channel constants visible to every epilogue thread
-      mbar_arrive(barSplit);
-      if (tid == 0) DTP_TRACE(j, 8);
+      fence_proxy_async_smem();   // the stage is read by the tensor core (async proxy)
+      tc_fence_before();          // and, the first time, so are the W columns in TMEM
+      mbar_arrive(&barSplit[st]);
       return true;
     };
-    auto epilogue_tile = [&](int it) -> bool {
-      const int j = it - it0, s = j & 1, bb = j % NBB;
-      int m0, n0;
-      tile_mn(it, m0, n0);
-      if (DISC && !wait(&barB[bb], (j / NBB) & 1, 9514)) return false;
-      if (tid == 0) DTP_TRACE(j, 10);
-      const float* col = reinterpret_cast<const float*>(smem + OFF_COL) + s * 3 * TN;
-      float acc[16];
-      tmem_ld16(tmem + tlane + TM_D + (uint32_t)(s * TN + qt * 16), acc);
+    // B values of this thread's 32 rows of tile j, one per register
+    float bv[32];
+    auto tile_rc = [&](int j, int& row0, int& c) {
+      const int it = it0 + j;
+      row0 = (it % nrb) * RN + 32 * qt;
+      c = (it / nrb) * CM + co;
+    };
+    if (DISC) {
+      int row0, c;
+      tile_rc(0, row0, c);
+      const float* bp = B + (int64_t)row0 * H + c;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) bv[i] = (c < H && row0 + i < rows) ? __ldcs(bp + (int64_t)i * H) : 0.f;
+    }
+    bool ok = split_tile(0);
+    for (int j = 0; ok && j < ntile; ++j) {
+      const int s = j & 1;
+      ok = wait(&barMMA[s], (j >> 1) & 1, 9512);
+      if (ok && j + 1 < ntile) {
+        tc_fence_after();
+        ok = split_tile(j + 1);
+      }
+      // the warp leaves together: the TMEM load below is a whole-warp instruction
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      float acc[32];
+      tmem_ld32(tmem + tlane + TM_D + (uint32_t)(s * RN + 32 * qt), acc);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&barTfree[s]);   // this thread is done with the accumulator
-      // the previous tile's stores have finished reading the staging tiles
-      if (tid == 0) bulk_wait_read<0>();
-      named_bar_sync(1, NEPI);
-      if (tid == 0) DTP_TRACE(j, 11);
-      const int hf = qt >> 1;               // 32-channel half (one swizzled [128 x 128 B] tile)
-      uint8_t* o0 = smem + OFF_O + hf * 2 * HALF;
-      uint8_t* o1 = o0 + HALF;
-      const uint8_t* bt = smem + OFF_B + bb * 2 * HALF + hf * HALF;
+      int row0, c;
+      tile_rc(j, row0, c);
+      const int slot = (it0 + j) / nrb - cb0;
+      const float bs = slot ? cbias[1] : cbias[0];
+      const bool cl = c < H;
+      const int64_t o = (int64_t)row0 * H + c;
+      if (DISC) {
+        const float a = slot ? ca[1] : ca[0], ra = slot ? cra[1] : cra[0];
+        int row0n = 0, cn = H;
+        if (j + 1 < ntile) tile_rc(j + 1, row0n, cn);
+        const float* bpn = B + (int64_t)row0n * H + cn;
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const uint32_t q = (uint32_t)((qt & 1) * 4 + q4);   // 16-byte chunk of the 128-byte row
-        const uint32_t off = (uint32_t)r * 128u + (((q ^ ((uint32_t)r & 7u)) & 7u) << 4);
-        float bv[4] = {0.f, 0.f, 0.f, 0.f};
-        if (DISC) {
-          const float4 t = *reinterpret_cast<const float4*>(bt + off);
-          bv[0] = t.x; bv[1] = t.y; bv[2] = t.z; bv[3] = t.w;
-        }
-        float y0[4], y1[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = qt * 16 + q4 * 4 + e;
-          const float v = acc[q4 * 4 + e] + col[c];
-          const float dtv = fminf(fmaxf(logf(1.0f + expf(v)), dt_min), dt_max);
-          if (DISC) {
-            const float x = dtv * col[TN + c];
-            const float ex = expf(x);
-            y0[e] = ex;
-            y1[e] = expm1_guard_f32(x, ex) * col[2 * TN + c] * bv[e];
-          } else {
-            y0[e] = dtv;
-            y1[e] = 0.f;
+        for (int i = 0; i < 32; ++i) {
+          const float v = acc[i] + bs;
+          const float dtv = fminf(fmaxf(__logf(1.0f + __expf(v)), dt_min), dt_max);
+          const float x = dtv * a;
+          const float e = __expf(x);
+          const float bb = expm1_guard_f32(x, e) * ra * bv[i];
+          if (cl && row0 + i < rows) {
+            __stcs(out0 + o + (int64_t)i * H, e);
+            __stcs(out1 + o + (int64_t)i * H, bb);
+            if (dt_out) __stcs(dt_out + o + (int64_t)i * H, dtv);
           }
+          // the next tile's B value for this register, loaded while this tile finishes
+          bv[i] = (cn < H && row0n + i < rows) ? __ldcs(bpn + (int64_t)i * H) : 0.f;
         }
-        *reinterpret_cast<float4*>(o0 + off) = make_float4(y0[0], y0[1], y0[2], y0[3]);
-        if (DISC) *reinterpret_cast<float4*>(o1 + off) = make_float4(y1[0], y1[1], y1[2], y1[3]);
-      }
-      if (DISC) mbar_arrive(&barBfree[bb]);   // done with the B tile
-      fence_proxy_async_smem();
-      named_bar_sync(1, NEPI);
-      if (tid == 0) DTP_TRACE(j, 12);
-      if (tid == 0) {
+      } else {
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint8_t* p0 = smem + OFF_O + h2 * 2 * HALF;
-          tma_store_2d(&tmO0, p0, n0 + 32 * h2, m0);
-          if (DISC) tma_store_2d(&tmO1, p0 + HALF, n0 + 32 * h2, m0);
+        for (int i = 0; i < 32; ++i) {
+          const float v = acc[i] + bs;
+          const float dtv = fminf(fmaxf(__logf(1.0f + __expf(v)), dt_min), dt_max);
+          if (cl && row0 + i < rows) __stcs(out0 + o + (int64_t)i * H, dtv);
         }
-        bulk_commit();
       }
-      return true;
-    };
-    bool ok = it0 >= it1 || split_tile(it0);
-    for (int it = it0; ok && it < it1; ++it) {
-      const int j = it - it0, s = j & 1;
-      if (!(ok = wait(&barMMA[s], (j >> 1) & 1, 9513))) break;
-      if (tid == 0) DTP_TRACE(j, 9);
-      tc_fence_after();
-      if (it + 1 < it1 && !(ok = split_tile(it + 1))) break;
-      ok = epilogue_tile(it);
     }
-    if (tid == 0) bulk_wait<0>();
   }
   __syncthreads();
   if (warp == 0) {
@@ -380,47 +297,35 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
 
 }  // namespace
 
-#ifdef TSSM_DTPROJ_TRACE
-extern "C" int tssm_debug_read_dtp_trace(unsigned long long* out, int n) {
-  return cudaMemcpyFromSymbol(out, g_dtp_trace, sizeof(unsigned long long) * (n < 1024 ? n : 1024)) == cudaSuccess ? 0 : 3;
-}
-#endif
-
-// The tensor-core path: R <= 64, rows of dt_raw, W, B and the outputs 16-byte
-// aligned (R % 4 == 0, H % 4 == 0, 16-byte aligned bases), and no dt output in
-// the fused form.  Returns TSSM_ERR_UNSUPPORTED when those do not hold, so the
-// caller takes the CUDA-core kernel instead.
+// The tensor-core path: R <= 64 with R % 4 == 0 and a 16-byte aligned dt_raw
+// (its rows are TMA-loaded), fewer than 2^31 rows and channels, and at most two
+// channel blocks per CTA (H below about 148 x 128 x the row blocks' count per
+// CTA).  Returns TSSM_ERR_UNSUPPORTED when those do not hold, so the caller
+// takes the CUDA-core kernel instead.
 int launch_dtproj_tc(bool disc, const void* dt_raw, const void* W, const void* bias, const void* A_log, const void* B,
                      void* dt_out, void* Abar, void* Bbar, int64_t rows, int64_t H, int64_t R, double dt_min,
                      double dt_max, cudaStream_t st) {
-  if (R > KM || R % 4 || H % 4 || (disc && dt_out) || !aligned16(dt_raw) || !aligned16(W) ||
-      (disc ? !(aligned16(B) && aligned16(Abar) && aligned16(Bbar)) : !aligned16(dt_out)) ||
-      rows >= (int64_t(1) << 31) || H >= (int64_t(1) << 31))
+  if (R > KM || R % 4 || !aligned16(dt_raw) || rows >= (int64_t(1) << 31) - RN || H >= (int64_t(1) << 31) - CM)
     return TSSM_ERR_UNSUPPORTED;
+  const int64_t nrb = cdiv(rows, RN), ncb = cdiv(H, CM), nitems = nrb * ncb;
+  if (nitems >= (int64_t(1) << 31)) return TSSM_ERR_UNSUPPORTED;
+  const int64_t per = cdiv(nitems, std::min<int64_t>(nitems, num_sms()));
+  if (per > nrb) return TSSM_ERR_UNSUPPORTED;   // a CTA's range would meet a third channel block
   int* status = device_status_ptr();
   if (!status) {
     set_error("dt_project: device status word unavailable");
     return TSSM_ERR_CUDA;
   }
-  CUtensorMap mX, mW, mB, mO0, mO1;
-  void* o0 = disc ? Abar : dt_out;
-  void* o1 = disc ? Bbar : dt_out;
-  const void* bsrc = disc ? B : dt_out;
-  if (!tmap2d_f32_sw128(&mX, dt_raw, (uint64_t)R, (uint64_t)rows, TM) ||
-      !tmap2d_f32_sw128(&mW, W, (uint64_t)H, (uint64_t)R, KM) ||
-      !tmap2d_f32_sw128(&mB, bsrc, (uint64_t)H, (uint64_t)rows, TM) ||
-      !tmap2d_f32_sw128(&mO0, o0, (uint64_t)H, (uint64_t)rows, TM) ||
-      !tmap2d_f32_sw128(&mO1, o1, (uint64_t)H, (uint64_t)rows, TM)) {
-    return TSSM_ERR_UNSUPPORTED;   // e.g. a tensor narrower than one box: the CUDA-core kernel takes it
-  }
-  const int64_t ntm = cdiv(rows, TM), ntn = cdiv(H, TN), nitems = ntm * ntn;
-  TSSM_REQUIRE(nitems < (int64_t(1) << 31), "dt_project: size exceeds the grid");
-  const int grid = (int)std::min<int64_t>(nitems, num_sms());
+  CUtensorMap mX;
+  if (!tmap2d_f32_sw128(&mX, dt_raw, (uint64_t)R, (uint64_t)rows, RN)) return TSSM_ERR_UNSUPPORTED;
+  const int grid = (int)cdiv(nitems, per);
   auto kern = disc ? dtproj_tc_kernel<true> : dtproj_tc_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES) != cudaSuccess)
     return check_launch("dt_project: set smem attribute");
-  kern<<<grid, NTHR, SMEM_BYTES, st>>>(mX, mW, mB, mO0, mO1, (const float*)bias, (const float*)A_log, status,
-                                       (int)H, (int)R, (float)dt_min, (float)dt_max, (int)ntn, (int)nitems);
+  kern<<<grid, NTHR, SMEM_BYTES, st>>>(mX, (const float*)W, (const float*)bias, (const float*)A_log,
+                                       (const float*)B, (float*)(disc ? Abar : dt_out), (float*)Bbar,
+                                       (float*)(disc ? dt_out : nullptr), status, (int)rows, (int)H, (int)R,
+                                       (float)dt_min, (float)dt_max, (int)nrb, (int)nitems, (int)per);
   return check_launch(disc ? "zoh_discretize_dtproj" : "dt_project_softplus");
 }
 
