@@ -19,8 +19,10 @@
 // products hi.hi + hi.lo + lo.hi (the dropped lo.lo term is below 2^-22 of each
 // product: f32-accurate, as the 1e-4 parity bar needs).
 //
-// exp and log are the hardware approximations (ex2 / lg2 with a scale: relative
-// error near 2^-22), which is also how the reference's tl.exp / tl.log compile.
+// exp and log are the hardware approximations, exp(x) = 2^(x log2 e) and
+// log(u) = log2(u) ln 2 on ex2 / lg2 (relative error near 2^-22), which is also
+// how the reference's tl.exp / tl.log compile.  Full tiles take an epilogue
+// without per-row checks whose addresses advance by one row per step.
 //
 // Persistent CTAs (about one per SM) take a contiguous range of tiles, rows
 // fastest within a channel block, so a CTA meets at most two channel blocks:
@@ -69,6 +71,61 @@ __device__ __forceinline__ float tf32_round(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
+}
+
+constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+
+// Per-channel constants of an epilogue thread: bias * log2(e), a, a * log2(e)
+// and 1 / (a + 1e-12).
+struct ChanConst {
+  float bsl, a, al, ra;
+};
+
+// dt = clamp(softplus(acc + bias)) with exp(v) = 2^(v log2 e) and
+// log(u) = log2(u) ln 2 on the hardware approximations.
+__device__ __forceinline__ float softplus_clamped(float acc, const ChanConst& k, float dt_min, float dt_max) {
+  const float t = fast_exp2(fmaf(acc, kLog2e, k.bsl));
+  return fminf(fmaxf(fast_log2(1.0f + t) * kLn2, dt_min), dt_max);
+}
+
+// The fused epilogue over 16 of this thread's rows of one tile (one channel),
+// rows I0 .. I0+15 of its 32: stores Abar, Bbar (and dt when dto, on the
+// checked path only) row by row, and when NEXT loads the next tile's B values
+// into the registers this tile has consumed.  CHECK guards rows past the end
+// (nv, nvn valid rows of this tile and the next); without it every access is
+// unconditional and each stream's address is bumped by one row.
+template <bool CHECK, bool NEXT, int I0>
+__device__ __forceinline__ void epi_disc_rows(const float (&acc)[16], float (&bv)[32], const ChanConst& k,
+                                              float dt_min, float dt_max, float*& p0, float*& p1, float*& pd,
+                                              const float*& pb, int64_t H, int nv, int nvn, bool dto) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float dtv = softplus_clamped(acc[i], k, dt_min, dt_max);
+    const float x = dtv * k.a;
+    const float e = fast_exp2(dtv * k.al);
+    const float bb = expm1_guard_f32(x, e) * (k.ra * bv[I0 + i]);
+    if (!CHECK || I0 + i < nv) {
+      __stcs(p0, e);
+      __stcs(p1, bb);
+      if (CHECK && dto) __stcs(pd, dtv);
+    }
+    if (NEXT) bv[I0 + i] = (!CHECK || I0 + i < nvn) ? __ldcs(pb) : 0.f;
+    p0 += H;
+    p1 += H;
+    if (CHECK && dto) pd += H;
+    if (NEXT) pb += H;
+  }
+}
+
+template <bool CHECK, int I0>
+__device__ __forceinline__ void epi_dt_rows(const float (&acc)[16], const ChanConst& k, float dt_min, float dt_max,
+                                            float*& p0, int64_t H, int nv) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float dtv = softplus_clamped(acc[i], k, dt_min, dt_max);
+    if (!CHECK || I0 + i < nv) __stcs(p0, dtv);
+    p0 += H;
+  }
 }
 
 template <bool DISC>
@@ -180,7 +237,7 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
     const int nslot = (it1 - 1) / nrb - cb0 + 1;   // 1 or 2 (the host checks)
     // W of the CTA's channel blocks, split, into TMEM: lane = channel, column = k;
     // this thread writes its channel's 16 K columns [16 qt, 16 qt + 16)
-    float cbias[2], ca[2], cra[2];
+    ChanConst kc[2];
 #pragma unroll
     for (int sl = 0; sl < 2; ++sl) {
       const int c = (cb0 + sl) * CM + co;
@@ -197,9 +254,10 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
         tmem_st16(tmem + tlane + TM_W + (uint32_t)(sl * 2 * KM + 16 * qt), hi);
         tmem_st16(tmem + tlane + TM_W + (uint32_t)(sl * 2 * KM + KM + 16 * qt), lo);
       }
-      cbias[sl] = live ? __ldg(bias + c) : 0.f;
-      ca[sl] = (DISC && live) ? -expf(__ldg(A_log + c)) : -1.f;
-      cra[sl] = 1.0f / (ca[sl] + 1e-12f);
+      kc[sl].bsl = (live ? __ldg(bias + c) : 0.f) * kLog2e;
+      kc[sl].a = (DISC && live) ? -expf(__ldg(A_log + c)) : -1.f;
+      kc[sl].al = kc[sl].a * kLog2e;
+      kc[sl].ra = 1.0f / (kc[sl].a + 1e-12f);
     }
     tmem_wait_st();
     // the landed dt_raw rows of tile j, split in place: hi over the rows, lo beside
@@ -224,18 +282,21 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
     };
     // B values of this thread's 32 rows of tile j, one per register
     float bv[32];
-    auto tile_rc = [&](int j, int& row0, int& c) {
+    // tile j's first row for this thread, its channel, and how many of its 32 rows exist
+    auto tile_rc = [&](int j, int& row0, int& c) -> int {
       const int it = it0 + j;
       row0 = (it % nrb) * RN + 32 * qt;
       c = (it / nrb) * CM + co;
+      return c < H ? max(0, min(32, rows - row0)) : 0;
     };
     if (DISC) {
       int row0, c;
-      tile_rc(0, row0, c);
+      const int nv = tile_rc(0, row0, c);
       const float* bp = B + (int64_t)row0 * H + c;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) bv[i] = (c < H && row0 + i < rows) ? __ldcs(bp + (int64_t)i * H) : 0.f;
+      for (int i = 0; i < 32; ++i) bv[i] = i < nv ? __ldcs(bp + (int64_t)i * H) : 0.f;
     }
+    const int64_t H64 = H;
     bool ok = split_tile(0);
     for (int j = 0; ok && j < ntile; ++j) {
       const int s = j & 1;
@@ -244,47 +305,46 @@ __global__ void __launch_bounds__(NTHR, 1) dtproj_tc_kernel(
         tc_fence_after();
         ok = split_tile(j + 1);
       }
-      // the warp leaves together: the TMEM load below is a whole-warp instruction
+      // the warp leaves together: the TMEM loads below are whole-warp instructions
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
-      float acc[32];
-      tmem_ld32(tmem + tlane + TM_D + (uint32_t)(s * RN + 32 * qt), acc);
+      int row0, c;
+      const int nv = tile_rc(j, row0, c);
+      const ChanConst& k = ((it0 + j) / nrb - cb0) ? kc[1] : kc[0];
+      const int64_t o = (int64_t)row0 * H + c;
+      const bool next = DISC && j + 1 < ntile;
+      int row0n = 0, cn = 0;
+      const int nvn = next ? tile_rc(j + 1, row0n, cn) : 0;
+      float* p0 = out0 + o;
+      float* p1 = DISC ? out1 + o : nullptr;
+      float* pd = (DISC && dt_out) ? dt_out + o : nullptr;
+      const float* pb = B + (int64_t)row0n * H + cn;
+      const bool fast = nv == 32 && !pd && (nvn == 32 || !next);
+      const bool dto = pd != nullptr;
+      // the accumulator's 32 columns in two halves of 16 (register budget)
+      const uint32_t dcol = tmem + tlane + TM_D + (uint32_t)(s * RN + 32 * qt);
+      float acc[16];
+      tmem_ld16(dcol, acc);
+      tmem_wait_ld();
+      if (DISC) {
+        if (fast && next) epi_disc_rows<false, true, 0>(acc, bv, k, dt_min, dt_max, p0, p1, pd, pb, H64, nv, nvn, dto);
+        else if (fast) epi_disc_rows<false, false, 0>(acc, bv, k, dt_min, dt_max, p0, p1, pd, pb, H64, nv, nvn, dto);
+        else epi_disc_rows<true, true, 0>(acc, bv, k, dt_min, dt_max, p0, p1, pd, pb, H64, nv, nvn, dto);
+      } else {
+        if (fast) epi_dt_rows<false, 0>(acc, k, dt_min, dt_max, p0, H64, nv);
+        else epi_dt_rows<true, 0>(acc, k, dt_min, dt_max, p0, H64, nv);
+      }
+      tmem_ld16(dcol + 16, acc);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&barTfree[s]);   // this thread is done with the accumulator
-      int row0, c;
-      tile_rc(j, row0, c);
-      const int slot = (it0 + j) / nrb - cb0;
-      const float bs = slot ? cbias[1] : cbias[0];
-      const bool cl = c < H;
-      const int64_t o = (int64_t)row0 * H + c;
       if (DISC) {
-        const float a = slot ? ca[1] : ca[0], ra = slot ? cra[1] : cra[0];
-        int row0n = 0, cn = H;
-        if (j + 1 < ntile) tile_rc(j + 1, row0n, cn);
-        const float* bpn = B + (int64_t)row0n * H + cn;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v = acc[i] + bs;
-          const float dtv = fminf(fmaxf(__logf(1.0f + __expf(v)), dt_min), dt_max);
-          const float x = dtv * a;
-          const float e = __expf(x);
-          const float bb = expm1_guard_f32(x, e) * ra * bv[i];
-          if (cl && row0 + i < rows) {
-            __stcs(out0 + o + (int64_t)i * H, e);
-            __stcs(out1 + o + (int64_t)i * H, bb);
-            if (dt_out) __stcs(dt_out + o + (int64_t)i * H, dtv);
-          }
-          // the next tile's B value for this register, loaded while this tile finishes
-          bv[i] = (cn < H && row0n + i < rows) ? __ldcs(bpn + (int64_t)i * H) : 0.f;
-        }
+        if (fast && next) epi_disc_rows<false, true, 16>(acc, bv, k, dt_min, dt_max, p0, p1, pd, pb, H64, nv, nvn, dto);
+        else if (fast) epi_disc_rows<false, false, 16>(acc, bv, k, dt_min, dt_max, p0, p1, pd, pb, H64, nv, nvn, dto);
+        else epi_disc_rows<true, true, 16>(acc, bv, k, dt_min, dt_max, p0, p1, pd, pb, H64, nv, nvn, dto);
       } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v = acc[i] + bs;
-          const float dtv = fminf(fmaxf(__logf(1.0f + __expf(v)), dt_min), dt_max);
-          if (cl && row0 + i < rows) __stcs(out0 + o + (int64_t)i * H, dtv);
-        }
+        if (fast) epi_dt_rows<false, 16>(acc, k, dt_min, dt_max, p0, H64, nv);
+        else epi_dt_rows<true, 16>(acc, k, dt_min, dt_max, p0, H64, nv);
       }
     }
   }

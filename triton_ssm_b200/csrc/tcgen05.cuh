@@ -103,6 +103,14 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// log2(x) with the hardware approximation (lg2.approx.ftz: absolute error near
+// 2^-22 for x near 1, relative elsewhere; subnormal inputs read as zero).
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ------------------------------------------------------------------ fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
