@@ -63,10 +63,13 @@ def test_discretize_dtproj_vs_composition(cuda_ops, Bt, T, H, R):
     assert rel_err(Ab2, Ab) < 1e-5 and rel_err(Bb2, Bb) < 1e-5
 
 
-@pytest.mark.parametrize("Bt,T,H,R", [(16, 64, 1024, 64), (3, 100, 200, 64), (2, 130, 68, 32), (1, 300, 520, 12)])
+@pytest.mark.parametrize("Bt,T,H,R", [(16, 64, 1024, 64), (3, 100, 200, 64), (2, 130, 68, 32), (1, 300, 520, 12),
+                                      (2, 40, 37, 8), (4, 96, 100, 16)])
 def test_dtproj_tensor_core_shapes(cuda_ops, Bt, T, H, R):
-    """Shapes the tcgen05 kernel takes (R <= 64, R and H multiples of 4), with
-    partial 128-row and 64-channel tiles and K padded past R, against the oracle."""
+    """Shapes the tcgen05 kernel takes (R <= 64, R a multiple of 4), against the
+    oracle: partial 128-row and 128-channel tiles, K padded past R, warp blocks
+    split between the 16-byte staged epilogue and the checked one, and H % 4 != 0
+    (every block on the checked epilogue)."""
     dt_raw, W, bias, A_log, B = _inputs(Bt, T, H, R, seed=Bt * T + H + R)
     ref_dt = oracle.dt_project_softplus(dt_raw, W, bias, 1e-3, 0.1)
     rA, rB = oracle.zoh_discretize_dt(A_log, B, ref_dt)
