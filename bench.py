@@ -608,7 +608,7 @@ def run_ours_c2(args, rank, world, local):
     # ---- end to end through the public host-buffer API (pinned host memory)
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd)
+        e2e = run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd, t_step)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -623,9 +623,18 @@ def run_ours_c2(args, rank, world, local):
                  "ssd_chunk_scan_c2.md", clocks, cpu=cpu, e2e=e2e)
 
 
-def run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd):
-    from triton_ssm_b200.host import SSDHostPipeline
+def run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd, t_kernel):
+    from triton_ssm_b200.host import SSDHostPipeline, bind_host_to_gpu, pinned_copy_gbs
     e2e_steps = max(3, min(args.steps, 20))
+    # pinned buffers on the GPU's NUMA node, then the host link measured with
+    # every rank copying at once (the bound the host-buffer path runs against)
+    numa = bind_host_to_gpu(dev)
+    barrier(world)
+    h2d_gbs, d2h_gbs = pinned_copy_gbs(dev)
+    # the slowest rank's link
+    h2d_gbs = 1.0 / max_over_ranks(1.0 / h2d_gbs, world)
+    d2h_gbs = 1.0 / max_over_ranks(1.0 / d2h_gbs, world)
+    barrier(world)
     host = {k: v.cpu().pin_memory() for k, v in inp.items()}
     y_h = torch.empty(y.shape, dtype=y.dtype).pin_memory()
     pipe = SSDHostPipeline(Bt, L, H, P, N, dev, nslices=8)
@@ -646,10 +655,18 @@ def run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd):
     # spot-check the host result against the device result
     if not torch.equal(y_h.to(dev), y):
         raise RuntimeError("host-pipeline output differs from the device run")
+    h2d_ms = pipe.h2d_bytes() / (h2d_gbs * 1e9) * 1e3
     return {"value": world * upd / e2e_t, "unit": UNIT, "h2d_bytes_per_step": pipe.h2d_bytes(),
             "d2h_bytes_per_step": pipe.d2h_bytes(), "ms_per_step": e2e_t * 1e3, "steps": e2e_steps,
             "gpu_launches": len(pipe.slices) * e2e_steps,
-            "path": "triton_ssm_b200.host.SSDHostPipeline (pinned host buffers, 8 batch slices)"}
+            "path": "triton_ssm_b200.host.SSDHostPipeline (pinned host buffers, 8 batch slices)",
+            "host_link": {"h2d_gbs": round(h2d_gbs, 2), "d2h_gbs": round(d2h_gbs, 2),
+                          "numa_node": numa["numa_node"] if numa else None,
+                          "bound_cpus": numa["cpus"] if numa else None,
+                          "binding": numa["source"] if numa else "none (one NUMA node, or the GPU's CPUs are all allowed ones)",
+                          "how": "256 MiB pinned copies timed with CUDA events, all %d rank(s) at once" % world},
+            "limit": "host->device copies: %.2f ms of the %.2f ms step at the slowest rank's measured %.1f GB/s; "
+                     "the scan kernel is %.3f ms" % (h2d_ms, e2e_t * 1e3, h2d_gbs, t_kernel * 1e3)}
 
 
 SUB_KEYS = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "scaling", "dtype", "config", "roofline",

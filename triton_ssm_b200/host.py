@@ -4,9 +4,110 @@ overlapped across batch slices on three CUDA streams (two copy engines and
 the SMs work at once).  Device buffers are allocated once per pipeline object
 and reused.
 """
+import os
+
 import torch
 
 from . import ops
+
+
+def gpu_numa_node(device):
+    """NUMA node of the GPU's PCI device (sysfs), or None where the platform
+    does not say (single-node hosts report -1)."""
+    props = torch.cuda.get_device_properties(torch.device(device))
+    bus = "%04x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+    try:
+        with open("/sys/bus/pci/devices/%s/numa_node" % bus) as f:
+            node = int(f.read().strip())
+    except (OSError, ValueError):
+        return None
+    return node if node >= 0 else None
+
+
+def parse_cpulist(text):
+    """CPU ids of a kernel cpulist string ("0-7,16-23")."""
+    cpus = set()
+    for part in filter(None, text.strip().split(",")):
+        lo, _, hi = part.partition("-")
+        cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def node_cpus(node):
+    """CPU ids of a NUMA node (empty when sysfs does not list it)."""
+    try:
+        with open("/sys/devices/system/node/node%d/cpulist" % node) as f:
+            return parse_cpulist(f.read())
+    except OSError:
+        return set()
+
+
+def gpu_ideal_cpus(device):
+    """The CPUs NVML reports as nearest the GPU (a read-only query), or an
+    empty set when NVML is unavailable."""
+    try:
+        import pynvml
+    except ImportError:
+        return set()
+    props = torch.cuda.get_device_properties(torch.device(device))
+    bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+    cpus = set()
+    try:
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+            for w, mask in enumerate(words):
+                cpus.update(64 * w + i for i in range(64) if (int(mask) >> i) & 1)
+        finally:
+            pynvml.nvmlShutdown()
+    except pynvml.NVMLError:
+        return set()
+    return cpus
+
+
+def bind_host_to_gpu(device):
+    """Restrict this process's CPUs to those nearest the GPU -- its NUMA node's
+    (sysfs), else the set NVML reports -- so pinned buffers allocated (first
+    touched) afterwards sit in the memory nearest the GPU's PCIe root and host
+    copies do not cross the inter-socket link.  Returns {"numa_node", "cpus",
+    "source"} or None when neither source narrows the allowed CPUs (the
+    affinity is then left as it was)."""
+    allowed = set(os.sched_getaffinity(0))
+    node = gpu_numa_node(device)
+    cpus, source = (node_cpus(node) & allowed, "sysfs") if node is not None else (set(), None)
+    if not cpus:
+        cpus, source = gpu_ideal_cpus(device) & allowed, "nvml"
+    if not cpus or cpus == allowed:
+        return None
+    os.sched_setaffinity(0, cpus)
+    return {"numa_node": node, "cpus": len(cpus), "source": source}
+
+
+def pinned_copy_gbs(device, nbytes=256 << 20, reps=4):
+    """(host->device, device->host) GB/s of one pinned buffer of `nbytes`,
+    timed with CUDA events on a side stream (the best of `reps` copies each)."""
+    dev = torch.device(device)
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s = torch.cuda.Stream(dev)
+    best = []
+    for direction in ("h2d", "d2h"):
+        times = []
+        with torch.cuda.stream(s):
+            for _ in range(reps + 1):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                if direction == "h2d":
+                    d.copy_(h, non_blocking=True)
+                else:
+                    h.copy_(d, non_blocking=True)
+                e1.record(s)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1) / 1e3)
+        best.append(nbytes / min(times[1:]) / 1e9)
+    return best[0], best[1]
 
 
 class SSDHostPipeline:
