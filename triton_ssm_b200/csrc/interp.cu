@@ -891,7 +891,7 @@ constexpr size_t kScanSmem = 2 * RMAX * 32 * 4 + 3 * QB * sizeof(Nbr) + 2 * QB *
 // 32 features) one block ahead, both completing on mbarriers; each block's
 // values are interpolated from the staged rows into registers eight queries
 // at a time, and the outputs go out as coalesced 128-byte rows.
-constexpr int CH_WARPS = 8;   // chunks (warps) per CTA
+constexpr int CH_WARPS = 8;   // chunks of a (b, 32 features) row, one warp each
 constexpr int CTS = 3;        // table slots: block k running, k+1 landed, k+2 in flight
 constexpr int CRB = 2;        // row buffers: block k running, k+1 in flight
 
@@ -901,9 +901,9 @@ struct alignas(128) ChunkWarpSmem {
   uint64_t tbar[CTS];
   uint64_t rbar[CRB];
 };
+template <int WPC>
 struct alignas(128) ChunkSmem {
-  ChunkWarpSmem w[CH_WARPS];
-  float2 carry[8][32];            // final state of the previous chunk (sequential mode)
+  ChunkWarpSmem w[WPC];
 };
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -928,18 +928,22 @@ __device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, uint64
   return sm100::mbar_test(bar, parity) || mbar_poll_slow(bar, parity, timeout_ns);
 }
 
-template <int NP2, bool VHAT>
-__global__ void __launch_bounds__(CH_WARPS * 32, 2) interp_ssm_scan_chunk_kernel(
+// WPC warps per CTA: the CTAs of one (b, 32 features) row take its CH_WARPS
+// chunks WPC at a time, so small CTAs spread the row's warps over every SM.
+template <int NP2, bool VHAT, int WPC>
+__global__ void __launch_bounds__(WPC * 32, 16 / WPC) interp_ssm_scan_chunk_kernel(
     const __grid_constant__ CUtensorMap tmV, const float* __restrict__ Vp, const int4* __restrict__ tabq,
     const float* __restrict__ A_log, const float* __restrict__ Bp, const float* __restrict__ Cp,
     const float* __restrict__ Dskip, const float* __restrict__ dt, float* __restrict__ y, float* __restrict__ h_last,
     float* __restrict__ vhat_out, int* __restrict__ status, int T, int Dm, int N, int Lq, int FTILE, int ntiles) {
   extern __shared__ __align__(16) uint8_t dsm[];
-  ChunkSmem& CS = *reinterpret_cast<ChunkSmem*>(dsm + ((128u - (sm100::smem_u32(dsm) & 127u)) & 127u));
+  ChunkSmem<WPC>& CS = *reinterpret_cast<ChunkSmem<WPC>*>(dsm + ((128u - (sm100::smem_u32(dsm) & 127u)) & 127u));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   ChunkWarpSmem& S = CS.w[warp];
   const int dpr = Dm / 32;
-  const int b = blockIdx.x / dpr, d0 = (blockIdx.x % dpr) * 32, d = d0 + lane;
+  constexpr int NGRP = CH_WARPS / WPC;   // CTAs per (b, 32 features) row
+  const int row = blockIdx.x / NGRP, chunk = (blockIdx.x % NGRP) * WPC + warp;
+  const int b = row / dpr, d0 = (row % dpr) * 32, d = d0 + lane;
   const int nblk = (Lq + WQB - 1) / WQB;
   const int4* tq = tabq + ((int64_t)b * ntiles + d0 / FTILE) * nblk * (WQB + 1);
   const float* Vl = Vp + (int64_t)b * T * Dm + d;   // this lane's feature; + row * Dm
@@ -992,8 +996,18 @@ __global__ void __launch_bounds__(CH_WARPS * 32, 2) interp_ssm_scan_chunk_kernel
     const float steps = amax > 0.f ? ceilf(40.0f / -log2f(amax)) : 0.f;
     if (steps < (float)(1 << 30)) wb = ((int)steps + WQB - 1) / WQB;
   }
+  // sequential mode (the warm-up would exceed a chunk): chunk 0's warp walks the
+  // whole row from a zero state -- the same recurrence as the chunks run in order
+  // with their final states carried -- and the other warps have nothing to do
   const bool sequential = wb >= chb && nblk > chb;
-  const int jc0 = min(nblk, warp * chb), jc1 = min(nblk, jc0 + chb);   // this chunk's output blocks
+  int jc0, jc1;   // this warp's output blocks
+  if (sequential) {
+    jc0 = 0;
+    jc1 = chunk == 0 ? nblk : 0;
+  } else {
+    jc0 = min(nblk, chunk * chb);
+    jc1 = min(nblk, jc0 + chb);
+  }
 
   bool alive = true;
   int t_issued = 0, t_done = 0, r_issued = 0, r_done = 0;   // this warp's copies: issued / waited
@@ -1131,23 +1145,9 @@ __global__ void __launch_bounds__(CH_WARPS * 32, 2) interp_ssm_scan_chunk_kernel
     }
   };
 
-  // warm-up mode: every warp walks its chunk at once; sequential mode: the
-  // chunks in order, each starting from the previous one's final state
-#pragma unroll 1
-  for (int p = 0; p < (sequential ? CH_WARPS : 1); ++p) {
-    if (jc0 < jc1 && (!sequential || warp == p)) {
-      if (sequential && p > 0) {
-#pragma unroll
-        for (int k = 0; k < NP2; ++k) g2[k] = CS.carry[k][lane];
-      }
-      walk(sequential ? jc0 : max(0, jc0 - wb), jc0, jc1);
-      if (sequential) {
-#pragma unroll
-        for (int k = 0; k < NP2; ++k) CS.carry[k][lane] = g2[k];
-      }
-    }
-    if (sequential) __syncthreads();
-  }
+  // warm-up mode: every warp walks its chunk from wb blocks early; sequential
+  // mode: one warp walks the row
+  if (jc0 < jc1) walk(sequential ? 0 : max(0, jc0 - wb), jc0, jc1);
   if (!alive) {
     // copies still in flight after a failed wait: wait for them (bounded) before the CTA exits
     for (; t_done < t_issued; ++t_done) mbar_poll(&S.tbar[t_done % CTS], (uint32_t)((t_done / CTS) & 1), 100000000ull);
@@ -1342,19 +1342,23 @@ extern "C" int tssm_interp_ssm(const void* V, const void* Mk, const void* tau, c
       set_error("interp_ssm: device status word unavailable");
       return TSSM_ERR_CUDA;
     }
-    TSSM_REQUIRE(Bsz * (Dm / 32) < (int64_t(1) << 31), "interp_ssm: size exceeds the grid");
+    TSSM_REQUIRE(Bsz * (Dm / 32) * CH_WARPS < (int64_t(1) << 31), "interp_ssm: size exceeds the grid");
     CUtensorMap tmV;
     if (!tmap3d_f32(&tmV, V, (uint64_t)Dm, (uint64_t)T, (uint64_t)Bsz, 32, WRB)) {
       set_error("interp_ssm: cuTensorMapEncodeTiled failed");
       return TSSM_ERR_CUDA;
     }
-    const size_t shm = sizeof(ChunkSmem) + 128;   // + alignment slack
+    // one CTA per row (eight warps, two CTAs per SM).  Two- and one-warp CTAs,
+    // which spread the warps over every SM, measured 5 % slower on config 3
+    // (same results): the busier chip runs at a lower clock under the power cap.
+    constexpr int WPC = 8;
+    const size_t shm = sizeof(ChunkSmem<WPC>) + 128;   // + alignment slack
 #define CHUNK_SCAN_LAUNCH(NP2, VH)                                                                              \
   do {                                                                                                          \
-    auto kern = interp_ssm_scan_chunk_kernel<NP2, VH>;                                                         \
+    auto kern = interp_ssm_scan_chunk_kernel<NP2, VH, WPC>;                                                    \
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm) != cudaSuccess)       \
       return check_launch("interp_ssm: scan smem");                                                             \
-    kern<<<(unsigned)(Bsz * (Dm / 32)), CH_WARPS * 32, shm, st>>>(                                              \
+    kern<<<(unsigned)(Bsz * (Dm / 32) * (CH_WARPS / WPC)), WPC * 32, shm, st>>>(                              \
         tmV, Vf, reinterpret_cast<const int4*>(tab), (const float*)A_log, (const float*)B, (const float*)C,     \
         (const float*)Dskip, (const float*)dt, (float*)y, (float*)h_last, (float*)vhat, status, (int)T,         \
         (int)Dm, (int)N, (int)Lq, (int)FTILE, ntiles);                                                          \
