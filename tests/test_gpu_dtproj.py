@@ -87,3 +87,34 @@ def test_dt_project_rejects_bad_args(cuda_ops):
         cuda_ops.dt_project_softplus(z(2, 3, 300), z(300, 6), z(6))   # R > 256, refused by the library
     with pytest.raises(ValueError):
         cuda_ops.dt_project_softplus(z(2, 3, 4), z(4, 6), z(6), 1.0, 0.5)
+
+
+@pytest.mark.parametrize("Bt,T,H,R", [(1, 1, 4, 4), (1, 5, 20, 60), (3, 77, 300, 40), (2, 64, 256, 64)])
+def test_dtproj_tensor_core_small_and_odd(cuda_ops, Bt, T, H, R):
+    """Tiny and odd shapes on the tcgen05 kernel: one row, fewer than 32 rows or
+    channels, K padded past R inside a 32-wide atom, whole and partial blocks;
+    both outputs of the fused form and the dt-only form, with and without dt."""
+    dt_raw, W, bias, A_log, B = _inputs(Bt, T, H, R, seed=7 * T + H + R)
+    ref_dt = oracle.dt_project_softplus(dt_raw, W, bias, 1e-3, 0.1)
+    rA, rB = oracle.zoh_discretize_dt(A_log, B, ref_dt)
+    Ab, Bb, dt = cuda_ops.zoh_discretize_dtproj(cu(A_log), cu(B), cu(dt_raw), cu(W), cu(bias), 1e-3, 0.1,
+                                                return_dt=True)
+    assert rel_err(Ab, rA) < 1e-5 and rel_err(Bb, rB) < 1e-5 and rel_err(dt, ref_dt) < 1e-5
+    dt2 = cuda_ops.dt_project_softplus(cu(dt_raw), cu(W), cu(bias), 1e-3, 0.1)
+    assert rel_err(dt2, ref_dt) < 1e-5
+
+
+def test_dtproj_tensor_core_matches_cuda_core_kernel(cuda_ops):
+    """dt_rank 64 takes the tcgen05 kernel; the same problem padded to dt_rank 65
+    with a zero column and a zero row of W takes the CUDA-core kernel.  The two
+    agree to f32 accuracy (different summation order, different exp/log forms)."""
+    Bt, T, H, R = 4, 130, 520, 64
+    dt_raw, W, bias, A_log, B = _inputs(Bt, T, H, R, seed=11)
+    dt_raw65 = torch.cat([dt_raw, torch.zeros(Bt, T, 1)], dim=2)
+    W65 = torch.cat([W, torch.zeros(1, H)], dim=0)
+    a_tc, b_tc = cuda_ops.zoh_discretize_dtproj(cu(A_log), cu(B), cu(dt_raw), cu(W), cu(bias), 1e-3, 0.1)
+    a_cc, b_cc = cuda_ops.zoh_discretize_dtproj(cu(A_log), cu(B), cu(dt_raw65), cu(W65), cu(bias), 1e-3, 0.1)
+    assert rel_err(a_tc, a_cc) < 1e-5 and rel_err(b_tc, b_cc) < 1e-5
+    d_tc = cuda_ops.dt_project_softplus(cu(dt_raw), cu(W), cu(bias), 1e-3, 0.1)
+    d_cc = cuda_ops.dt_project_softplus(cu(dt_raw65), cu(W65), cu(bias), 1e-3, 0.1)
+    assert rel_err(d_tc, d_cc) < 1e-5
