@@ -37,6 +37,41 @@ def test_slices_chained_equal_whole_sequence(cuda_ops, N, R, L):
     assert rel_err(y, whole) < TOL_BF16
 
 
+@pytest.mark.parametrize("N", [64, 128])
+def test_slices_chained_slow_decay(cuda_ops, N):
+    """A decay slow enough that a slice's carry reaches far more than the 16
+    chunks the fix-up spreads over CTAs (dt = 2e-3, A = -0.5: ~100k tokens to
+    underflow): the last CTA walks the rest of each slice, in both the
+    cross-slice and the in-device pieces fix-ups."""
+    Bt, L, H, P, R = 1, 6144, 2, 64, 2
+    x, dt, A_log, B, C, D = make_inputs(Bt, L, H, P, N, seed=5)
+    dt = torch.full_like(dt, 2e-3)
+    A_log = torch.full_like(A_log, float(torch.log(torch.tensor(0.5))))
+    xd, dtd, Ad, Bd, Cd, Dd = (t.to(dev) for t in (x, dt, A_log, B, C, D))
+    whole = cuda_ops.multihead_ssm(xd, Ad, Bd, Cd, dtd, Dd)
+    from triton_ssm_b200 import parallel
+    cuts = [parallel.shard_range(L, r, R) for r in range(R)]
+    outs, Ss, ds = [], [], []
+    for a, b in cuts:
+        y, S, d = cuda_ops.multihead_ssm(xd[:, a:b].contiguous(), Ad, Bd[:, a:b].contiguous(),
+                                         Cd[:, a:b].contiguous(), dtd[:, a:b].contiguous(), Dd,
+                                         return_state=True, return_decay=True)
+        outs.append(y)
+        Ss.append(S)
+        ds.append(d)
+    S_all = torch.stack(Ss).contiguous()
+    d_all = torch.stack(ds).contiguous()
+    for r, (a, b) in enumerate(cuts):
+        cuda_ops.ssd_carry_fixup(S_all, d_all, r, Cd[:, a:b].contiguous(), dtd[:, a:b].contiguous(), Ad, outs[r])
+    yk = cuda_ops.multihead_ssm(xd, Ad, Bd, Cd, dtd, Dd, pieces=2)
+    cuda_ops.check_device_status()
+    y = torch.cat(outs, dim=1)
+    ref, _ = oracle.ssd_scan_chunked(x, dt, A_log, B, C, D, chunk=128)
+    parity("slow-decay slices chained (N%d, 2 x 3072 tokens)" % N, y, ref, TOL_BF16)
+    assert rel_err(y, whole) < TOL_BF16
+    assert rel_err(yk, ref) < TOL_BF16 and rel_err(yk, whole) < TOL_BF16
+
+
 def test_decay_output_matches_dt_sum(cuda_ops):
     x, dt, A_log, B, C, D = make_inputs(2, 333, 4, 64, 64, seed=1)
     _, _, d = cuda_ops.multihead_ssm(x.to(dev), A_log.to(dev), B.to(dev), C.to(dev), dt.to(dev), D.to(dev),

@@ -9,16 +9,19 @@
 // the block-level form of the reference's carry scan (ssm_scan.py:53-65,
 // :68-98).  Its effect on the slice's outputs is
 //     y[t, p] += exp(A_h * cumdt(t)) * sum_n C[t, n] carry[p, n],
-// which decays monotonically; the fix-up walks 64-token chunks from the slice
-// start and stops at the first chunk whose starting decay is exactly 0 in f32,
-// after which every further term is exactly 0 as well.
+// which decays monotonically; a chunk of 64 tokens whose starting decay is
+// exactly 0 in f32 needs no work, nor does any chunk after it.  The first FKC
+// chunks of a slice go to FKC CTAs, each of which sums the decay of the tokens
+// before its chunk itself and exits when that decay is 0; the last of them
+// walks on through the later chunks until the decay reaches 0.
 #include "common.cuh"
 
 namespace tssm {
 namespace {
 
-constexpr int FQ = 64;   // tokens per fix-up chunk
-constexpr int FP = 64;   // head dim
+constexpr int FQ = 64;    // tokens per fix-up chunk
+constexpr int FP = 64;    // head dim
+constexpr int FKC = 16;   // CTAs per (slice, sequence, head), one chunk each (the last walks on)
 
 // Slices and sequences: slice j of sequence b has its state at S_all + j*sj +
 // b*sb (+ h*P*N) and its log2 decay at d_all + j*dj + b*db (+ h).  The slice
@@ -35,10 +38,32 @@ __global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
   float* cs = carry + FP * (NST + 1);   // [FQ][NST + 1]
   float* es = cs + FQ * (NST + 1);      // [FQ] decay factor per token
   __shared__ float s_run;
-  const int h = blockIdx.x, tid = threadIdx.x;
+  __shared__ float s_part[8];
+  const int h = blockIdx.x / FKC, kc = blockIdx.x % FKC, tid = threadIdx.x;
   const int slice = pieces > 0 ? (int)blockIdx.z + 1 : rank;
   const int64_t bo = blockIdx.y;
   const int b = pieces > 0 ? (int)(bo * pieces + slice) : (int)bo;   // sequence of C, dt, y
+  const float a2 = -expf(A_log[h]) * 1.4426950408889634f;
+  const int warp = tid >> 5, lane = tid & 31;
+  // log2 decay from the slice start to this CTA's first chunk (tokens [0, kc FQ))
+  const int tstart = kc * FQ;
+  if (tstart >= L) return;
+  {
+    float part = 0.f;
+    for (int t = tid; t < tstart; t += 256) part += dt[((int64_t)b * L + t) * H + h] * a2;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0) s_part[warp] = part;
+    __syncthreads();
+    if (tid == 0) {
+      float run = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) run += s_part[w];
+      s_run = run;
+    }
+    __syncthreads();
+    if (exp2f(s_run) == 0.f) return;   // uniform: this chunk and every later one add exactly 0
+  }
   // carry entering this slice
   const int64_t base = bo * sb + (int64_t)h * FP * NST;
   for (int e = tid; e < FP * NST; e += 256) {
@@ -46,12 +71,9 @@ __global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
     for (int j = 0; j < slice; ++j) c = exp2f(d_all[(int64_t)j * dj + bo * db + h]) * c + S_all[j * sj + base + e];
     carry[(e / NST) * (NST + 1) + (e % NST)] = c;
   }
-  if (tid == 0) s_run = 0.f;
-  const float a2 = -expf(A_log[h]) * 1.4426950408889634f;
-  const int warp = tid >> 5, lane = tid & 31;
   const int tt = tid >> 4, pp = tid & 15;   // 4 tokens x 4 head dims per thread
   __syncthreads();
-  for (int t0 = 0; t0 < L; t0 += FQ) {
+  for (int t0 = tstart; t0 < L; t0 += FQ) {
     // decay factors of this chunk (warp 0) and the chunk's C rows (all)
     if (warp == 0) {
       float l[2];
@@ -109,6 +131,7 @@ __global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
 #pragma unroll
       for (int j = 0; j < 4; ++j) yr[j] = __float2bfloat16_rn(__bfloat162float(yr[j]) + e * acc[i][j]);
     }
+    if (kc != FKC - 1) break;   // one chunk per CTA, except the last CTA of the slice
     __syncthreads();
   }
 }
@@ -151,7 +174,7 @@ extern "C" int tssm_ssd_carry_fixup(const void* S_all, const void* decay_log2_al
   TSSM_REQUIRE(S_all && decay_log2_all && C && dt && A_log && y, "ssd_carry_fixup: null pointer");
   TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31), "ssd_carry_fixup: size out of range");
   return launch_fixup(S_all, decay_log2_all, (int)rank, 0, Bsz * H * P * N, H * P * N, Bsz * H, H, C, dt, A_log, y,
-                      dim3((unsigned)H, (unsigned)Bsz), L, H, N, reinterpret_cast<cudaStream_t>(stream));
+                      dim3((unsigned)(H * FKC), (unsigned)Bsz), L, H, N, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int tssm_ssd_carry_fixup_pieces(const void* S, const void* decay_log2, int64_t pieces, const void* C,
@@ -166,7 +189,7 @@ extern "C" int tssm_ssd_carry_fixup_pieces(const void* S, const void* decay_log2
   TSSM_REQUIRE(Bsz <= 65535 && H <= 65535 && L < (int64_t(1) << 31), "ssd_carry_fixup_pieces: size out of range");
   // piece k of sequence b is sequence b*pieces + k of the [Bsz*pieces, L/pieces, ...] views
   return launch_fixup(S, decay_log2, 0, (int)pieces, H * P * N, pieces * H * P * N, H, pieces * H, C, dt, A_log, y,
-                      dim3((unsigned)H, (unsigned)Bsz, (unsigned)(pieces - 1)), L / pieces, H, N,
+                      dim3((unsigned)(H * FKC), (unsigned)Bsz, (unsigned)(pieces - 1)), L / pieces, H, N,
                       reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -215,7 +238,7 @@ extern "C" int tssm_ssd_carry_fixup_packed(const void* packed, int64_t rank, int
   const int64_t n = Bsz * H * P * N, per_rank = n + Bsz * H;
   const float* base = static_cast<const float*>(packed);
   return launch_fixup(base, base + n, (int)rank, 0, per_rank, H * P * N, per_rank, H, C, dt, A_log, y,
-                      dim3((unsigned)H, (unsigned)Bsz), L, H, N, reinterpret_cast<cudaStream_t>(stream));
+                      dim3((unsigned)(H * FKC), (unsigned)Bsz), L, H, N, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int tssm_ssd_pieces_final_state(const void* S, const void* decay_log2, int64_t pieces, void* state_out,
