@@ -628,6 +628,7 @@ def run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd, t_kernel):
     e2e_steps = max(3, min(args.steps, 20))
     # pinned buffers on the GPU's NUMA node, then the host link measured with
     # every rank copying at once (the bound the host-buffer path runs against)
+    affinity = os.sched_getaffinity(0)
     numa = bind_host_to_gpu(dev)
     barrier(world)
     h2d_gbs, d2h_gbs = pinned_copy_gbs(dev)
@@ -652,6 +653,7 @@ def run_e2e_c2(inp, y, Bt, L, H, P, N, dev, args, world, upd, t_kernel):
     ev1.record(pipe.s_h2d)
     torch.cuda.synchronize()
     e2e_t = max_over_ranks(ev0.elapsed_time(ev1) / 1e3 / e2e_steps, world)
+    os.sched_setaffinity(0, affinity)   # the CPU-baseline leg after this uses every allowed core again
     # spot-check the host result against the device result
     if not torch.equal(y_h.to(dev), y):
         raise RuntimeError("host-pipeline output differs from the device run")
