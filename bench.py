@@ -590,6 +590,40 @@ def run_ours_c4(args, rank, world, local):
     return out
 
 
+def run_ours_c4_bh(args, rank, world, local):
+    """Config 4 sharded by batch x head instead of by sequence, for comparison:
+    rank r scans heads [r H/world, (r+1) H/world) of every batch over the whole
+    L, each sequence cut into in-device pieces so that the rank's few streams
+    still fill its SMs; no collective."""
+    import triton_ssm_b200 as ts
+    from triton_ssm_b200 import parallel, workloads
+    dev = torch.device("cuda", local)
+    c = workloads.C4
+    Bt, H, P, N = c["Bt"], c["H"], c["P"], c["N"]
+    L = args.seq_len or c["L"]
+    h0, h1 = parallel.shard_range(H, rank, world)
+    Hl = h1 - h0
+    inp = workloads.ssd_inputs_slice(Bt, 0, L, Hl, P, N, dev, seed=40 + rank)
+    inp["A_log"] = torch.log(1.0 + ((h0 + torch.arange(Hl, device=dev)) % 16).float())   # A_h = -(1 + h mod 16)
+    K = parallel.ssd_local_pieces(Bt, Hl, L, torch.cuda.get_device_properties(dev).multi_processor_count)
+    y = torch.empty_like(inp["x"])
+    step = lambda: ts.multihead_ssm(inp["x"], inp["A_log"], inp["B"], inp["C"], inp["dt"], inp["D"], y=y, pieces=K)
+    t_step, clocks = _timed(args, world, dev, step)
+    upd = Bt * L * H * P * N
+    alg = workloads.ssd_bytes(Bt, L, H, P, N)
+    cfg = {"workload": "config4 sharded by batch x head: B%d H%d P%d N%d L=%d bf16, %d head(s) of every batch per "
+                       "rank over the whole sequence, %d in-device pieces, no collective" % (Bt, H, P, N, L, Hl, K),
+           "global_batch": Bt, "seq_len": L, "parallelism": "batch x head over %d rank(s)" % world,
+           "heads_per_rank": Hl, "in_device_pieces": K}
+    out = _line(args, world, METRIC, upd / t_step, t_step, "bf16", cfg, alg // world,
+                "ssd_chunk_scan_kernel<128,false> + ssd_carry_fixup_kernel<128>", None, clocks,
+                launches=(1 + (K > 1)) * args.steps)
+    out["scaling"] = "strong"
+    out["roofline"]["note"] = "algorithmic bytes per rank (1/world of the whole problem)"
+    del inp, y
+    return out
+
+
 def run_ours_c2(args, rank, world, local):
     import triton_ssm_b200 as ts
     from triton_ssm_b200 import workloads
@@ -679,16 +713,20 @@ def run_sub_configs(args, rank, world, local):
     """The other benchmark configs, each timed like the headline (warm-up, a
     second of load, exactly `steps` CUDA-event-timed steps, clocks sampled),
     reported as sub-records of the one JSON line.  Config 4 is the sequence-
-    sharded scan over all ranks (its one collective); configs 1, 3 and 5 run on
-    a single GPU (only when world == 1)."""
+    sharded scan over all ranks (its one collective), and, with more than one
+    rank, config 4 sharded by batch x head for comparison ("c4_bh"); configs
+    1, 3 and 5 run on a single GPU (only when world == 1)."""
     import copy
     out = {}
     names = [c.strip() for c in args.configs.split(",") if c.strip()]
-    runners = {"c1": run_ours_c1, "c3": run_ours_c3, "c4": run_ours_c4, "c5": run_ours_c5}
+    runners = {"c1": run_ours_c1, "c3": run_ours_c3, "c4": run_ours_c4, "c5": run_ours_c5,
+               "c4_bh": run_ours_c4_bh}
+    if world > 1 and "c4" in names and "c4_bh" not in names:
+        names.insert(names.index("c4") + 1, "c4_bh")   # the batch x head sharding of config 4, for comparison
     for name in names:
         if name not in runners:
             raise SystemExit("unknown sub-config %r" % name)
-        if name != "c4" and world > 1:
+        if name not in ("c4", "c4_bh") and world > 1:
             continue
         a = copy.copy(args)
         a.batch = None
