@@ -105,6 +105,15 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
+def min_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return float(t.item())
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -562,6 +571,7 @@ def run_ours_c4(args, rank, world, local):
     torch.cuda.synchronize()
     scan_ms = statistics.median(s.elapsed_time(m) for s, m in zip(starts, marks))
     xfix_ms = statistics.median(m.elapsed_time(e) for m, e in zip(marks, ends))
+    xfix_min_ms = min_over_ranks(xfix_ms, world)
     scan_ms = max_over_ranks(scan_ms, world)
     xfix_ms = max_over_ranks(xfix_ms, world)
     upd = Bt * L * H * P * N
@@ -584,8 +594,12 @@ def run_ours_c4(args, rank, world, local):
     out["roofline"]["note"] = "algorithmic bytes per rank (1/world of the whole sequence)"
     out["split_ms"] = {"local_scan": scan_ms, "exchange_and_fixup": xfix_ms,
                        "exchange_and_fixup_frac": xfix_ms / max(1e-9, scan_ms + xfix_ms),
+                       "exchange_and_fixup_min_rank": xfix_min_ms,
+                       "exchange_and_fixup_min_rank_frac": xfix_min_ms / max(1e-9, scan_ms + xfix_ms),
                        "how": "median over %d steps of CUDA events before the step, after the local scan, after "
-                              "the fix-up; max over ranks" % n_split}
+                              "the fix-up; max over ranks (which includes a fast rank waiting in the all-gather for "
+                              "the slowest rank's local scan) and min over ranks (about the exchange and fix-up "
+                              "alone)" % n_split}
     del inp, y
     return out
 
