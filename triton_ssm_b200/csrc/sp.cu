@@ -39,7 +39,9 @@ __global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
   float* es = cs + FQ * (NST + 1);      // [FQ] decay factor per token
   __shared__ float s_run;
   __shared__ float s_part[8];
-  const int h = blockIdx.x / FKC, kc = blockIdx.x % FKC, tid = threadIdx.x;
+  // chunk-major order: every slice's first chunks are dispatched first (the
+  // later chunks' CTAs mostly find a zero decay and exit at once)
+  const int h = blockIdx.x % H, kc = blockIdx.x / H, tid = threadIdx.x;
   const int slice = pieces > 0 ? (int)blockIdx.z + 1 : rank;
   const int64_t bo = blockIdx.y;
   const int b = pieces > 0 ? (int)(bo * pieces + slice) : (int)bo;   // sequence of C, dt, y
@@ -66,10 +68,24 @@ __global__ void __launch_bounds__(256) ssd_carry_fixup_kernel(
   }
   // carry entering this slice
   const int64_t base = bo * sb + (int64_t)h * FP * NST;
-  for (int e = tid; e < FP * NST; e += 256) {
-    float c = 0.f;
-    for (int j = 0; j < slice; ++j) c = exp2f(d_all[(int64_t)j * dj + bo * db + h]) * c + S_all[j * sj + base + e];
-    carry[(e / NST) * (NST + 1) + (e % NST)] = c;
+  // slices outermost, this thread's FP*NST/256 elements in registers: the loads
+  // of one slice are independent, so the chain costs one round trip per slice
+  {
+    constexpr int EPT = FP * NST / 256;
+    float cr[EPT];
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) cr[k] = 0.f;
+    for (int j = 0; j < slice; ++j) {
+      const float f = exp2f(d_all[(int64_t)j * dj + bo * db + h]);
+      const float* Sj = S_all + j * sj + base;
+#pragma unroll
+      for (int k = 0; k < EPT; ++k) cr[k] = f * cr[k] + Sj[tid + k * 256];
+    }
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      const int e = tid + k * 256;
+      carry[(e / NST) * (NST + 1) + (e % NST)] = cr[k];
+    }
   }
   const int tt = tid >> 4, pp = tid & 15;   // 4 tokens x 4 head dims per thread
   __syncthreads();
