@@ -118,3 +118,15 @@ def test_dtproj_tensor_core_matches_cuda_core_kernel(cuda_ops):
     d_tc = cuda_ops.dt_project_softplus(cu(dt_raw), cu(W), cu(bias), 1e-3, 0.1)
     d_cc = cuda_ops.dt_project_softplus(cu(dt_raw65), cu(W65), cu(bias), 1e-3, 0.1)
     assert rel_err(d_tc, d_cc) < 1e-5
+
+
+def test_dtproj_wide_rows_fall_back_to_cuda_cores(cuda_ops):
+    """A single 128-row block across more channel blocks than SMs would give a
+    CTA three channel blocks: the tensor-core launcher declines it and the
+    CUDA-core kernel computes it, with the same result as the oracle."""
+    Bt, T, H, R = 1, 128, 19000, 64
+    dt_raw, W, bias, A_log, B = _inputs(Bt, T, H, R, seed=19)
+    ref_dt = oracle.dt_project_softplus(dt_raw, W, bias, 1e-3, 0.1)
+    rA, rB = oracle.zoh_discretize_dt(A_log, B, ref_dt)
+    Ab, Bb = cuda_ops.zoh_discretize_dtproj(cu(A_log), cu(B), cu(dt_raw), cu(W), cu(bias), 1e-3, 0.1)
+    assert rel_err(Ab, rA) < 1e-5 and rel_err(Bb, rB) < 1e-5
